@@ -1,0 +1,238 @@
+"""Write the golden fixtures of this directory by running the REFERENCE code on seeded inputs.
+
+Usage (only where the reference checkout exists; the GPU box does not have it):
+    DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py
+
+Every array saved here is produced by the reference's own functions (scripts/progressive.py,
+scripts/kvtc.py, scripts/compressed_attention.py, scripts/dimmer.py, scripts/methods.py,
+scripts/fit_kvtc.py) on the seeded tiny model of ``tinymodel.py``. Tests compare the numpy
+oracle and the CUDA path against these arrays; nothing at test time imports the reference.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import tempfile
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+REF = Path(os.environ.get("DIMMERKV_REFERENCE", "/root/reference")) / "scripts"
+sys.path.insert(0, str(REF))
+
+import compressed_attention  # noqa: E402  (reference)
+import dimmer  # noqa: E402
+import kvtc  # noqa: E402
+import progressive  # noqa: E402
+from common import build_cache  # noqa: E402
+from fit_kvtc import TARGETS, build_ladder  # noqa: E402
+from methods import Methods  # noqa: E402
+
+import tinymodel as tm  # noqa: E402
+
+
+def bits16(t: torch.Tensor) -> np.ndarray:
+    """bf16 / f16 tensor -> uint16 bit patterns."""
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def codes_fixture(out: Path) -> None:
+    g = torch.Generator().manual_seed(5)
+    coeff = torch.randn(96, 512, generator=g) * torch.logspace(1, -3, 512)[None]
+    coeff[3, :64] = 0.0           # constant group (span rounds to 0)
+    coeff[4, 64:128] = 0.25       # constant non-zero group
+    coeff[5, 128:192] *= 1e-7     # tiny span
+    codes, low, span = progressive.quantize8(coeff, 64)
+    planes = torch.randint(0, 9, (96, 8), generator=g)
+    deq = progressive.dequantize(codes, low, span, planes)
+    bits = torch.tensor([8, 4, 4, 2, 2, 2, 0, 0])
+    ladder = kvtc.quantize_groups(coeff, bits, 64)
+    np.savez_compressed(
+        out / "codes.npz", coeff=coeff.numpy(), codes=codes.numpy(), low=bits16(low), span=bits16(span),
+        planes=planes.numpy(), deq=deq.numpy(),
+        ladder_bits=bits.numpy(), ladder=ladder.numpy(),
+    )
+
+
+def allocator_fixture(out: Path) -> None:
+    g = torch.Generator().manual_seed(8)
+    middle, levels = 50, 6
+    errors = torch.rand(2 * middle, levels, generator=g).sort(dim=1, descending=True).values
+    level_bytes = torch.tensor([10, 20, 40, 80, 160, 320, 12, 24, 48, 96, 192, 384])
+    chosen = kvtc.allocate_rungs(errors, level_bytes, middle, 8000)
+    np.savez_compressed(out / "allocator.npz", errors=errors.numpy(), level_bytes=level_bytes.numpy(),
+                        middle=middle, budget=8000, chosen=chosen.numpy())
+
+
+def main() -> None:
+    out = HERE
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    codes_fixture(out)
+    allocator_fixture(out)
+
+    model = tm.build_model(torch.bfloat16)
+    dimmer.install(model)
+    cfg = model.config
+    layers, heads, dim = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+    features = layers * heads * dim
+    ids = tm.context_ids()
+    with torch.inference_mode():
+        cache, scores = dimmer.prefill_with_scores(model, ids)
+    keys = [l.keys.clone() for l in cache.layers]
+    values = [l.values.clone() for l in cache.layers]
+    tokens = keys[0].shape[2]
+    cos, sin = kvtc.rope_tables(model, tokens, "cpu")
+    start, end = tm.SINKS, tokens - tm.RECENT
+
+    # Synthetic calibration files (full-rank seeded bases; mean over this context's middle tokens).
+    saved = {"model": "tiny", "layers": layers, "heads": heads, "head_dim": dim, "group": tm.GROUP, "sinks": tm.SINKS}
+    orders = {"model": "tiny", "kvtc": "kvtc.pt"}
+    bases = {}
+    for index, (kind, tensors) in enumerate((("key", keys), ("value", values))):
+        basis = tm.seeded_basis(features, features, tm.SEED_BASIS + index)
+        bases[kind] = basis
+        matrix = kvtc.token_matrix([kvtc.derotate(t, cos, sin) for t in tensors] if kind == "key" else tensors)
+        mean = matrix[start:end].mean(0)
+        coefficients = (matrix[start:end] - mean) @ basis
+        rungs, sizes = build_ladder(coefficients, tm.GROUP, features * 2)
+        saved[kind] = {"mean": mean, "basis": basis, "rungs": rungs, "rung_bytes": sizes}
+        order = progressive.build_order(coefficients, tm.GROUP, TARGETS, features * 2)
+        orders[kind] = {"planes": order.planes, "prefix_bytes": order.prefix_bytes, "rungs": order.rungs}
+    tmp = Path(tempfile.mkdtemp())
+    torch.save(saved, tmp / "kvtc.pt")
+    torch.save(orders, tmp / "progressive.pt")
+    methods = Methods("tiny", tmp / "none", tmp / "none", torch.device("cpu"), tm.RECENT, model=model,
+                      kvtc=tmp / "kvtc.pt", progressive=tmp / "progressive.pt")
+
+    inputs = dict(ids=ids.numpy(), keys=np.stack([bits16(k[0]) for k in keys]),
+                  values=np.stack([bits16(v[0]) for v in values]),
+                  snap=torch.stack(scores["snap"]).float().numpy(),
+                  checksum=tm.model_checksum(model),
+                  basis_checksum=np.array([float(bases[k].double().sum()) for k in ("key", "value")]),
+                  mean_key=saved["key"]["mean"].numpy(), mean_value=saved["value"]["mean"].numpy(),
+                  cos=cos.numpy(), sin=sin.numpy())
+    for kind in ("key", "value"):
+        inputs[f"rungs_{kind}"] = saved[kind]["rungs"].numpy()
+        inputs[f"rung_bytes_{kind}"] = np.array(saved[kind]["rung_bytes"])
+        inputs[f"order_planes_{kind}"] = orders[kind]["planes"].numpy()
+        inputs[f"order_prefix_{kind}"] = orders[kind]["prefix_bytes"].numpy()
+        inputs[f"order_rungs_{kind}"] = np.array(orders[kind]["rungs"])
+    np.savez_compressed(out / "tiny_inputs.npz", **inputs)
+
+    g = torch.Generator().manual_seed(21)
+    module = types.SimpleNamespace(num_key_value_groups=cfg.num_attention_heads // heads)
+    queries = {q: torch.randn(1, cfg.num_attention_heads, q, dim, generator=g) for q in (1, 4)}
+    news = {q: (torch.randn(1, heads, q, dim, generator=g), torch.randn(1, heads, q, dim, generator=g)) for q in (1, 4)}
+
+    def attend_all(ctx, dtype):
+        result = {}
+        for layer in range(layers):
+            module.layer_idx = layer
+            ex = ctx.exact_cache.layers[layer]
+            for q in (1, 4):
+                k = torch.cat([ex.keys, news[q][0].to(dtype)], dim=2)
+                v = torch.cat([ex.values, news[q][1].to(dtype)], dim=2)
+                mask = None
+                if q > 1:
+                    e = k.shape[2]
+                    mask = torch.zeros(1, 1, q, e, dtype=dtype)
+                    causal = torch.triu(torch.ones(q, q, dtype=torch.bool), 1)
+                    mask[0, 0, :, e - q:][causal] = torch.finfo(dtype).min
+                out_, _ = ctx.attend(module, queries[q].to(dtype), k, v, mask, dim ** -0.5)
+                result[f"attend_l{layer}_q{q}"] = out_.float().numpy()
+            if dtype == torch.bfloat16 or layer == 0:
+                rebuilt = ctx._keys(layer)
+                result[f"keys_l{layer}"] = bits16(rebuilt) if dtype == torch.bfloat16 else rebuilt.numpy()
+        return result
+
+    shared_attend_inputs = {f"query_q{q}": queries[q].numpy() for q in (1, 4)}
+    for q in (1, 4):
+        shared_attend_inputs[f"newk_q{q}"] = news[q][0].numpy()
+        shared_attend_inputs[f"newv_q{q}"] = news[q][1].numpy()
+
+    # ---- dkvtc@b:snap:floor1 (the kvtc ladder entry point)
+    name = "dkvtc@0.1:snap:floor1"
+    with torch.inference_mode():
+        compressed = methods.apply(name, keys, values, scores)
+        codec = methods.codec("kvtc")
+        fixture = {"name": name, "used_bytes": compressed.used_bytes,
+                   "span": np.array(codec.last_span)}
+        for kind in ("key", "value"):
+            fixture[f"choice_{kind}"] = codec.last_choice[kind].numpy()
+            fixture[f"coeff_{kind}"] = codec.last_coefficients[kind].numpy()
+        for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+            ctx = compressed_attention.CompressedContext(codec, [k.to(dtype) for k in keys],
+                                                         [v.to(dtype) for v in values], model, dtype=dtype)
+            for key, val in attend_all(ctx, dtype).items():
+                fixture[f"{tag}_{key}"] = val
+            fixture[f"{tag}_code_bytes"] = ctx.code_bytes()
+        # Direct greedy answer over codes vs the rebuilt cache (test_compressed_attention.py:89-98).
+        tail = tm.question_ids()
+        ctx = compressed_attention.CompressedContext(codec, keys, values, model, dtype=torch.bfloat16)
+        exact = build_cache([l.keys.clone() for l in ctx.exact_cache.layers],
+                            [l.values.clone() for l in ctx.exact_cache.layers], model)
+        tok = types.SimpleNamespace(eos_token_id=-1, all_special_ids=[], decode=lambda ids, skip_special_tokens=True: " ".join(map(str, ids)))
+        text_d, logits_d = compressed_attention.greedy_answer(model, tok, ctx, exact, tail[None], tokens, 4,
+                                                              stop_at_eos=False)
+        full = build_cache([k.clone() for k in compressed.keys], [v.clone() for v in compressed.values], model)
+        text_r, logits_r = compressed_attention.greedy_answer(model, tok, None, full, tail[None], tokens, 4,
+                                                              stop_at_eos=False)
+        fixture.update(tail=tail.numpy(), greedy_direct=np.array([int(x) for x in text_d.split()]),
+                       greedy_rebuilt=np.array([int(x) for x in text_r.split()]),
+                       logits_direct=logits_d.numpy(), logits_rebuilt=logits_r.numpy())
+    fixture.update(shared_attend_inputs)
+    np.savez_compressed(out / "tiny_dkvtc.npz", **fixture)
+
+    # ---- prog@b:r<frac> (progressive codec, hot tier, question-time refine)
+    name, budget, fraction = "prog@0.1:r0.05", 0.1, 0.05
+    with torch.inference_mode():
+        pcodec = methods.codec("prog")
+        stored = pcodec.encode(keys, values, budget, tm.RECENT, None)
+        fixture = {"name": name, "hot_bytes": stored.hot_bytes, "cold_bytes": stored.cold_bytes,
+                   "budget_bytes": stored.budget_bytes, "span": np.array([stored.start, stored.end])}
+        for kind in ("key", "value"):
+            s = stored.stores[kind]
+            fixture[f"codes_{kind}"] = s.codes.numpy()
+            fixture[f"low_{kind}"] = bits16(s.low)
+            fixture[f"lowspan_{kind}"] = bits16(s.span)
+            fixture[f"hot_pieces_{kind}"] = s.hot_pieces.numpy()
+        hot_keys, hot_values = stored.hot()
+        importance = progressive.question_importance(model, hot_keys, hot_values, tm.question_ids(), tokens)
+        middle = stored.end - stored.start
+        count = max(1, int(round(fraction * middle)))
+        top = importance[stored.start:stored.end].topk(count).indices + stored.start
+        ref_keys, ref_values, fetched = stored.refine(hot_keys, hot_values, top)
+        fixture.update(importance=importance.float().numpy(), top=top.numpy(), fetched=fetched, count=count)
+        rows = top.sort().values
+        fixture["refined_keys"] = np.stack([bits16(k[0][:, rows]) for k in ref_keys])
+        fixture["refined_values"] = np.stack([bits16(v[0][:, rows]) for v in ref_values])
+        fixture["hot_keys_rows"] = np.stack([bits16(k[0][:, rows]) for k in hot_keys])
+        # Direct attention over the hot progressive codes: a codec shim exposing what
+        # CompressedContext reads (compressed_attention.py:36-54), as in the survey probes.
+        shim = types.SimpleNamespace(layers=layers, heads=heads, head_dim=dim, device=torch.device("cpu"),
+                                     last_span=(stored.start, stored.end), streams={}, last_choice={},
+                                     last_coefficients={})
+        for kind in ("key", "value"):
+            s = stored.stores[kind]
+            planes = pcodec.orders[kind].planes[s.hot_pieces]
+            shim.streams[kind] = pcodec.base.streams[kind]
+            shim.last_choice[kind] = s.hot_pieces
+            shim.last_coefficients[kind] = progressive.dequantize(s.codes, s.low, s.span, planes)
+        for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+            ctx = compressed_attention.CompressedContext(shim, [k.to(dtype) for k in keys],
+                                                         [v.to(dtype) for v in values], model, dtype=dtype)
+            for key, val in attend_all(ctx, dtype).items():
+                fixture[f"{tag}_{key}"] = val
+    fixture.update(shared_attend_inputs)
+    np.savez_compressed(out / "tiny_prog.npz", **fixture)
+    for f in sorted(out.glob("*.npz")):
+        print(f.name, f.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

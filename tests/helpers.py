@@ -1,0 +1,78 @@
+"""Helpers shared by the CPU and GPU tests: rebuild the golden inputs as numpy / torch objects."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+import tinymodel as tm
+from oracle import codes as oc
+from oracle.attention import OracleContext
+
+
+def f32_from_bits(bits: np.ndarray) -> np.ndarray:
+    return oc.bf16_to_f32(bits)
+
+
+def f16_from_bits(bits: np.ndarray) -> np.ndarray:
+    return np.asarray(bits, dtype=np.uint16).view(np.float16)
+
+
+def tiny_bases(inputs: dict) -> dict:
+    features = tm.TINY["num_hidden_layers"] * tm.TINY["num_key_value_heads"] * tm.TINY["head_dim"]
+    out = {}
+    for index, kind in enumerate(("key", "value")):
+        basis = tm.seeded_basis(features, features, tm.SEED_BASIS + index)
+        got = float(basis.double().sum())
+        want = float(inputs["basis_checksum"][index])
+        if abs(got - want) > 1e-6 * max(1.0, abs(want)):
+            raise RuntimeError(f"seeded basis drifted: {got} vs {want}")
+        out[kind] = basis.numpy()
+    return out
+
+
+def prog_decoded(fix: dict, inputs: dict) -> tuple[dict, dict, dict]:
+    """(choice, decoded, planes) of the progressive hot tier, decoded with the oracle."""
+    choice, decoded, planes = {}, {}, {}
+    for kind in ("key", "value"):
+        hot = fix[f"hot_pieces_{kind}"]
+        p = inputs[f"order_planes_{kind}"][hot]
+        low = f16_from_bits(fix[f"low_{kind}"])
+        span = f16_from_bits(fix[f"lowspan_{kind}"])
+        choice[kind] = hot
+        planes[kind] = p
+        decoded[kind] = oc.dequantize(fix[f"codes_{kind}"], low, span, p)
+    return choice, decoded, planes
+
+
+def oracle_context(fix: dict, inputs: dict, dtype: str, prog: bool) -> OracleContext:
+    start, end = (int(v) for v in fix["span"])
+    if prog:
+        choice, decoded, _ = prog_decoded(fix, inputs)
+    else:
+        choice = {k: fix[f"choice_{k}"] for k in ("key", "value")}
+        decoded = {k: fix[f"coeff_{k}"] for k in ("key", "value")}
+    bases = tiny_bases(inputs)
+    return OracleContext(
+        start=start, end=end, layers=tm.TINY["num_hidden_layers"], heads=tm.TINY["num_key_value_heads"],
+        head_dim=tm.TINY["head_dim"], choice=choice, decoded=decoded, basis=bases,
+        mean={"key": inputs["mean_key"], "value": inputs["mean_value"]}, cos=inputs["cos"], sin=inputs["sin"],
+        dtype=dtype)
+
+
+def exact_kv(fix: dict, inputs: dict, layer: int, q: int, dtype: str):
+    """Exact keys/values of one layer (sinks + recent + the q new tokens) and the causal mask."""
+    start, end = (int(v) for v in fix["span"])
+    keys = f32_from_bits(inputs["keys"][layer])  # [Hkv, T, D]
+    values = f32_from_bits(inputs["values"][layer])
+    k = np.concatenate([keys[:, :start], keys[:, end:], oc.round_dtype(fix[f"newk_q{q}"][0], dtype)], axis=1)[None]
+    v = np.concatenate([values[:, :start], values[:, end:], oc.round_dtype(fix[f"newv_q{q}"][0], dtype)], axis=1)[None]
+    mask = None
+    if q > 1:
+        e = k.shape[2]
+        finfo_min = float(torch.finfo(torch.bfloat16 if dtype == "bf16" else torch.float32).min)
+        mask = np.zeros((1, 1, q, e), dtype=np.float32)
+        causal = np.triu(np.ones((q, q), dtype=bool), 1)
+        sub = mask[0, 0, :, e - q:]
+        sub[causal] = finfo_min
+    return k, v, mask
