@@ -1,0 +1,271 @@
+// capi.cu — extern "C" entry points of libdimmerkv.so (declared in include/dimmer_kv.h).
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "../../include/dimmer_kv.h"
+#include "dkv_format.cuh"
+#include "dkv_kernels.h"
+
+namespace {
+
+using dkv::GroupDesc;
+using dkv::TileDesc;
+
+static_assert(sizeof(dkv_tile) == sizeof(TileDesc), "tile layout");
+static_assert(sizeof(dkv_group) == sizeof(GroupDesc), "group layout");
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Basis tensor maps, cached by (address, rows, width, box rows).
+std::mutex g_map_mutex;
+std::map<std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t>, CUtensorMap> g_maps;
+
+int basis_map(const void* basis, uint64_t rows, uint64_t width, uint32_t box_rows, CUtensorMap* out) {
+  if (basis == nullptr || rows == 0 || width == 0 || width % 64 != 0) return DKV_ERR_ARGS;
+  if (reinterpret_cast<uintptr_t>(basis) % 16 != 0) return DKV_ERR_ARGS;
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(basis), rows, width, box_rows);
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return DKV_OK;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return DKV_ERR_TENSORMAP;
+  CUtensorMap map;
+  cuuint64_t gdim[2] = {width, rows};
+  cuuint64_t gstride[1] = {width * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(basis), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return DKV_ERR_TENSORMAP;
+  if (g_maps.size() > 256) g_maps.clear();
+  g_maps[key] = map;
+  *out = map;
+  return DKV_OK;
+}
+
+int sm_count() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+int check_common(const dkv_attend_args* a) {
+  if (a == nullptr) return DKV_ERR_ARGS;
+  if (a->n_seq < 0 || a->q_len < 1 || a->n_kv_heads < 1 || a->n_q_heads % a->n_kv_heads != 0) return DKV_ERR_ARGS;
+  if (a->layer < 0 || a->layer >= a->n_layers) return DKV_ERR_ARGS;
+  if (a->head_dim != 64 && a->head_dim != 128) return DKV_ERR_CONFIG;
+  return DKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dkv_version(void) { return 100; }
+
+const char* dkv_status_string(int status) {
+  switch (status) {
+    case DKV_OK: return "ok";
+    case DKV_ERR_ARGS: return "invalid argument";
+    case DKV_ERR_CONFIG: return "unsupported configuration";
+    case DKV_ERR_CUDA: return "CUDA error";
+    case DKV_ERR_TENSORMAP: return "tensor map encoding failed";
+    default: return "unknown status";
+  }
+}
+
+int dkv_key_scores(const dkv_attend_args* a, void* stream) {
+  int rc = check_common(a);
+  if (rc != DKV_OK) return rc;
+  if (a->n_k_items == 0) return DKV_OK;
+  const int n_cols = a->n_kv_heads * a->head_dim;
+  const int nb = a->k_block_cols;
+  if ((nb != 128 && nb != 256 && nb != 512) || n_cols % nb != 0 || nb % a->head_dim != 0) return DKV_ERR_CONFIG;
+  CUtensorMap map;
+  rc = basis_map(a->k_basis, static_cast<uint64_t>(a->n_layers) * n_cols, static_cast<uint64_t>(a->k_width),
+                 nb > 256 ? 256u : static_cast<uint32_t>(nb), &map);
+  if (rc != DKV_OK) return rc;
+  dkv::KeyScoreParams p{};
+  p.code = a->k_code;
+  p.code_size = a->k_code_size;
+  p.tiles = reinterpret_cast<const TileDesc*>(a->k_tiles);
+  p.groups = reinterpret_cast<const GroupDesc*>(a->k_groups);
+  p.tok_pos = a->k_pos;
+  p.items = a->k_items;
+  p.n_items = a->n_k_items;
+  p.n_union_groups = static_cast<uint32_t>(a->k_width / 64);
+  p.query = static_cast<const __nv_bfloat16*>(a->query);
+  p.mean = static_cast<const __nv_bfloat16*>(a->k_mean);
+  p.mean_seq_stride = a->k_mean_seq_stride;
+  p.cos_t = static_cast<const __nv_bfloat16*>(a->cos_t);
+  p.sin_t = static_cast<const __nv_bfloat16*>(a->sin_t);
+  p.max_pos = a->max_pos;
+  p.seq_score_off = a->seq_score_off;
+  p.seq_m = a->seq_m;
+  p.scores = a->scores;
+  p.layer = a->layer;
+  p.n_cols = n_cols;
+  p.n_q_heads = a->n_q_heads;
+  p.q_per_kv = a->n_q_heads / a->n_kv_heads;
+  p.q_len = a->q_len;
+  p.head_dim = a->head_dim;
+  p.scaling = a->scaling;
+  p.status = a->status;
+  const int grid = a->grid_k > 0 ? a->grid_k : (a->n_k_items < sm_count() ? a->n_k_items : sm_count());
+  return dkv::run_key_scores(map, p, nb, grid, static_cast<cudaStream_t>(stream));
+}
+
+int dkv_softmax_stats(const dkv_attend_args* a, void* stream) {
+  int rc = check_common(a);
+  if (rc != DKV_OK) return rc;
+  dkv::SoftmaxParams p{};
+  p.scores = a->scores;
+  p.seq_score_off = a->seq_score_off;
+  p.seq_m = a->seq_m;
+  p.query = static_cast<const __nv_bfloat16*>(a->query);
+  p.exact_k = static_cast<const __nv_bfloat16*>(a->exact_k);
+  p.mask = a->mask;
+  p.n_seq = a->n_seq;
+  p.n_q_heads = a->n_q_heads;
+  p.q_per_kv = a->n_q_heads / a->n_kv_heads;
+  p.q_len = a->q_len;
+  p.head_dim = a->head_dim;
+  p.n_exact = a->n_exact;
+  p.scaling = a->scaling;
+  p.row_stats = a->row_stats;
+  p.p_exact = a->p_exact;
+  return dkv::run_softmax_stats(p, static_cast<cudaStream_t>(stream));
+}
+
+static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_rows, void* stream) {
+  dkv::ValueWeightParams p{};
+  p.code = a->v_code;
+  p.code_size = a->v_code_size;
+  p.tiles = reinterpret_cast<const TileDesc*>(a->v_tiles);
+  p.groups = reinterpret_cast<const GroupDesc*>(a->v_groups);
+  p.tok_sidx = a->v_sidx;
+  p.items = a->v_items;
+  p.n_items = a->n_v_items;
+  p.item_groups = a->v_item_groups;
+  p.scores = a->scores;
+  p.seq_score_off = a->seq_score_off;
+  p.seq_m = a->seq_m;
+  p.row_stats = a->row_stats;
+  p.n_q_heads = a->n_q_heads;
+  p.q_len = a->q_len;
+  p.row_begin = row_begin;
+  p.n_rows = n_rows;
+  p.n_rows_pad = a->rows_pad;
+  p.partial = a->partial;
+  p.status = a->status;
+  const int grid = a->grid_v > 0 ? a->grid_v : (a->n_v_items < sm_count() ? a->n_v_items : sm_count());
+  return dkv::run_value_weights(p, grid, static_cast<cudaStream_t>(stream));
+}
+
+static int finalize_rows(const dkv_attend_args* a, int row_begin, int n_rows, void* stream) {
+  dkv::FinalizeParams p{};
+  p.partial = a->partial;
+  p.items = a->v_items;
+  p.seq_items = a->v_seq_items;
+  p.item_groups = a->v_item_groups;
+  p.n_rows_pad = a->rows_pad;
+  p.row_begin = row_begin;
+  p.n_rows = n_rows;
+  p.basis_v = static_cast<const __nv_bfloat16*>(a->v_basis);
+  p.r_v = a->v_width;
+  p.mean_v = static_cast<const __nv_bfloat16*>(a->v_mean);
+  p.mean_seq_stride = a->v_mean_seq_stride;
+  p.row_stats = a->row_stats;
+  p.p_exact = a->p_exact;
+  p.exact_v = static_cast<const __nv_bfloat16*>(a->exact_v);
+  p.n_seq = a->n_seq;
+  p.n_q_heads = a->n_q_heads;
+  p.q_per_kv = a->n_q_heads / a->n_kv_heads;
+  p.q_len = a->q_len;
+  p.head_dim = a->head_dim;
+  p.n_exact = a->n_exact;
+  p.layer = a->layer;
+  p.n_cols = a->n_kv_heads * a->head_dim;
+  p.out = a->out;
+  p.out_f32 = a->out_f32;
+  return dkv::run_finalize(p, static_cast<cudaStream_t>(stream));
+}
+
+int dkv_value_weights(const dkv_attend_args* a, void* stream) {
+  int rc = check_common(a);
+  if (rc != DKV_OK) return rc;
+  const int rows = a->n_q_heads * a->q_len;
+  if (a->rows_pad < 16 || a->rows_pad > 128 || a->rows_pad % 16) return DKV_ERR_CONFIG;
+  for (int r0 = 0; r0 < rows; r0 += a->rows_pad) {
+    const int n = rows - r0 < a->rows_pad ? rows - r0 : a->rows_pad;
+    rc = value_weights_rows(a, r0, n, stream);
+    if (rc != DKV_OK) return rc;
+  }
+  return DKV_OK;
+}
+
+int dkv_finalize(const dkv_attend_args* a, void* stream) {
+  int rc = check_common(a);
+  if (rc != DKV_OK) return rc;
+  const int rows = a->n_q_heads * a->q_len;
+  if (rows > a->rows_pad) return DKV_ERR_CONFIG;  // multi-chunk rows go through dkv_attend_layer
+  return finalize_rows(a, 0, rows, stream);
+}
+
+int dkv_attend_layer(const dkv_attend_args* a, void* stream) {
+  int rc = dkv_key_scores(a, stream);
+  if (rc != DKV_OK) return rc;
+  rc = dkv_softmax_stats(a, stream);
+  if (rc != DKV_OK) return rc;
+  const int rows = a->n_q_heads * a->q_len;
+  if (a->rows_pad < 16 || a->rows_pad > 128 || a->rows_pad % 16) return DKV_ERR_CONFIG;
+  for (int r0 = 0; r0 < rows; r0 += a->rows_pad) {
+    const int n = rows - r0 < a->rows_pad ? rows - r0 : a->rows_pad;
+    rc = value_weights_rows(a, r0, n, stream);
+    if (rc != DKV_OK) return rc;
+    rc = finalize_rows(a, r0, n, stream);
+    if (rc != DKV_OK) return rc;
+  }
+  return DKV_OK;
+}
+
+int dkv_unpack(const dkv_unpack_args* a, void* stream) {
+  if (a == nullptr || a->code == nullptr || a->tiles == nullptr || a->groups == nullptr || a->out == nullptr)
+    return DKV_ERR_ARGS;
+  dkv::UnpackParams p{};
+  p.code = a->code;
+  p.code_size = a->code_size;
+  p.tiles = reinterpret_cast<const TileDesc*>(a->tiles);
+  p.groups = reinterpret_cast<const GroupDesc*>(a->groups);
+  p.n_tiles = a->n_tiles;
+  p.out = a->out;
+  p.out_cols = a->out_cols;
+  p.out_bf16 = a->out_bf16;
+  p.status = a->status;
+  return dkv::run_unpack(p, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,116 @@
+// dkv_kernels.h — parameter blocks and launchers of the DimmerKV sm_100a kernels (internal).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace dkv {
+
+// Return codes shared with the C ABI (include/dimmer_kv.h).
+enum : int {
+  kDkvOk = 0,
+  kDkvErrArgs = 1,     // a pointer, size or shape argument is invalid
+  kDkvErrConfig = 2,   // a shape this build has no kernel for (head_dim, GQA group, ...)
+  kDkvErrCuda = 3,     // a CUDA runtime call or launch failed
+  kDkvErrTensorMap = 4 // cuTensorMapEncodeTiled rejected the basis layout
+};
+
+struct TileDesc;
+struct GroupDesc;
+
+// Fused key rebuild + RoPE + query-key products (key_scores.cu).
+struct KeyScoreParams {
+  const uint8_t* code;            // key plane blocks
+  uint64_t code_size;
+  const TileDesc* tiles;
+  const GroupDesc* groups;
+  const int32_t* tok_pos;         // absolute RoPE position per key token; < 0 hides the token
+  const int32_t* items;           // work items: tile * (n_cols / NB) + column block
+  int n_items;
+  uint32_t n_union_groups;        // groups covered by the basis tensor map
+  const __nv_bfloat16* query;     // [n_seq][n_q_heads][q_len][head_dim]
+  const __nv_bfloat16* mean;      // [.][n_layers][n_cols], conversation stride mean_seq_stride (0 = shared)
+  int64_t mean_seq_stride;
+  const __nv_bfloat16* cos_t;     // [max_pos][head_dim / 2]
+  const __nv_bfloat16* sin_t;
+  int max_pos;
+  const int64_t* seq_score_off;   // [n_seq] first score of each conversation
+  const int32_t* seq_m;           // [n_seq] score-order length (row stride of the scores)
+  float* scores;                  // [sum over seq][n_q_heads][q_len][M_s]
+  int layer, n_cols, n_q_heads, q_per_kv, q_len, head_dim;
+  float scaling;
+  int* status;
+};
+int run_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int nb, int grid, cudaStream_t stream);
+
+// Softmax statistics over compressed + exact tokens (softmax.cu).
+struct SoftmaxParams {
+  const float* scores;
+  const int64_t* seq_score_off;
+  const int32_t* seq_m;
+  const __nv_bfloat16* query;     // [n_seq][n_q_heads][q_len][head_dim]
+  const __nv_bfloat16* exact_k;   // [n_seq][n_kv_heads][n_exact][head_dim]
+  const float* mask;              // [n_seq][q_len][n_exact] additive, or null
+  int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact;
+  float scaling;
+  float* row_stats;               // [n_seq][n_q_heads][q_len][4]: max, 1/sum, compressed mass, 0
+  float* p_exact;                 // [n_seq][n_q_heads][q_len][n_exact]
+};
+int run_softmax_stats(const SoftmaxParams& p, cudaStream_t stream);
+
+// Probability-weighted value coefficients (value_weights.cu).
+struct ValueWeightParams {
+  const uint8_t* code;
+  uint64_t code_size;
+  const TileDesc* tiles;
+  const GroupDesc* groups;
+  const int32_t* tok_sidx;        // value token -> index in its conversation's score order
+  const int32_t* items;           // [n_items][4]: seq, tile_begin, tile_end, first union group
+  int n_items;
+  int item_groups;                // union groups covered by one item (2 x pairs)
+  const float* scores;
+  const int64_t* seq_score_off;
+  const int32_t* seq_m;
+  const float* row_stats;
+  int n_q_heads, q_len;
+  int row_begin, n_rows, n_rows_pad;  // rows = q_head * q_len + qi; N of the MMA = n_rows_pad
+  float* partial;                 // [n_items][n_rows_pad][item_groups * 64]
+  int* status;
+};
+int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream);
+
+// Value basis, mean and exact tokens -> attention output (finalize.cu).
+struct FinalizeParams {
+  const float* partial;
+  const int32_t* items;           // value items [n_items][4]
+  const int32_t* seq_items;       // [n_seq][2] item range of each conversation
+  int item_groups, n_rows_pad, row_begin, n_rows;
+  const __nv_bfloat16* basis_v;   // [n_layers][r_v][n_cols]
+  int r_v;                        // union components of the value basis
+  const __nv_bfloat16* mean_v;    // [.][n_layers][n_cols]
+  int64_t mean_seq_stride;
+  const float* row_stats;
+  const float* p_exact;
+  const __nv_bfloat16* exact_v;   // [n_seq][n_kv_heads][n_exact][head_dim]
+  int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact, layer, n_cols;
+  void* out;                      // [n_seq][q_len][n_q_heads][head_dim]
+  int out_f32;                    // fp32 output instead of bf16
+};
+int run_finalize(const FinalizeParams& p, cudaStream_t stream);
+
+// Standalone ragged bit-plane unpack (unpack.cu).
+struct UnpackParams {
+  const uint8_t* code;
+  uint64_t code_size;
+  const TileDesc* tiles;
+  const GroupDesc* groups;
+  int n_tiles;
+  void* out;                      // [tokens][out_cols] fp32 or bf16, stream order
+  int64_t out_cols;
+  int out_bf16;
+  int* status;
+};
+int run_unpack(const UnpackParams& p, cudaStream_t stream);
+
+}  // namespace dkv

@@ -1,0 +1,146 @@
+// softmax.cu — one softmax over compressed and exact tokens, as statistics.
+//
+// Replaces the normalisation of CompressedContext.attend (scripts/compressed_attention.py:122-128):
+// scores_e = q . k_exact * scaling (+ mask), then softmax over cat(scores_c, scores_e) in float32.
+// Instead of materialising probabilities for the compressed tokens, each (conversation, query
+// head, query row) gets its row maximum, 1 / sum of exponentials and the probability mass of the
+// compressed part; the exact tokens' probabilities are written out (there are few of them).
+#include <cfloat>
+#include <cmath>
+#include "dkv_kernels.h"
+
+namespace dkv {
+
+namespace {
+constexpr int kSoftmaxThreads = 256;
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void merge_ml(float& m, float& l, float m2, float l2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    l = l2;
+    return;
+  }
+  if (m2 > m) {
+    l = l * expf(m - m2) + l2;
+    m = m2;
+  } else {
+    l = l + l2 * expf(m2 - m);
+  }
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const SoftmaxParams p) {
+  extern __shared__ float sh[];
+  const int D = p.head_dim;
+  float* qv = sh;                     // [D]
+  float* se = qv + D;                 // [n_exact]
+  float* red_m = se + p.n_exact;      // [16]
+  float* red_l = red_m + 16;          // [8]
+
+  const int row = blockIdx.x;
+  const int qi = row % p.q_len;
+  const int hq = (row / p.q_len) % p.n_q_heads;
+  const int s = row / (p.q_len * p.n_q_heads);
+  const int kvh = hq / p.q_per_kv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  const __nv_bfloat16* q = p.query + ((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D;
+  for (int d = tid; d < D; d += blockDim.x) qv[d] = __bfloat162float(q[d]);
+  __syncthreads();
+
+  // Exact-token scores, one warp per token.
+  const __nv_bfloat16* kbase = p.exact_k + (static_cast<int64_t>(s) * (p.n_q_heads / p.q_per_kv) + kvh) *
+                                               static_cast<int64_t>(p.n_exact) * D;
+  for (int e = warp; e < p.n_exact; e += blockDim.x / 32) {
+    const __nv_bfloat16* k = kbase + static_cast<int64_t>(e) * D;
+    float dot = 0.f;
+    for (int d = lane; d < D; d += 32) dot += qv[d] * __bfloat162float(k[d]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0) {
+      float v = dot * p.scaling;
+      if (p.mask != nullptr) v += p.mask[(static_cast<int64_t>(s) * p.q_len + qi) * p.n_exact + e];
+      se[e] = v;
+    }
+  }
+
+  // Compressed part: running (max, sum of exp) per thread, then a block reduction.
+  const int64_t m_s = p.seq_m[s];
+  const float* sc = p.scores + p.seq_score_off[s] + (static_cast<int64_t>(hq) * p.q_len + qi) * m_s;
+  float m = -INFINITY, l = 0.f;
+  for (int64_t n = tid; n < m_s; n += blockDim.x) {
+    const float x = sc[n];
+    if (x == -INFINITY) continue;
+    if (x > m) {
+      l = (m == -INFINITY ? 0.f : l * expf(m - x)) + 1.f;
+      m = x;
+    } else {
+      l += expf(x - m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float l2 = __shfl_xor_sync(0xffffffffu, l, o);
+    merge_ml(m, l, m2, l2);
+  }
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_l[warp] = l;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float mc = -INFINITY, lc = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) merge_ml(mc, lc, red_m[w], red_l[w]);
+    float mx = mc;
+    for (int e = 0; e < p.n_exact; ++e) mx = fmaxf(mx, se[e]);
+    float sum = (mc == -INFINITY) ? 0.f : lc * expf(mc - mx);
+    for (int e = 0; e < p.n_exact; ++e) sum += expf(se[e] - mx);
+    red_m[0] = mx;
+    red_l[0] = 1.f / sum;
+  }
+  __syncthreads();
+  const float mx = red_m[0], inv = red_l[0];
+  // The reference casts the probabilities to the cache dtype before the value products
+  // (compressed_attention.py:127-128, 130): exact probabilities and the compressed mass used by
+  // the mean term are sums of bf16-rounded probabilities here too.
+  for (int e = tid; e < p.n_exact; e += blockDim.x)
+    p.p_exact[static_cast<int64_t>(row) * p.n_exact + e] = bf16_round(expf(se[e] - mx) * inv);
+  float mass = 0.f;
+  for (int64_t n = tid; n < m_s; n += blockDim.x) {
+    const float x = sc[n];
+    if (x != -INFINITY) mass += bf16_round(expf(x - mx) * inv);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mass += __shfl_xor_sync(0xffffffffu, mass, o);
+  __syncthreads();
+  if (lane == 0) red_m[8 + warp] = mass;
+  __syncthreads();
+  if (tid == 0) {
+    float total = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) total += red_m[8 + w];
+    float* st = p.row_stats + static_cast<int64_t>(row) * 4;
+    st[0] = mx;
+    st[1] = inv;
+    st[2] = total;
+    st[3] = 0.f;
+  }
+}
+
+int run_softmax_stats(const SoftmaxParams& p, cudaStream_t stream) {
+  if (p.n_exact < 0 || p.n_exact > 16384 || p.head_dim > 256) return kDkvErrConfig;
+  const int rows = p.n_seq * p.n_q_heads * p.q_len;
+  if (rows == 0) return kDkvOk;
+  const int smem = (p.head_dim + p.n_exact + 24) * 4;
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(softmax_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kDkvErrCuda;
+  }
+  softmax_stats_kernel<<<rows, kSoftmaxThreads, smem, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
+}  // namespace dkv

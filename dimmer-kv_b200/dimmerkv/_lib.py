@@ -1,0 +1,96 @@
+"""ctypes binding of libdimmerkv.so (the C ABI declared in include/dimmer_kv.h).
+
+The library is built in-tree by ``build_lib.py`` (``__graft_entry__.build()`` calls it). There is
+no fallback: if the library is missing, ``lib()`` raises, and so does every op that needs it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int32, c_int64, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libdimmerkv.so"
+
+DKV_OK = 0
+STATUS_TEXT = {0: "ok", 1: "invalid argument", 2: "unsupported configuration", 3: "CUDA error",
+               4: "tensor map encoding failed"}
+DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out waiting for a basis tile",
+                 103: "timed out waiting for an operand tile", 104: "timed out waiting for a free stage",
+                 105: "timed out waiting for the accumulator", 106: "timed out waiting for TMEM to drain",
+                 107: "timed out draining async work", 110: "descriptor out of bounds"}
+
+EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
+           "dkv_unpack", "dkv_version", "dkv_status_string")
+
+
+class AttendArgs(ctypes.Structure):
+    """Mirror of ``dkv_attend_args``."""
+
+    _fields_ = [
+        ("k_code", c_void_p), ("k_code_size", c_uint64), ("k_tiles", c_void_p), ("k_groups", c_void_p),
+        ("k_pos", c_void_p), ("k_items", c_void_p), ("n_k_items", c_int32), ("k_block_cols", c_int32),
+        ("k_basis", c_void_p), ("k_width", c_int32), ("k_mean", c_void_p), ("k_mean_seq_stride", c_int64),
+        ("v_code", c_void_p), ("v_code_size", c_uint64), ("v_tiles", c_void_p), ("v_groups", c_void_p),
+        ("v_sidx", c_void_p), ("v_items", c_void_p), ("n_v_items", c_int32), ("v_item_groups", c_int32),
+        ("v_seq_items", c_void_p), ("v_basis", c_void_p), ("v_width", c_int32), ("v_mean", c_void_p),
+        ("v_mean_seq_stride", c_int64),
+        ("cos_t", c_void_p), ("sin_t", c_void_p), ("max_pos", c_int32),
+        ("n_seq", c_int32), ("seq_score_off", c_void_p), ("seq_m", c_void_p),
+        ("n_layers", c_int32), ("layer", c_int32), ("n_kv_heads", c_int32), ("n_q_heads", c_int32),
+        ("head_dim", c_int32), ("q_len", c_int32), ("scaling", c_float),
+        ("query", c_void_p), ("exact_k", c_void_p), ("exact_v", c_void_p), ("n_exact", c_int32), ("mask", c_void_p),
+        ("scores", c_void_p), ("row_stats", c_void_p), ("p_exact", c_void_p), ("partial", c_void_p),
+        ("rows_pad", c_int32), ("grid_k", c_int32), ("grid_v", c_int32),
+        ("out", c_void_p), ("out_f32", c_int32), ("status", c_void_p),
+    ]
+
+
+class UnpackArgs(ctypes.Structure):
+    """Mirror of ``dkv_unpack_args``."""
+
+    _fields_ = [
+        ("code", c_void_p), ("code_size", c_uint64), ("tiles", c_void_p), ("n_tiles", c_int32),
+        ("groups", c_void_p), ("out", c_void_p), ("out_cols", c_int64), ("out_bf16", c_int32), ("status", c_void_p),
+    ]
+
+
+_LIB = None
+
+
+class DimmerKVError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load the library (once). Raises DimmerKVError when it has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise DimmerKVError(f"{LIB_PATH} is missing: build it with dimmer-kv_b200/build_lib.py "
+                                "(there is no CPU fallback)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name in ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize"):
+            fn = getattr(handle, name)
+            fn.argtypes = [ctypes.POINTER(AttendArgs), c_void_p]
+            fn.restype = c_int32
+        handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
+        handle.dkv_unpack.restype = c_int32
+        handle.dkv_version.argtypes = []
+        handle.dkv_version.restype = c_int32
+        handle.dkv_status_string.argtypes = [c_int32]
+        handle.dkv_status_string.restype = ctypes.c_char_p
+        _LIB = handle
+    return _LIB
+
+
+def check(rc: int, what: str) -> None:
+    if rc != DKV_OK:
+        raise DimmerKVError(f"{what}: {STATUS_TEXT.get(rc, rc)}")
+
+
+def check_device_status(status) -> None:
+    """Raise if a kernel recorded a device-side error in ``status`` (a 1-element int32 cuda tensor)."""
+    code = int(status.item())
+    if code != 0:
+        raise DimmerKVError(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown')}")

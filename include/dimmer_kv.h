@@ -1,0 +1,148 @@
+/* dimmer_kv.h — C ABI of the DimmerKV B200 library (libdimmerkv.so).
+ *
+ * Attention directly over a compressed KV cache (bit-plane / ladder PCA codes), for the
+ * path of SrikanthBalaaji/Dimmer-KV named by scripts/compressed_attention.py and
+ * scripts/progressive.py. Every entry point takes plain device pointers, sizes and a
+ * cudaStream_t (passed as void*), enqueues work on that stream and returns a status
+ * code (DKV_OK or one of the DKV_ERR_* values). Kernels report device-side failures
+ * (a descriptor out of bounds, a wait that timed out) in the int pointed to by
+ * `status`; the caller reads it after synchronising.
+ *
+ * The reference is Python and has no FFI of its own: each entry point below names the
+ * reference function whose work it replaces. The Python host package (dimmerkv) binds
+ * these symbols with ctypes; INTEGRATION.md shows the binding.
+ */
+#ifndef DIMMER_KV_H_
+#define DIMMER_KV_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DKV_OK 0
+#define DKV_ERR_ARGS 1       /* invalid pointer, size or shape argument */
+#define DKV_ERR_CONFIG 2     /* no kernel for this head_dim / GQA group / width */
+#define DKV_ERR_CUDA 3       /* CUDA runtime call or launch failed */
+#define DKV_ERR_TENSORMAP 4  /* cuTensorMapEncodeTiled rejected the basis layout */
+
+/* Packed plane-stream descriptors (layout documented in DESIGN.md, "Plane stream"). */
+typedef struct dkv_tile {
+  int32_t seq, token_base, n_tokens, n_groups, group_base, score_base, reserved0, reserved1;
+} dkv_tile;
+
+typedef struct dkv_group {
+  uint32_t group, code_offset, code_bytes;
+  uint8_t kind, max_planes, pad0, pad1;
+  uint8_t first[16];
+} dkv_group;
+
+/* Arguments of one attention layer over a batch of compressed conversations. */
+typedef struct dkv_attend_args {
+  /* key stream (tokens in score order) */
+  const uint8_t* k_code;
+  uint64_t k_code_size;
+  const dkv_tile* k_tiles;
+  const dkv_group* k_groups;
+  const int32_t* k_pos;          /* RoPE position per key token; < 0 hides the token */
+  const int32_t* k_items;        /* work items: tile * (n_cols / k_block_cols) + column block */
+  int32_t n_k_items;
+  int32_t k_block_cols;          /* key columns per work item: 128, 256 or 512 */
+  const void* k_basis;           /* bf16 [n_layers * n_cols][k_width]: per layer, per key column, its components */
+  int32_t k_width;               /* union components of the key basis, multiple of 64 */
+  const void* k_mean;            /* bf16 [.][n_layers][n_cols] */
+  int64_t k_mean_seq_stride;     /* elements between conversations' means; 0 = one shared mean */
+  /* value stream (tokens in value-rung order) */
+  const uint8_t* v_code;
+  uint64_t v_code_size;
+  const dkv_tile* v_tiles;
+  const dkv_group* v_groups;
+  const int32_t* v_sidx;         /* value token -> index in its conversation's score order */
+  const int32_t* v_items;        /* [n_v_items][4]: seq, first tile, end tile, first union group */
+  int32_t n_v_items;
+  int32_t v_item_groups;         /* union groups per value item; (v_item_groups / 2) * rows_pad <= 512 */
+  const int32_t* v_seq_items;    /* [n_seq][2]: value item range of each conversation */
+  const void* v_basis;           /* bf16 [n_layers][v_width][n_cols] */
+  int32_t v_width;
+  const void* v_mean;            /* bf16 [.][n_layers][n_cols] */
+  int64_t v_mean_seq_stride;
+  /* RoPE tables of the model (cos, sin per position, first half of head_dim), bf16 */
+  const void* cos_t;
+  const void* sin_t;
+  int32_t max_pos;
+  /* batch */
+  int32_t n_seq;
+  const int64_t* seq_score_off;  /* [n_seq] offset of each conversation's scores */
+  const int32_t* seq_m;          /* [n_seq] key tokens in score order */
+  /* model geometry */
+  int32_t n_layers, layer, n_kv_heads, n_q_heads, head_dim, q_len;
+  float scaling;
+  /* per-call tensors (bf16) */
+  const void* query;             /* [n_seq][n_q_heads][q_len][head_dim], RoPE applied */
+  const void* exact_k;           /* [n_seq][n_kv_heads][n_exact][head_dim] sinks, recent, new tokens */
+  const void* exact_v;
+  int32_t n_exact;
+  const float* mask;             /* [n_seq][q_len][n_exact] additive, or NULL */
+  /* workspace (device, caller-allocated) */
+  float* scores;                 /* sum_s n_q_heads * q_len * seq_m[s] */
+  float* row_stats;              /* n_seq * n_q_heads * q_len * 4 */
+  float* p_exact;                /* n_seq * n_q_heads * q_len * n_exact */
+  float* partial;                /* n_v_items * rows_pad * v_item_groups * 64 */
+  int32_t rows_pad;              /* value MMA width: multiple of 16, <= 128 */
+  int32_t grid_k, grid_v;        /* CTAs of the key / value kernels (0 = one per SM) */
+  /* output */
+  void* out;                     /* [n_seq][q_len][n_q_heads][head_dim], bf16 or fp32 */
+  int32_t out_f32;               /* 1: fp32 output (parity checks), 0: bf16 (the cache dtype) */
+  int* status;                   /* device int32 */
+} dkv_attend_args;
+
+/* One attention layer, all four stages below in order.
+ * Replaces CompressedContext.attend (scripts/compressed_attention.py:113-137), batched over
+ * conversations: compressed_attention.py:118-137 for every conversation of the batch. */
+int dkv_attend_layer(const dkv_attend_args* args, void* stream);
+
+/* Stage 1: key rebuild (tcgen05) + RoPE + q.k -> fp32 scores.
+ * Replaces CompressedContext._keys (compressed_attention.py:105-111) and the compressed
+ * score einsum of attend (compressed_attention.py:118-120). */
+int dkv_key_scores(const dkv_attend_args* args, void* stream);
+
+/* Stage 2: exact-token scores and the softmax statistics over compressed + exact tokens.
+ * Replaces compressed_attention.py:122-128. */
+int dkv_softmax_stats(const dkv_attend_args* args, void* stream);
+
+/* Stage 3: probabilities (bf16, as the reference rounds them) times value coefficients (tcgen05).
+ * Replaces the per-block einsum of compressed_attention.py:132-133. */
+int dkv_value_weights(const dkv_attend_args* args, void* stream);
+
+/* Stage 4: value basis per head + mean + exact-token values -> output.
+ * Replaces compressed_attention.py:130-131, 134-137. */
+int dkv_finalize(const dkv_attend_args* args, void* stream);
+
+/* Ragged bit-plane unpack of a packed stream to dense coefficients (stream order).
+ * Replaces progressive.dequantize (scripts/progressive.py:47-55) and the ladder decode of
+ * kvtc.quantize_groups (scripts/kvtc.py:78). */
+typedef struct dkv_unpack_args {
+  const uint8_t* code;
+  uint64_t code_size;
+  const dkv_tile* tiles;
+  int32_t n_tiles;
+  const dkv_group* groups;
+  void* out;                     /* [tokens][out_cols] */
+  int64_t out_cols;
+  int32_t out_bf16;              /* 1: bf16 (the reference's .to(dtype)), 0: fp32 */
+  int* status;
+} dkv_unpack_args;
+int dkv_unpack(const dkv_unpack_args* args, void* stream);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int dkv_version(void);
+
+/* Text of a DKV_* status code. */
+const char* dkv_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIMMER_KV_H_ */
