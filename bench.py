@@ -1,0 +1,430 @@
+"""Decode throughput over a compressed KV cache (BASELINE metric, config 3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg3|cfg1]
+
+Workload: Llama-3.2-3B architecture, random-init bf16 weights; a batch of
+64 compressed conversations per GPU with lengths uniform in [4096, 16384] (seeded), 3% hot budget,
+per-token plane counts {0,1,2,4,6,8} @ {.05,.35,.25,.2,.1,.05} on the first G coefficient groups
+(dimmerkv.synthetic documents the rules). A step = one decode step of every conversation of the
+batch: the HF model forward with every attention layer running over the packed codes
+(dkv_attend_layer: tcgen05 key rebuild + RoPE + QK, softmax statistics, tcgen05 value weighting,
+value basis + exact tokens). Conversation-parallel across GPUs: each rank decodes its own 64
+conversations, no data-path collective ("scaling": "weak"); the timed region is bracketed by a
+barrier and synchronize on every rank and the maximum over ranks is reported.
+
+--impl reference times the reference algorithm on the host CPU (the numpy restatement under
+oracle/, float32, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dimmer-kv_b200"))
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    "cfg3": dict(arch="3b", seqs=64, tmin=4096, tmax=16384, budget=0.03, max_groups=64,
+                 workload="3B random-init, 64 ragged conversations T~U[4096,16384], 3% hot budget, bs64 decode"),
+    "cfg1": dict(arch="1b", seqs=1, tmin=1536, tmax=1536, budget=0.03, max_groups=16,
+                 workload="1B random-init, 1 conversation T=1536, 3% hot budget, bs1 decode"),
+}
+METRIC = "decode tok/s over compressed KV (3B,16K,bs64)"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=8)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", choices=tuple(CONFIGS), default="cfg3")
+    p.add_argument("--seqs", type=int, default=None, help="conversations per GPU (default: the config's)")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "lines", []):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+def build_workload(cfg: dict, seqs: int, seed: int, device):
+    import torch
+
+    from dimmerkv import dimmer, synthetic
+    from dimmerkv.context import CompressedBatch, rope_tables
+
+    arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
+    model = synthetic.build_model(arch, device=device, seed=seed)
+    dimmer.install(model)
+    c = model.config
+    layers, kv, hd, hq = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
+    features = layers * kv * hd
+    rank = cfg["max_groups"] * 64
+    bases = {kind: synthetic.seeded_basis(features, rank, 1000 + seed * 2 + i, device)
+             for i, kind in enumerate(("key", "value"))}
+    g = torch.Generator().manual_seed(10_000 + seed)
+    lengths = torch.randint(cfg["tmin"], cfg["tmax"] + 1, (seqs,), generator=g).tolist()
+    max_t = max(lengths)
+    cos_f, sin_f = synthetic.rope_full(model, max_t, device)
+    convs = []
+    median = sorted(range(seqs), key=lambda i: lengths[i])[seqs // 2]
+    for i, t in enumerate(lengths):
+        ids = torch.randint(0, c.vocab_size, (1, t), generator=g).to(device)
+        keys, values = synthetic.prefill(model, ids)
+        with torch.inference_mode():
+            conv = synthetic.compress_conversation(keys, values, cos_f[:t], sin_f[:t], bases, cfg["budget"], g,
+                                                   cfg["max_groups"], keep_cpu=(i == median))
+        del keys, values
+        convs.append(conv)
+    mean = {kind: torch.stack([cv.mean[kind] for cv in convs]) for kind in ("key", "value")}
+    cos, sin = rope_tables(model, max_t + 4096, device)
+    batch = CompressedBatch([cv.codes for cv in convs], layers=layers, kv_heads=kv, head_dim=hd, q_heads=hq,
+                            basis=bases, mean=mean, cos=cos, sin=sin, device=device)
+    for cv in convs:
+        cv.codes = None  # the packed streams hold the codes now
+    return model, batch, convs, lengths, bases
+
+
+def exact_cache(model, convs):
+    import torch
+
+    from transformers import DynamicCache
+
+    layers = model.config.num_hidden_layers
+    keys = [torch.cat([cv.exact_keys[l] for cv in convs]) for l in range(layers)]
+    values = [torch.cat([cv.exact_values[l] for cv in convs]) for l in range(layers)]
+    return DynamicCache(list(zip(keys, values)), config=model.config)
+
+
+# ----------------------------------------------------------------------------- runs
+def run_ours(args, cfg, rank, world, device):
+    import torch
+    import torch.distributed as dist
+
+    from dimmerkv import dimmer
+
+    seqs = args.seqs or cfg["seqs"]
+    t0 = time.time()
+    model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed + 7919 * rank, device)
+    setup_s = time.time() - t0
+    layers = model.config.num_hidden_layers
+    # Algorithmic work of one step (SURVEY-style count): key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per
+    # layer for the key_scores launch; code bytes of both streams re-read once per layer.
+    flops_layer = 0
+    code_bytes_step = 0
+    for cv in convs:
+        flops_layer += 2 * cv.busy_key * cv.groups * 64 * batch.n_cols + 2 * cv.middle * batch.q_heads * batch.head_dim
+        code_bytes_step += cv.hot_bytes * layers
+
+    cache = exact_cache(model, convs)
+    ids = torch.randint(0, model.config.vocab_size, (seqs, 1), device=device,
+                        generator=torch.Generator(device=device).manual_seed(args.seed + rank))
+    positions = torch.tensor(lengths, device=device)[:, None]
+    dimmer.STATE.compressed = batch
+    stream = torch.cuda.current_stream(device)
+
+    # Per-launch timing of the key-rebuild kernel: events around each stage of every layer.
+    key_events = []
+
+    def timed_layer(layer, call, a, s):
+        from dimmerkv import _lib
+
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _lib.check(batch.lib.dkv_key_scores(a, s), "dkv_key_scores")
+        e1.record(stream)
+        _lib.check(batch.lib.dkv_softmax_stats(a, s), "dkv_softmax_stats")
+        rows = batch.q_heads * int(a.q_len)
+        for r0 in range(0, rows, a.rows_pad):
+            n = min(a.rows_pad, rows - r0)
+            if n != rows:
+                raise RuntimeError("bench timing expects one row chunk")
+        _lib.check(batch.lib.dkv_value_weights(a, s), "dkv_value_weights")
+        _lib.check(batch.lib.dkv_finalize(a, s), "dkv_finalize")
+        key_events.append((e0, e1))
+
+    def step(ids_, pos_):
+        out = model(input_ids=ids_, past_key_values=cache, position_ids=pos_, use_cache=True)
+        return out.logits[:, -1].argmax(-1, keepdim=True)
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            ids = step(ids, positions)
+            positions = positions + 1
+        torch.cuda.synchronize(device)
+        batch.check_status()
+        if world > 1:
+            dist.barrier()
+        batch.timer = timed_layer
+        key_events.clear()
+        with ClockSampler(device.index if device.index is not None else 0) as clocks:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(device)
+            start.record(stream)
+            for _ in range(args.steps):
+                ids = step(ids, positions)
+                positions = positions + 1
+            end.record(stream)
+            torch.cuda.synchronize(device)
+        batch.timer = None
+        batch.check_status()
+        elapsed = start.elapsed_time(end) / 1e3
+        key_ms = [a.elapsed_time(b) for a, b in key_events]
+
+    t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    elapsed_max = float(t.item())
+
+    # End to end through the public API: host token ids in, host next tokens out, every step.
+    e2e = None
+    if not args.no_e2e:
+        from dimmerkv.compressed_attention import greedy_decode_batch
+
+        host_ids = ids.cpu().pin_memory()
+        with torch.inference_mode():
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            _, stats = greedy_decode_batch(model, batch, cache, host_ids, positions.cpu(), args.steps)
+            torch.cuda.synchronize(device)
+            e2e_s = time.perf_counter() - t0
+        t = torch.tensor([e2e_s], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * seqs * args.steps / float(t.item()), "unit": "tok/s",
+               "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"]}
+    dimmer.STATE.compressed = None
+
+    result = None
+    if rank == 0:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+        peak_name = "of measured (bf16_tflops_sustained)" if peaks else "of fallback"
+        key_avg_ms = statistics.mean(key_ms) if key_ms else float("nan")
+        achieved = flops_layer / (key_avg_ms / 1e3) / 1e12
+        traffic = None
+        prof = ROOT / "profiles" / "key_scores_traffic.json"
+        if prof.exists():
+            traffic = json.loads(prof.read_text()).get("bytes_per_launch")
+        clk = clocks.summary()
+        tokps = world * seqs * args.steps / elapsed_max
+        result = {
+            "metric": METRIC, "value": round(tokps, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, "
+            "random token ids, synthetic PCA basis and plane counts)",
+            "config": {"workload": cfg["workload"], "conversations_per_gpu": seqs, "context_min": min(lengths),
+                       "context_max": max(lengths), "context_mean": round(sum(lengths) / len(lengths), 1),
+                       "budget": cfg["budget"], "parallelism": f"conversation-parallel x{world}",
+                       "l2": "inputs larger than L2 (codes re-read per layer, > 1 GB per layer)"},
+            "code_read_gbs": round(code_bytes_step / (elapsed_max / args.steps) / 1e9, 2),
+            "roofline": {"bound": "tensor", "kernel": "key_scores (tcgen05 key rebuild + RoPE + QK)",
+                         "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak_tf, 4), "peak_source": peak_name,
+                         "avg_launch_ms": round(key_avg_ms, 4), "launches": len(key_ms),
+                         "algorithmic_flop_per_launch": flops_layer, "traffic": traffic},
+            "clocks": clk,
+            "gpu_launches": len(key_ms) * 4,
+            "e2e": e2e,
+            "setup_s": round(setup_s, 1),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_sample(model, convs, bases, lengths, layers=2)
+    return result
+
+
+def cpu_sample(model, convs, bases, lengths, layers: int = 2) -> dict:
+    """The reference algorithm on the host: one conversation, ``layers`` attention layers of one decode
+    step (numpy float32, all host threads), scaled to a full step of every conversation."""
+    import numpy as np
+    import torch
+
+    from oracle import codes as oc
+    from oracle.attention import OracleContext
+
+    cv = next(c for c in convs if c.cpu_codes is not None)  # the median-length conversation
+    c = model.config
+    L, H, D, HQ = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
+    decoded, choice = {}, {}
+    for kind in ("key", "value"):
+        codes, low, span, planes, m = cv.cpu_codes[kind]
+        decoded[kind] = oc.dequantize(codes, low, span, planes)
+        choice[kind] = m
+    from dimmerkv.synthetic import rope_full
+
+    cos, sin = rope_full(model, cv.tokens, next(model.parameters()).device)
+    ctx = OracleContext(start=4, end=cv.tokens - 32, layers=L, heads=H, head_dim=D, choice=choice, decoded=decoded,
+                        basis={k: v.cpu().numpy() for k, v in bases.items()},
+                        mean={k: v.cpu().numpy() for k, v in cv.mean.items()},
+                        cos=cos.cpu().numpy(), sin=sin.cpu().numpy(), dtype="bf16", compute=np.float32)
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, HQ, 1, D)).astype(np.float32)
+    k = rng.standard_normal((1, H, 36, D)).astype(np.float32)
+    v = rng.standard_normal((1, H, 36, D)).astype(np.float32)
+    t0 = time.perf_counter()
+    for layer in range(layers):
+        ctx.attend(layer, q, k, v, None, D ** -0.5)
+    per_layer = (time.perf_counter() - t0) / layers
+    per_token = per_layer * L
+    return {"value": round(1.0 / per_token, 5), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle attention (numpy float32) over one conversation of {cv.tokens} tokens, {layers} of {L} "
+                      f"layers of one decode step, scaled to one token per conversation (per-layer {per_layer:.3f} s)"}
+
+
+def run_reference(args, cfg, rank, world):
+    """The reference algorithm on the host cores (oracle port), rank 0 only, bounded samples per step."""
+    if rank != 0:
+        return None
+    import numpy as np
+    import torch
+
+    from oracle import codes as oc
+    from oracle.attention import OracleContext
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(os.cpu_count() or 1)
+    except ImportError:
+        pass
+    rng = np.random.default_rng(args.seed)
+    L, H, D, HQ = (28, 8, 128, 24) if cfg["arch"] == "3b" else (16, 8, 64, 32)
+    F = L * H * D
+    T = (cfg["tmin"] + cfg["tmax"]) // 2
+    M = T - 36
+    probs = np.array([.05, .35, .25, .2, .1, .05])
+    m = {k: rng.choice([0, 1, 2, 4, 6, 8], size=M, p=probs) for k in ("key", "value")}
+    exact = F * 2
+    remaining = int(cfg["budget"] * T * 2 * exact) - 36 * 2 * exact
+    per_group = sum(int((8 * m[k] + 4 * (m[k] > 0)).sum()) for k in m)
+    G = max(1, min(cfg["max_groups"], (remaining - 2 * M) // per_group))
+    R = G * 64
+    decoded = {}
+    for kind in ("key", "value"):
+        coeff = rng.standard_normal((M, R)).astype(np.float32)
+        codes, low, span = oc.quantize8(coeff, 64)
+        decoded[kind] = np.zeros((M, R), dtype=np.float32)
+        decoded[kind][:] = oc.dequantize(codes, low, span, np.repeat(m[kind][:, None], G, axis=1))
+    basis = {k: np.linalg.qr(rng.standard_normal((F, R)).astype(np.float32))[0].astype(np.float32) for k in m}
+    mean = {k: (rng.standard_normal(F) * 0.1).astype(np.float32) for k in m}
+    pos = np.arange(T, dtype=np.float32)
+    inv = 1.0 / (500000.0 ** (np.arange(0, D, 2, dtype=np.float32) / D))
+    ang = pos[:, None] * inv
+    cos = np.concatenate([np.cos(ang), np.cos(ang)], 1).astype(np.float32)
+    sin = np.concatenate([np.sin(ang), np.sin(ang)], 1).astype(np.float32)
+    ctx = OracleContext(start=4, end=T - 32, layers=L, heads=H, head_dim=D, choice=m, decoded=decoded, basis=basis,
+                        mean=mean, cos=cos, sin=sin, dtype="bf16", compute=np.float32)
+    q = rng.standard_normal((1, HQ, 1, D)).astype(np.float32)
+    k = rng.standard_normal((1, H, 36, D)).astype(np.float32)
+    v = rng.standard_normal((1, H, 36, D)).astype(np.float32)
+    for i in range(args.warmup):
+        ctx.attend(i % L, q, k, v, None, D ** -0.5)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ctx.attend(i % L, q, k, v, None, D ** -0.5)
+    per_layer = (time.perf_counter() - t0) / args.steps
+    value = 1.0 / (per_layer * L)
+    cores = os.cpu_count() or 1
+    sample = (f"oracle attention (numpy float32) over one {T}-token conversation (G={G} groups), one layer per step, "
+              f"scaled x{L} layers to one token per conversation")
+    return {"metric": METRIC, "value": round(value, 5), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_layer * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": cfg["workload"], "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        result = run_reference(args, cfg, rank, world)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(minutes=10), device_id=device)
+    try:
+        result = run_ours(args, cfg, rank, world, device)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -23,9 +23,9 @@ GROUP = 64
 def from_progressive(codes: torch.Tensor, low: torch.Tensor, span: torch.Tensor, planes: torch.Tensor,
                      rung: torch.Tensor) -> TokenCodes:
     """codes u8 [M, G, 64], low/span f16 [M, G], planes [M, G] (0..8), rung [M] (e.g. hot_pieces)."""
-    m = planes.to(torch.int32)
-    index = torch.where(m[..., None] > 0, codes.to(torch.int32) >> (8 - m).clamp(0, 8)[..., None],
-                        torch.zeros((), dtype=torch.int32, device=codes.device))
+    m = planes.to(torch.uint8)
+    index = torch.where(m[..., None] > 0, codes >> (8 - m).clamp(0, 8)[..., None],
+                        torch.zeros((), dtype=torch.uint8, device=codes.device))
     return TokenCodes(rung=rung.to(torch.int64), planes=planes.to(torch.uint8), index=index.contiguous(),
                       header=header_bits(low, span), kind=KIND_PROGRESSIVE)
 

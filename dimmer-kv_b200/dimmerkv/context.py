@@ -27,7 +27,7 @@ class TokenCodes:
 
     rung: torch.Tensor    # int64 [M]: precision step; < 0 = evicted
     planes: torch.Tensor  # uint8 [M, G]
-    index: torch.Tensor   # int32 [M, G, 64]
+    index: torch.Tensor   # uint8 (planes <= 8) or int32 (raw bf16 bits) [M, G, 64]
     header: torch.Tensor  # int32 [M, G]
     kind: int = KIND_PROGRESSIVE
 

@@ -35,7 +35,7 @@ class StreamCodes:
     """One conversation's compressed tokens of one stream (keys or values), in stream order."""
 
     planes: torch.Tensor  # uint8 [n, G]: planes per (token, group); 0 none, 1..8, 16 raw bf16
-    index: torch.Tensor   # int32 [n, G, 64]: the m-bit index (bf16 bits when planes == 16)
+    index: torch.Tensor   # uint8 or int32 [n, G, 64]: the m-bit index (bf16 bits, int32, when planes == 16)
     header: torch.Tensor  # int32 [n, G]: f16 bits of low | f16 bits of mult << 16
     aux: torch.Tensor     # int32 [n]: RoPE position (keys) or score-order index (values)
     kind: int = KIND_PROGRESSIVE
@@ -93,8 +93,9 @@ def pack_streams(convs: list[StreamCodes], union: torch.Tensor | None = None) ->
     union = union.to(device=device, dtype=torch.int64)
     gu = int(union.numel())
     P = planes_all[:, union]                                        # [N, Gu]
-    IDX = torch.cat([c.index for c in convs])[:, union] if sum(sizes) else \
-        torch.zeros(0, gu, GROUP, dtype=torch.int32, device=device)
+    index_dtype = torch.uint8 if all(c.index.dtype == torch.uint8 for c in convs) else torch.int32
+    IDX = torch.cat([c.index.to(index_dtype) for c in convs])[:, union] if sum(sizes) else \
+        torch.zeros(0, gu, GROUP, dtype=index_dtype, device=device)
     HDR = torch.cat([c.header for c in convs])[:, union] if sum(sizes) else \
         torch.zeros(0, gu, dtype=torch.int32, device=device)
     aux = torch.cat([c.aux.to(torch.int32) for c in convs]) if sum(sizes) else \
@@ -156,20 +157,23 @@ def pack_streams(convs: list[StreamCodes], union: torch.Tensor | None = None) ->
         t_ = tile_of[tok]
         off = offsets[t_, grp] + (row_of[tok] - first[0][t_, grp]) * 4
         code32[off // 4] = HDR[tok, grp]
-    # Plane words, most significant plane first.
+    # Plane words, most significant plane first (in slices to bound the temporaries).
     weights = (2 ** torch.arange(8, device=device, dtype=torch.int32)).to(torch.int32)
+    chunk = 1 << 21
     for j in range(MAX_PLANES):
-        tok, grp = torch.nonzero(P > j, as_tuple=True)
-        if tok.numel() == 0:
+        tok_all, grp_all = torch.nonzero(P > j, as_tuple=True)
+        if tok_all.numel() == 0:
             break
-        t_ = tile_of[tok]
-        m = P[tok, grp]
-        shift = (m - 1 - j).to(torch.int32)
-        bits = (IDX[tok, grp] >> shift[:, None]) & 1                      # [K, 64]
-        packed = (bits.view(-1, 8, 8) * weights).sum(dim=-1).to(torch.uint8)  # [K, 8]
-        words = packed.contiguous().view(torch.int64).view(-1)
-        off = offsets[t_, grp] + seg_off[j][t_, grp] + (row_of[tok] - first[j][t_, grp]) * 8
-        code64[off // 8] = words
+        for c0 in range(0, tok_all.numel(), chunk):
+            tok, grp = tok_all[c0 : c0 + chunk], grp_all[c0 : c0 + chunk]
+            t_ = tile_of[tok]
+            m = P[tok, grp]
+            shift = (m - 1 - j).to(torch.int32)
+            bits = (IDX[tok, grp].to(torch.int32) >> shift[:, None]) & 1                # [K, 64]
+            packed = (bits.view(-1, 8, 8) * weights).sum(dim=-1).to(torch.uint8)       # [K, 8]
+            words = packed.contiguous().view(torch.int64).view(-1)
+            off = offsets[t_, grp] + seg_off[j][t_, grp] + (row_of[tok] - first[j][t_, grp]) * 8
+            code64[off // 8] = words
 
     # Descriptors.
     tt, gg = torch.nonzero(present, as_tuple=True)

@@ -52,14 +52,16 @@ class OracleContext:
 
     def __init__(self, *, start: int, end: int, layers: int, heads: int, head_dim: int,
                  choice: dict, decoded: dict, basis: dict, mean: dict, cos: np.ndarray, sin: np.ndarray,
-                 dtype: str = "bf16"):
+                 dtype: str = "bf16", compute=np.float64):
         """``choice[kind]`` [M] rung (-1 evicted); ``decoded[kind]`` [M, F] float32 dequantised
-        coefficients; ``basis[kind]`` [F, F]; ``mean[kind]`` [F]; cos/sin [tokens, head_dim] float32."""
+        coefficients; ``basis[kind]`` [F, F]; ``mean[kind]`` [F]; cos/sin [tokens, head_dim] float32.
+        ``compute`` is the arithmetic type (float64 for checking; float32 when timed as the CPU baseline)."""
+        f = self.f = compute
         self.start, self.end = start, end
         self.layers, self.heads, self.head_dim = layers, heads, head_dim
         self.dtype = dtype
-        self.cos = round_dtype(cos[start:end], dtype).astype(np.float64)
-        self.sin = round_dtype(sin[start:end], dtype).astype(np.float64)
+        self.cos = round_dtype(cos[start:end], dtype).astype(f)
+        self.sin = round_dtype(sin[start:end], dtype).astype(f)
         key_choice = np.asarray(choice["key"])
         self.mean, self.coeff, self.basis, self.rows = {}, {}, {}, {}
         for kind in ("key", "value"):
@@ -68,10 +70,10 @@ class OracleContext:
             dec = np.asarray(decoded[kind], dtype=np.float32)
             union = np.nonzero((dec[kept] != 0).any(axis=0))[0]  # :53
             self.basis[kind] = round_dtype(np.asarray(basis[kind], dtype=np.float32)[:, union].T, dtype).astype(
-                np.float64).reshape(len(union), layers, -1)  # :54
+                f).reshape(len(union), layers, -1)  # :54
             self.mean[kind] = round_dtype(np.asarray(mean[kind], dtype=np.float32), dtype).astype(
-                np.float64).reshape(layers, -1)  # :45
-            self.coeff[kind] = round_dtype(dec[:, union], dtype).astype(np.float64)  # :76 (per block)
+                f).reshape(layers, -1)  # :45
+            self.coeff[kind] = round_dtype(dec[:, union], dtype).astype(f)  # :76 (per block)
             self.rows[kind] = np.nonzero(kept)[0]
         order = self.rows["key"][np.argsort(key_choice[self.rows["key"]], kind="stable")]
         self.order = order  # :79
@@ -92,9 +94,10 @@ class OracleContext:
 
         Returns output [B, q, Hq, D] float64 (and, with return_probs, (p_c, p_e) in float64 with
         p_c in score order)."""
-        q = round_dtype(np.asarray(query, np.float32), self.dtype).astype(np.float64)
-        k = round_dtype(np.asarray(key, np.float32), self.dtype).astype(np.float64)
-        v = round_dtype(np.asarray(value, np.float32), self.dtype).astype(np.float64)
+        f = self.f
+        q = round_dtype(np.asarray(query, np.float32), self.dtype).astype(f)
+        k = round_dtype(np.asarray(key, np.float32), self.dtype).astype(f)
+        v = round_dtype(np.asarray(value, np.float32), self.dtype).astype(f)
         batch, q_heads, q_len, dim = q.shape
         groups = q_heads // self.heads
         ck = self.keys(layer)
@@ -102,14 +105,14 @@ class OracleContext:
         scores_c = np.einsum("bhgqd,hnd->bhgqn", gq, ck) * scaling  # :120
         scores_e = np.einsum("bhgqd,bhnd->bhgqn", gq, k) * scaling  # :122
         if attention_mask is not None:
-            scores_e = scores_e + np.asarray(attention_mask, np.float64)[:, :, None]  # :124
+            scores_e = scores_e + np.asarray(attention_mask, f)[:, :, None]  # :124
         middle = scores_c.shape[-1]
         allsc = np.concatenate([scores_c, scores_e], axis=-1)
         mx = allsc.max(axis=-1, keepdims=True)
         ex = np.exp(allsc - mx)
         probs = ex / ex.sum(axis=-1, keepdims=True)  # :126
-        p_c = round_dtype(probs[..., :middle].astype(np.float32), self.dtype).astype(np.float64)  # :127
-        p_e = round_dtype(probs[..., middle:].astype(np.float32), self.dtype).astype(np.float64)  # :128
+        p_c = round_dtype(probs[..., :middle].astype(np.float32), self.dtype).astype(f)  # :127
+        p_e = round_dtype(probs[..., middle:].astype(np.float32), self.dtype).astype(f)  # :128
         out_c = p_c.sum(axis=-1, keepdims=True) * self.mean["value"][layer].reshape(1, self.heads, 1, 1, dim)  # :130
         layer_basis = self.basis["value"][:, layer].reshape(-1, self.heads, self.head_dim)  # :131
         weighted = np.einsum("bhgqn,nr->bhgqr", p_c[..., self.value_index], self.coeff["value"][self.rows["value"]])
