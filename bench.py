@@ -182,25 +182,25 @@ def run_ours(args, cfg, rank, world, device):
     dimmer.STATE.compressed = batch
     stream = torch.cuda.current_stream(device)
 
-    # Per-launch timing of the key-rebuild kernel: events around each stage of every layer.
+    # Per-launch timing of every stage: CUDA events on the launching stream around each kernel.
     key_events = []
 
     def timed_layer(layer, call, a, s):
         from dimmerkv import _lib
 
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        if batch.q_heads * int(a.q_len) > a.rows_pad:
+            raise RuntimeError("bench timing expects one row chunk per layer")
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record(stream)
         _lib.check(batch.lib.dkv_key_scores(a, s), "dkv_key_scores")
-        e1.record(stream)
+        ev[1].record(stream)
         _lib.check(batch.lib.dkv_softmax_stats(a, s), "dkv_softmax_stats")
-        rows = batch.q_heads * int(a.q_len)
-        for r0 in range(0, rows, a.rows_pad):
-            n = min(a.rows_pad, rows - r0)
-            if n != rows:
-                raise RuntimeError("bench timing expects one row chunk")
+        ev[2].record(stream)
         _lib.check(batch.lib.dkv_value_weights(a, s), "dkv_value_weights")
+        ev[3].record(stream)
         _lib.check(batch.lib.dkv_finalize(a, s), "dkv_finalize")
-        key_events.append((e0, e1))
+        ev[4].record(stream)
+        key_events.append(ev)
 
     def step(ids_, pos_):
         out = model(input_ids=ids_, past_key_values=cache, position_ids=pos_, use_cache=True)
@@ -221,14 +221,18 @@ def run_ours(args, cfg, rank, world, device):
             torch.cuda.synchronize(device)
             start.record(stream)
             for _ in range(args.steps):
+                torch.cuda.nvtx.range_push("decode_step")
                 ids = step(ids, positions)
                 positions = positions + 1
+                torch.cuda.nvtx.range_pop()
             end.record(stream)
             torch.cuda.synchronize(device)
         batch.timer = None
         batch.check_status()
         elapsed = start.elapsed_time(end) / 1e3
-        key_ms = [a.elapsed_time(b) for a, b in key_events]
+        key_ms = [ev[0].elapsed_time(ev[1]) for ev in key_events]
+        stage_ms = {name: sum(ev[i].elapsed_time(ev[i + 1]) for ev in key_events) / args.steps
+                    for i, name in enumerate(("key_scores", "softmax_stats", "value_weights", "finalize"))}
 
     t = torch.tensor([elapsed], device=device, dtype=torch.float64)
     if world > 1:
@@ -286,6 +290,7 @@ def run_ours(args, cfg, rank, world, device):
                          "avg_launch_ms": round(key_avg_ms, 4), "launches": len(key_ms),
                          "algorithmic_flop_per_launch": flops_layer, "traffic": traffic},
             "clocks": clk,
+            "stage_ms_per_step": {k: round(v, 3) for k, v in stage_ms.items()},
             "gpu_launches": len(key_ms) * 4,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
