@@ -93,6 +93,7 @@ const char* dkv_status_string(int status) {
     case DKV_ERR_CONFIG: return "unsupported configuration";
     case DKV_ERR_CUDA: return "CUDA error";
     case DKV_ERR_TENSORMAP: return "tensor map encoding failed";
+    case DKV_ERR_SCRATCH: return "scratch larger than the static array of dkv_attend_layer_static";
     default: return "unknown status";
   }
 }

@@ -1,0 +1,74 @@
+// static_scratch.cu — dkv_attend_layer_static: one attention layer without any device allocation.
+//
+// dkv_attend_layer needs four scratch buffers between its kernels (scores, row statistics, exact-token
+// probabilities, value partial sums) and expects the caller to allocate them. Some callers cannot:
+// a plugin running inside another framework's memory manager (an inference-server backend, a custom
+// runtime) that owns every device allocation and forbids direct cudaMalloc / cudaFree, or a
+// latency-critical loop that may not pay for an allocation (cudaMalloc and cudaFree can synchronise
+// the device). For them this entry point carves the scratch out of one fixed array in device memory
+// that the library itself declares; the caller still passes the inputs, the output and the status word.
+//
+// Limits and behaviour:
+//   - the array holds kStaticScratchBytes (32 MiB). Every GPU that loads the library keeps it until the
+//     process exits. A call whose scratch does not fit returns DKV_ERR_SCRATCH and launches nothing.
+//     One conversation of 16K tokens of a Llama-3.2-3B-shaped model needs about 6 MiB per decode step.
+//   - the first call on a device looks the array's device address up (cudaGetSymbolAddress, with that
+//     device current) and caches it; make that first call before any stream capture.
+//   - all calls share the array and it keeps the last call's contents. Every scratch byte the kernels
+//     read is written earlier in the same call, so nothing needs clearing between calls, but two calls
+//     that overlap on the GPU (different streams, or different host threads) race on it.
+#include <mutex>
+
+#include "../../include/dimmer_kv.h"
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mutex;
+void* g_static_addr[kMaxDevices] = {};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Device address of the array on the current device (looked up once per device).
+int static_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DKV_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr) return DKV_ERR_CUDA;
+    g_static_addr[dev] = ptr;
+  }
+  *out = g_static_addr[dev];
+  return DKV_OK;
+}
+
+}  // namespace
+
+extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_scores, void* stream) {
+  if (args == nullptr || n_scores < 0 || args->n_seq < 0 || args->q_len < 1 || args->n_exact < 0 ||
+      args->n_v_items < 0 || args->rows_pad < 0 || args->v_item_groups < 0)
+    return DKV_ERR_ARGS;
+  const size_t rows = static_cast<size_t>(args->n_seq) * args->n_q_heads * args->q_len;
+  const size_t scores_bytes = align256(static_cast<size_t>(n_scores) * sizeof(float));
+  const size_t stats_bytes = align256(rows * 4 * sizeof(float));
+  const size_t exact_bytes = align256(rows * static_cast<size_t>(args->n_exact) * sizeof(float));
+  const size_t partial_bytes = align256(static_cast<size_t>(args->n_v_items) * args->rows_pad *
+                                        args->v_item_groups * 64 * sizeof(float));
+  const size_t total = scores_bytes + stats_bytes + exact_bytes + partial_bytes;
+  if (total > kStaticScratchBytes) return DKV_ERR_SCRATCH;
+  void* base = nullptr;
+  const int rc = static_scratch_address(&base);
+  if (rc != DKV_OK) return rc;
+  unsigned char* p = static_cast<unsigned char*>(base);
+  dkv_attend_args a = *args;
+  a.scores = reinterpret_cast<float*>(p);
+  a.row_stats = reinterpret_cast<float*>(p + scores_bytes);
+  a.p_exact = reinterpret_cast<float*>(p + scores_bytes + stats_bytes);
+  a.partial = reinterpret_cast<float*>(p + scores_bytes + stats_bytes + exact_bytes);
+  return dkv_attend_layer(&a, stream);
+}

@@ -26,6 +26,7 @@ extern "C" {
 #define DKV_ERR_CONFIG 2     /* no kernel for this head_dim / GQA group / width */
 #define DKV_ERR_CUDA 3       /* CUDA runtime call or launch failed */
 #define DKV_ERR_TENSORMAP 4  /* cuTensorMapEncodeTiled rejected the basis layout */
+#define DKV_ERR_SCRATCH 5    /* the call needs more scratch than dkv_attend_layer_static's fixed array */
 
 /* Packed plane-stream descriptors (layout documented in DESIGN.md, "Plane stream"). */
 typedef struct dkv_tile {
@@ -118,6 +119,17 @@ int dkv_value_weights(const dkv_attend_args* args, void* stream);
 /* Stage 4: value basis per head + mean + exact-token values -> output.
  * Replaces compressed_attention.py:130-131, 134-137. */
 int dkv_finalize(const dkv_attend_args* args, void* stream);
+
+/* dkv_attend_layer for callers that cannot allocate device memory. No counterpart in the reference.
+ * Callers inside another framework's memory manager (which owns every device allocation and forbids
+ * cudaMalloc / cudaFree) or in latency-critical loops pass the same arguments as to
+ * dkv_attend_layer except the four scratch pointers (scores, row_stats, p_exact, partial), which are
+ * ignored; the scratch comes from a fixed 32 MiB array declared by the library in device memory.
+ * n_scores = sum over conversations of n_q_heads * q_len * seq_m[s]. Returns DKV_ERR_SCRATCH, having
+ * launched nothing, when the scratch would not fit. The first call on a device looks up the array's
+ * address and must come before any stream capture. Calls share the array: calls that overlap on the
+ * GPU race. Allocates nothing. */
+int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_scores, void* stream);
 
 /* Ragged bit-plane unpack of a packed stream to dense coefficients (stream order).
  * Replaces progressive.dequantize (scripts/progressive.py:47-55) and the ladder decode of
