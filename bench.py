@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=None,
+                   help="build the model with this many layers (same per-layer shapes; for small profiling cases)")
     return p.parse_args()
 
 
@@ -106,14 +108,14 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workload
-def build_workload(cfg: dict, seqs: int, seed: int, device):
+def build_workload(cfg: dict, seqs: int, seed: int, device, layers_override=None):
     import torch
 
     from dimmerkv import dimmer, synthetic
     from dimmerkv.context import CompressedBatch, rope_tables
 
     arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
-    model = synthetic.build_model(arch, device=device, seed=seed)
+    model = synthetic.build_model(arch, device=device, seed=seed, layers=layers_override)
     dimmer.install(model)
     c = model.config
     layers, kv, hd, hq = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
@@ -164,7 +166,7 @@ def run_ours(args, cfg, rank, world, device):
 
     seqs = args.seqs or cfg["seqs"]
     t0 = time.time()
-    model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed + 7919 * rank, device)
+    model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed + 7919 * rank, device, args.layers)
     setup_s = time.time() - t0
     layers = model.config.num_hidden_layers
     # Algorithmic work of one step (SURVEY-style count): key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per

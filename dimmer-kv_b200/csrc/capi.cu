@@ -134,6 +134,7 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   p.q_len = a->q_len;
   p.head_dim = a->head_dim;
   p.scaling = a->scaling;
+  p.max_planes = a->k_max_planes;
   p.status = a->status;
   const int grid = a->grid_k > 0 ? a->grid_k : (a->n_k_items < sm_count() ? a->n_k_items : sm_count());
   return dkv::run_key_scores(map, p, nb, grid, static_cast<cudaStream_t>(stream));

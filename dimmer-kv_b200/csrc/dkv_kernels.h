@@ -40,6 +40,7 @@ struct KeyScoreParams {
   float* scores;                  // [sum over seq][n_q_heads][q_len][M_s]
   int layer, n_cols, n_q_heads, q_per_kv, q_len, head_dim;
   float scaling;
+  int max_planes;                 // largest plane count of any key block (> 8: raw blocks present)
   int* status;
 };
 int run_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int nb, int grid, cudaStream_t stream);

@@ -22,9 +22,10 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const Finali
   const int D = p.head_dim;
   const int G = p.q_per_kv;
   const int R = p.r_v;
-  const int parts = blockDim.x / D;
-  const int d = threadIdx.x % D;
-  const int part = threadIdx.x / D;
+  const int parts = blockDim.x / (D / 2);   // component slices
+  const int d2 = threadIdx.x % (D / 2);     // output dims 2*d2, 2*d2+1
+  const int part = threadIdx.x / (D / 2);
+  const int d = threadIdx.x;                // output dim of the final combine (threads 0 .. D-1)
   float* red = w + G * R;  // [parts][G][D]
   const int item_cols = p.item_groups * 64;
 
@@ -52,19 +53,33 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const Finali
       }
     }
     __syncthreads();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const __nv_bfloat16* bv = p.basis_v + static_cast<int64_t>(p.layer) * R * p.n_cols + kvh * D + d;
+    // Value basis of this KV head: each thread owns two adjacent output dims (one bf16x2 load per
+    // component) and a slice of the components; slices are summed through shared memory.
+    float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+    const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(
+        p.basis_v + static_cast<int64_t>(p.layer) * R * p.n_cols + kvh * D + 2 * d2);
+    const int64_t bstride = p.n_cols / 2;
+#pragma unroll 4
     for (int r = part; r < R; r += parts) {
-      const float b = __bfloat162float(bv[static_cast<int64_t>(r) * p.n_cols]);
+      const float2 b = __bfloat1622float2(bv[static_cast<int64_t>(r) * bstride]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (j < G) acc[j] += w[j * R + r] * b;
+      for (int j = 0; j < 4; ++j) {
+        if (j < G) {
+          const float wv = w[j * R + r];
+          acc[j][0] += wv * b.x;
+          acc[j][1] += wv * b.y;
+        }
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j < G) red[(part * G + j) * D + d] = acc[j];
+    for (int j = 0; j < 4; ++j) {
+      if (j < G) {
+        red[(part * G + j) * D + 2 * d2] = acc[j][0];
+        red[(part * G + j) * D + 2 * d2 + 1] = acc[j][1];
+      }
+    }
     __syncthreads();
-    if (part == 0) {
+    if (threadIdx.x < D) {
       const float mean = __bfloat162float(p.mean_v[static_cast<int64_t>(s) * p.mean_seq_stride +
                                                    static_cast<int64_t>(p.layer) * p.n_cols + kvh * D + d]);
       const __nv_bfloat16* vex = p.exact_v + (static_cast<int64_t>(s) * n_kv + kvh) * p.n_exact * D + d;
@@ -91,7 +106,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const Finali
 
 int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   if (p.q_per_kv > 4 || p.head_dim > 256 || kFinalizeThreads % p.head_dim != 0) return kDkvErrConfig;
-  const int parts = kFinalizeThreads / p.head_dim;
+  const int parts = kFinalizeThreads / (p.head_dim / 2);
   const int smem = (p.q_per_kv * p.r_v + parts * p.q_per_kv * p.head_dim) * 4;
   if (smem > 227 * 1024) return kDkvErrConfig;
   if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)

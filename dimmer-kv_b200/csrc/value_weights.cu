@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               const int gi = half ? hi : lo;
               if (gi < 0) continue;
               const GroupRegs gr = load_group(&p.groups[gi]);
-              if (gr.code_bytes > static_cast<uint32_t>(kVCodeSlot) ||
+              if (gr.code_bytes > static_cast<uint32_t>(kVCodeSlot - 32) ||
                   static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size) {
                 record_error(p.status, kErrBadDescriptor);
                 *abort_flag = 1;
@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
                 *abort_flag = 1;
                 break;
               }
+              stash_group(c_slots + (cs + 1) * kVCodeSlot, &p.groups[gi]);
               mbar_arrive_expect_tx(&code_full[cs], gr.code_bytes);
               bulk_load(c_slots + cs * kVCodeSlot, p.code + gr.code_offset, gr.code_bytes, &code_full[cs]);
               ++c_iter;
@@ -256,12 +257,12 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             uint8_t* dst = a + half * 16384;
             uint32_t out[16];
             if (gi >= 0) {
-              const GroupRegs gr = load_group(&p.groups[gi]);
               const int cs = c_iter % kVCodeSlots;
               if (!mbar_wait(&code_full[cs], (c_iter / kVCodeSlots) & 1, p.status, kErrWaitCodes)) {
                 *abort_flag = 1;
                 break;
               }
+              const GroupRegs gr = stashed_group(c_slots + (cs + 1) * kVCodeSlot);
               decode_half(c_slots + cs * kVCodeSlot, gr, tile.n_tokens, r, h, out);
               mbar_arrive(&code_empty[cs]);
               ++c_iter;

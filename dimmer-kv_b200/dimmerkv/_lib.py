@@ -43,6 +43,7 @@ class AttendArgs(ctypes.Structure):
         ("scores", c_void_p), ("row_stats", c_void_p), ("p_exact", c_void_p), ("partial", c_void_p),
         ("rows_pad", c_int32), ("grid_k", c_int32), ("grid_v", c_int32),
         ("out", c_void_p), ("out_f32", c_int32), ("status", c_void_p),
+        ("k_max_planes", c_int32), ("v_max_planes", c_int32),
     ]
 
 

@@ -213,6 +213,7 @@ class CompressedBatch:
         a.p_exact, a.partial = w["p_exact"].data_ptr(), w["partial"].data_ptr()
         a.rows_pad, a.grid_k, a.grid_v = rows_pad, 0, 0
         a.out, a.out_f32, a.status = out.data_ptr(), int(out.dtype == torch.float32), self.status.data_ptr()
+        a.k_max_planes, a.v_max_planes = ks.max_planes, vs.max_planes
         return a
 
     def attend_layer(self, layer: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,

@@ -52,6 +52,7 @@ class PackedStream:
     seq_tokens: list = field(default_factory=list)  # (first token, end token) per conversation
     present: torch.Tensor | None = None             # bool [n_tiles, Gu] on the CPU
     tile_blocks: torch.Tensor | None = None         # int64 [n_tiles] on the CPU (blocks per tile)
+    max_planes: int = 0                             # largest plane count of any block
 
     @property
     def n_tiles(self) -> int:
@@ -200,4 +201,5 @@ def pack_streams(convs: list[StreamCodes], union: torch.Tensor | None = None) ->
         tiles[:, 4] = group_base.to(torch.int32)
         tiles[:, 5] = (starts - conv_start).to(torch.int32)
     return PackedStream(code=code, tiles=tiles, groups=desc, aux=aux, union=union, seq_tiles=seq_tiles,
-                        seq_tokens=seq_tokens, present=present.cpu(), tile_blocks=blocks_per_tile.cpu())
+                        seq_tokens=seq_tokens, present=present.cpu(), tile_blocks=blocks_per_tile.cpu(),
+                        max_planes=int(max_planes.max()) if max_planes.numel() else 0)

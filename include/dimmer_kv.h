@@ -96,6 +96,8 @@ typedef struct dkv_attend_args {
   void* out;                     /* [n_seq][q_len][n_q_heads][head_dim], bf16 or fp32 */
   int32_t out_f32;               /* 1: fp32 output (parity checks), 0: bf16 (the cache dtype) */
   int* status;                   /* device int32 */
+  int32_t k_max_planes;          /* largest plane count of any key block (16 = raw blocks present) */
+  int32_t v_max_planes;          /* the same for the value stream */
 } dkv_attend_args;
 
 /* One attention layer, all four stages below in order.
