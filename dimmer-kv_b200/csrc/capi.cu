@@ -170,6 +170,9 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
   p.groups = reinterpret_cast<const GroupDesc*>(a->v_groups);
   p.tok_sidx = a->v_sidx;
   p.items = a->v_items;
+  p.item_ranges = a->v_item_ranges;
+  p.tile_chunk = a->v_tile_chunk;
+  p.max_planes = a->v_max_planes;
   p.n_items = a->n_v_items;
   p.item_groups = a->v_item_groups;
   p.scores = a->scores;

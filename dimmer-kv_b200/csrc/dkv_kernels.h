@@ -68,8 +68,11 @@ struct ValueWeightParams {
   const GroupDesc* groups;
   const int32_t* tok_sidx;        // value token -> index in its conversation's score order
   const int32_t* items;           // [n_items][4]: seq, tile_begin, tile_end, first union group
+  const int32_t* item_ranges;     // [n_items][tile_chunk][2]: descriptor range of each tile inside the item's groups
+  int tile_chunk;
   int n_items;
   int item_groups;                // union groups covered by one item (2 x pairs)
+  int max_planes;                 // largest plane count of any value block (> 8: raw blocks present)
   const float* scores;
   const int64_t* seq_score_off;
   const int32_t* seq_m;

@@ -14,6 +14,9 @@
 // The MMA warp accumulates D[128 components, rows] += C^T P^T with tcgen05 (M=128, N=rows,
 // K=16 tokens per instruction) into one TMEM column range per group pair. At the end of the
 // item the accumulators are written to `partial` (fp32), which finalize.cu reduces.
+// The producer copies each tile's descriptors (the host lists, per item and tile, the range of
+// descriptors inside the item's groups) into shared memory with one bulk copy; every role walks
+// the group pairs there, and the producer streams the code blocks into a ring of slots.
 #include "dkv_ptx.cuh"
 #include "dkv_format.cuh"
 #include "dkv_kernels.h"
@@ -22,62 +25,58 @@ namespace dkv {
 
 namespace {
 
-constexpr int kVThreads = 384;
-constexpr int kVCodeSlots = 4;
-constexpr int kVCodeSlot = 17408;
+constexpr int kVThreads = 384;  // producer, MMA, 2 idle, 8 workers (P build, decode; warps 4-7 also epilogue)
 constexpr int kPairTile = 32768;  // two groups x 128 tokens x 128 B
+constexpr int kMaxRangeGroups = 64;
 
-// Walks the groups of one tile that fall in [g0, g0 + ng): every role of the kernel uses the
-// same walk, so all agree on the sequence of code blocks and group pairs.
-struct PairWalk {
-  const GroupDesc* groups;
-  int base, count, g0, ng;
-  int gi;  // next group index (absolute)
-
-  __device__ __forceinline__ void begin(const TileDesc& t, const GroupDesc* all, int first_group, int n_groups) {
-    groups = all;
-    base = t.group_base;
-    count = t.n_groups;
-    g0 = first_group;
-    ng = n_groups;
-    gi = base;
-    while (gi < base + count && static_cast<int>(__ldg(&groups[gi].group)) < g0) ++gi;
-  }
-  // Next pair present in the tile: returns pair index or -1; sets descriptors of its halves.
-  __device__ __forceinline__ int next(int& lo_gi, int& hi_gi) {
-    lo_gi = hi_gi = -1;
-    if (gi >= base + count) return -1;
-    const int g = static_cast<int>(__ldg(&groups[gi].group));
-    if (g >= g0 + ng) return -1;
-    const int pair = (g - g0) >> 1;
-    if (((g - g0) & 1) == 0) {
-      lo_gi = gi++;
-      if (gi < base + count && static_cast<int>(__ldg(&groups[gi].group)) == g + 1) hi_gi = gi++;
-    } else {
-      hi_gi = gi++;
-    }
-    return pair;
-  }
+template <bool RAW>
+struct ValueSmem {
+  static constexpr int kCodeSlots = RAW ? 3 : 6;
+  static constexpr int kCodeSlot = RAW ? 17408 : 8960;
 };
+
+// Next group pair of a tile's descriptor list (in shared memory, sorted by union group).
+__device__ __forceinline__ int next_pair(const GroupDesc* d, int n, int g0, int& i, int& lo, int& hi) {
+  lo = hi = -1;
+  if (i >= n) return -1;
+  const int g = static_cast<int>(d[i].group);
+  const int pair = (g - g0) >> 1;
+  if (((g - g0) & 1) == 0) {
+    lo = i++;
+    if (i < n && static_cast<int>(d[i].group) == g + 1) hi = i++;
+  } else {
+    hi = i++;
+  }
+  return pair;
+}
 
 }  // namespace
 
+template <bool RAW>
 __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const ValueWeightParams p) {
+  using L = ValueSmem<RAW>;
+  constexpr int kCodeSlots = L::kCodeSlots;
+  constexpr int kCodeSlot = L::kCodeSlot;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int NR = p.n_rows_pad;            // MMA N (multiple of 16, <= 128)
-  const int p_tile = NR * 256;            // two K atoms of 64 tokens
-  uint8_t* a_tiles = smem;                                  // [2][kPairTile]
-  uint8_t* p_tiles = a_tiles + 2 * kPairTile;               // [2][p_tile]
-  uint8_t* c_slots = p_tiles + 2 * p_tile;                  // [kVCodeSlots][kVCodeSlot]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(c_slots + kVCodeSlots * kVCodeSlot);
+  const int NR = p.n_rows_pad;  // MMA N (multiple of 16, <= 128)
+  const int p_tile = NR * 256;  // two K atoms of 64 tokens
+  uint8_t* a_tiles = smem;                                    // [2][kPairTile]
+  uint8_t* p_tiles = a_tiles + 2 * kPairTile;                 // [2][p_tile]
+  GroupDesc* descs = reinterpret_cast<GroupDesc*>(p_tiles + 2 * p_tile);  // [2][kMaxRangeGroups]
+  float* stats_s = reinterpret_cast<float*>(descs + 2 * kMaxRangeGroups);  // [3][128][2] max, 1/sum
+  uint8_t* c_slots = reinterpret_cast<uint8_t*>(stats_s + 3 * 256);        // [kCodeSlots][kCodeSlot]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(c_slots + kCodeSlots * kCodeSlot);
   uint64_t* code_full = bars;
-  uint64_t* code_empty = code_full + kVCodeSlots;
-  uint64_t* a_full = code_empty + kVCodeSlots;    // [2]
-  uint64_t* a_empty = a_full + 2;                 // [2]
-  uint64_t* p_full = a_empty + 2;                 // [2]
-  uint64_t* p_empty = p_full + 2;                 // [2]
-  uint64_t* accum_full = p_empty + 2;
+  uint64_t* code_empty = code_full + kCodeSlots;
+  uint64_t* a_full = code_empty + kCodeSlots;  // [2]
+  uint64_t* a_empty = a_full + 2;              // [2]
+  uint64_t* p_full = a_empty + 2;              // [2]
+  uint64_t* p_empty = p_full + 2;              // [2]
+  uint64_t* d_full = p_empty + 2;              // [2]
+  uint64_t* d_empty = d_full + 2;              // [2]
+  uint64_t* stats_ready = d_empty + 2;         // [3]
+  uint64_t* accum_full = stats_ready + 3;
   uint64_t* accum_empty = accum_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -88,7 +87,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   const int n_pairs = p.item_groups / 2;
 
   if (tid == 0) {
-    for (int i = 0; i < kVCodeSlots; ++i) {
+    for (int i = 0; i < kCodeSlots; ++i) {
       mbar_init(&code_full[i], 1);
       mbar_init(&code_empty[i], 256);
     }
@@ -97,7 +96,10 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       mbar_init(&a_empty[i], 1);
       mbar_init(&p_full[i], 256);
       mbar_init(&p_empty[i], 1);
+      mbar_init(&d_full[i], 1);
+      mbar_init(&d_empty[i], 257);
     }
+    for (int i = 0; i < 3; ++i) mbar_init(&stats_ready[i], 256);
     mbar_init(accum_full, 1);
     mbar_init(accum_empty, 128);
     *abort_flag = 0;
@@ -109,47 +111,61 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer: code blocks
+    // ------------------------------------------------------------ producer: descriptors, code blocks
     if (lane == 0) {
-      uint32_t c_iter = 0;
+      uint32_t c_iter = 0, d_iter = 0;
       for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
-        const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
+        const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2];
         for (int t = tb; t < te && !*abort_flag; ++t) {
-          const TileDesc tile = p.tiles[t];
-          PairWalk walk;
-          walk.begin(tile, p.groups, g0, p.item_groups);
-          int lo, hi;
-          while (walk.next(lo, hi) >= 0) {
-            for (int half = 0; half < 2; ++half) {
-              const int gi = half ? hi : lo;
-              if (gi < 0) continue;
-              const GroupRegs gr = load_group(&p.groups[gi]);
-              if (gr.code_bytes > static_cast<uint32_t>(kVCodeSlot - 32) ||
-                  static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size) {
-                record_error(p.status, kErrBadDescriptor);
-                *abort_flag = 1;
-                break;
-              }
-              const int cs = c_iter % kVCodeSlots;
-              if (c_iter >= kVCodeSlots &&
-                  !mbar_wait(&code_empty[cs], ((c_iter / kVCodeSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
-                *abort_flag = 1;
-                break;
-              }
-              stash_group(c_slots + (cs + 1) * kVCodeSlot, &p.groups[gi]);
-              mbar_arrive_expect_tx(&code_full[cs], gr.code_bytes);
-              bulk_load(c_slots + cs * kVCodeSlot, p.code + gr.code_offset, gr.code_bytes, &code_full[cs]);
-              ++c_iter;
-            }
-            if (*abort_flag) break;
+          const int d0 = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
+          const int d1 = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1];
+          const int n = d1 - d0;
+          const int db = d_iter & 1;
+          if (n < 0 || n > kMaxRangeGroups) {
+            record_error(p.status, kErrBadDescriptor);
+            *abort_flag = 1;
+            break;
           }
+          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (n > 0) {
+            mbar_arrive_expect_tx(&d_full[db], n * 32);
+            bulk_load(descs + db * kMaxRangeGroups, p.groups + d0, n * 32, &d_full[db]);
+          } else {
+            mbar_arrive(&d_full[db]);
+          }
+          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
+            *abort_flag = 1;
+            break;
+          }
+          const GroupDesc* d = descs + db * kMaxRangeGroups;
+          for (int i = 0; i < n; ++i) {
+            const uint32_t off = d[i].code_offset, bytes = d[i].code_bytes;
+            if (bytes > static_cast<uint32_t>(kCodeSlot) || static_cast<uint64_t>(off) + bytes > p.code_size) {
+              record_error(p.status, kErrBadDescriptor);
+              *abort_flag = 1;
+              break;
+            }
+            const int cs = c_iter % kCodeSlots;
+            if (c_iter >= kCodeSlots &&
+                !mbar_wait(&code_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&code_full[cs], bytes);
+            bulk_load(c_slots + cs * kCodeSlot, p.code + off, bytes, &code_full[cs]);
+            ++c_iter;
+          }
+          ++d_iter;
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t a_iter = 0, p_iter = 0, item_iter = 0;
+      uint32_t a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
       for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
         const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
         if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
@@ -160,16 +176,17 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         uint32_t started = 0;  // pairs whose accumulator has been initialised in this item
         bool ok = true;
         for (int t = tb; t < te && ok; ++t) {
-          const TileDesc tile = p.tiles[t];
-          const int pb = p_iter & 1;
-          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA)) {
+          const int pb = p_iter & 1, db = d_iter & 1;
+          const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
+                        p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
+          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA) ||
+              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
             ok = false;
             break;
           }
-          PairWalk walk;
-          walk.begin(tile, p.groups, g0, p.item_groups);
-          int lo, hi, pair;
-          while ((pair = walk.next(lo, hi)) >= 0) {
+          const GroupDesc* d = descs + db * kMaxRangeGroups;
+          int i = 0, lo, hi, pair;
+          while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
             const int slot = a_iter & 1;
             if (!mbar_wait(&a_full[slot], (a_iter >> 1) & 1, p.status, kErrWaitA)) {
               ok = false;
@@ -179,10 +196,10 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             const uint32_t a_base = smem_u32(a_tiles + slot * kPairTile);
             const uint32_t p_base = smem_u32(p_tiles + pb * p_tile);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const uint64_t adesc = smem_desc_sw128(a_base + i * 2048, 16384, 1024);
-              const uint64_t bdesc = smem_desc_sw128(p_base + (i >> 2) * (NR * 128) + (i & 3) * 32, 16, 1024);
-              const uint32_t acc = ((started >> pair) & 1u) || i > 0 ? 1u : 0u;
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t adesc = smem_desc_sw128(a_base + k * 2048, 16384, 1024);
+              const uint64_t bdesc = smem_desc_sw128(p_base + (k >> 2) * (NR * 128) + (k & 3) * 32, 16, 1024);
+              const uint32_t acc = ((started >> pair) & 1u) || k > 0 ? 1u : 0u;
               mma_f16(tmem + pair * NR, adesc, bdesc, idesc, acc);
             }
             started |= 1u << pair;
@@ -191,7 +208,9 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           }
           if (!ok) break;
           mma_commit(&p_empty[pb]);
+          mbar_arrive(&d_empty[db]);
           ++p_iter;
+          ++d_iter;
         }
         if (!ok) {
           *abort_flag = 1;
@@ -206,16 +225,34 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
     const int u = tid - 128;
     const int r = u & 127;  // token row (decode) / token column (P)
     const int h = u >> 7;   // component half (decode) / row half (P)
-    uint32_t c_iter = 0, a_iter = 0, p_iter = 0, item_iter = 0;
+    uint32_t c_iter = 0, a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
     for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
       const int s = p.items[4 * it], tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
       const int64_t m_s = p.seq_m[s];
       const float* sc = p.scores + p.seq_score_off[s];
-      const float* stats = p.row_stats + static_cast<int64_t>(s) * p.n_q_heads * p.q_len * 4;
+      // Softmax statistics of the item's rows, staged once per item in one of three buffers: a worker
+      // can be at most two items ahead of the slowest one (each P tile waits for the MMA of the tile
+      // two before it, which waits for every worker), so three buffers never collide.
+      float* st_s = stats_s + (item_iter % 3) * 256;
+      if (u < NR) {
+        float mx = 0.f, inv = 0.f;
+        if (u < p.n_rows) {
+          const float* st = p.row_stats + (static_cast<int64_t>(s) * p.n_q_heads * p.q_len + p.row_begin + u) * 4;
+          mx = st[0];
+          inv = st[1];
+        }
+        st_s[2 * u] = mx;
+        st_s[2 * u + 1] = inv;
+      }
+      mbar_arrive(&stats_ready[item_iter % 3]);
+      if (!mbar_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kErrWaitA)) {
+        *abort_flag = 1;
+        break;
+      }
       uint32_t started = 0;
       for (int t = tb; t < te && !*abort_flag; ++t) {
         const TileDesc tile = p.tiles[t];
-        // ---- P^T tile: rows x 128 tokens, bf16
+        // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype)
         const int pb = p_iter & 1;
         if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
           *abort_flag = 1;
@@ -227,25 +264,36 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int sidx = tok_ok ? p.tok_sidx[tile.token_base + r] : 0;
           const int atom = r >> 6, chunk = (r & 63) >> 3, within = (r & 7) * 2;
           const int rows_half = NR / 2;
-          for (int n = h * rows_half; n < (h + 1) * rows_half; ++n) {
-            float prob = 0.f;
-            if (tok_ok && n < p.n_rows) {
-              const int row = p.row_begin + n;
-              const float x = sc[static_cast<int64_t>(row) * m_s + sidx];
-              prob = (x == -INFINITY) ? 0.f : expf(x - stats[row * 4]) * stats[row * 4 + 1];
+          for (int n0 = h * rows_half; n0 < (h + 1) * rows_half; n0 += 8) {
+            float x[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int n = n0 + k;
+              x[k] = (tok_ok && n < p.n_rows) ? sc[static_cast<int64_t>(p.row_begin + n) * m_s + sidx] : -INFINITY;
             }
-            *reinterpret_cast<__nv_bfloat16*>(pt + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
-                __float2bfloat16_rn(prob);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int n = n0 + k;
+              const float prob = (x[k] == -INFINITY) ? 0.f : expf(x[k] - st_s[2 * n]) * st_s[2 * n + 1];
+              *reinterpret_cast<__nv_bfloat16*>(pt + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
+                  __float2bfloat16_rn(prob);
+            }
           }
           fence_async_shared();
           mbar_arrive(&p_full[pb]);
           ++p_iter;
         }
         // ---- coefficient pairs
-        PairWalk walk;
-        walk.begin(tile, p.groups, g0, p.item_groups);
-        int lo, hi, pair;
-        while ((pair = walk.next(lo, hi)) >= 0) {
+        const int db = d_iter & 1;
+        const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
+                      p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
+        if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
+          *abort_flag = 1;
+          break;
+        }
+        const GroupDesc* d = descs + db * kMaxRangeGroups;
+        int i = 0, lo, hi, pair;
+        while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
           const int slot = a_iter & 1;
           if (a_iter >= 2 && !mbar_wait(&a_empty[slot], ((a_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
             *abort_flag = 1;
@@ -257,18 +305,19 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             uint8_t* dst = a + half * 16384;
             uint32_t out[16];
             if (gi >= 0) {
-              const int cs = c_iter % kVCodeSlots;
-              if (!mbar_wait(&code_full[cs], (c_iter / kVCodeSlots) & 1, p.status, kErrWaitCodes)) {
+              const int cs = c_iter % kCodeSlots;
+              if (!mbar_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kErrWaitCodes)) {
                 *abort_flag = 1;
                 break;
               }
-              const GroupRegs gr = stashed_group(c_slots + (cs + 1) * kVCodeSlot);
-              decode_half(c_slots + cs * kVCodeSlot, gr, tile.n_tokens, r, h, out);
+              const uint4* dw = reinterpret_cast<const uint4*>(d + gi);
+              const GroupRegs gr = group_from_words(dw[0], dw[1]);
+              decode_half(c_slots + cs * kCodeSlot, gr, tile.n_tokens, r, h, out);
               mbar_arrive(&code_empty[cs]);
               ++c_iter;
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) out[i] = 0u;
+              for (int k = 0; k < 16; ++k) out[k] = 0u;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -281,6 +330,8 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           ++a_iter;
           started |= 1u << pair;
         }
+        mbar_arrive(&d_empty[db]);
+        ++d_iter;
       }
       if (*abort_flag) break;
       // ---- epilogue (warps 4..7): TMEM -> partial sums
@@ -323,12 +374,21 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream) {
   if (p.n_rows_pad % 16 != 0 || p.n_rows_pad < 16 || p.n_rows_pad > 128 || p.n_rows > p.n_rows_pad)
     return kDkvErrConfig;
-  if ((p.item_groups / 2) * p.n_rows_pad > 512 || p.item_groups % 2 != 0 || p.item_groups > 64) return kDkvErrConfig;
+  if ((p.item_groups / 2) * p.n_rows_pad > 512 || p.item_groups % 2 != 0 || p.item_groups > kMaxRangeGroups)
+    return kDkvErrConfig;
   if (p.n_items == 0) return kDkvOk;
-  const int smem = 1024 + 2 * kPairTile + 2 * p.n_rows_pad * 256 + kVCodeSlots * kVCodeSlot + 32 * 8;
-  if (cudaFuncSetAttribute(value_weights_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return kDkvErrCuda;
-  value_weights_kernel<<<grid, kVThreads, smem, stream>>>(p);
+  const bool raw = p.max_planes > 8;
+  const int slots = raw ? ValueSmem<true>::kCodeSlots * ValueSmem<true>::kCodeSlot
+                        : ValueSmem<false>::kCodeSlots * ValueSmem<false>::kCodeSlot;
+  const int smem = 1024 + 2 * kPairTile + 2 * p.n_rows_pad * 256 + 2 * kMaxRangeGroups * 32 + 3 * 256 * 4 + slots + 40 * 8;
+  if (smem > 232448) return kDkvErrConfig;
+  cudaError_t e = raw ? cudaFuncSetAttribute(value_weights_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+                      : cudaFuncSetAttribute(value_weights_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return kDkvErrCuda;
+  if (raw)
+    value_weights_kernel<true><<<grid, kVThreads, smem, stream>>>(p);
+  else
+    value_weights_kernel<false><<<grid, kVThreads, smem, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

@@ -44,6 +44,7 @@ class AttendArgs(ctypes.Structure):
         ("rows_pad", c_int32), ("grid_k", c_int32), ("grid_v", c_int32),
         ("out", c_void_p), ("out_f32", c_int32), ("status", c_void_p),
         ("k_max_planes", c_int32), ("v_max_planes", c_int32),
+        ("v_item_ranges", c_void_p), ("v_tile_chunk", c_int32),
     ]
 
 

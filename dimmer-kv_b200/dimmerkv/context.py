@@ -143,12 +143,19 @@ class CompressedBatch:
         return m.to(self.dtype).reshape(-1, self.layers, self.n_cols).contiguous(), self.layers * self.n_cols
 
     def value_items(self, rows_pad: int):
-        """Value work items for an MMA width: (items [n, 4], seq ranges [n_seq, 2], groups per item)."""
+        """Value work items for an MMA width: (items [n, 4], seq ranges [n_seq, 2], groups per item, n,
+        descriptor ranges [n, tile_chunk, 2]). An item is (conversation, run of <= tile_chunk value tiles,
+        first union group); for each of its tiles the descriptor range covering the item's groups."""
         if rows_pad in self._v_items_cache:
             return self._v_items_cache[rows_pad]
         item_groups = min(64, 2 * (512 // rows_pad))
         present = self.values.present
-        rows, ranges = [], []
+        gu = int(present.shape[1]) if present is not None and present.dim() == 2 else 0
+        prefix = torch.zeros(present.shape[0], gu + 1, dtype=torch.int64)
+        if gu:
+            prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
+        group_base = self.values.tiles[:, 4].to(torch.int64).cpu()
+        rows, ranges, spans = [], [], []
         for s, (t0, t1) in enumerate(self.values.seq_tiles):
             first = len(rows)
             for c0 in range(t0, t1, self.tile_chunk):
@@ -157,10 +164,17 @@ class CompressedBatch:
                 for g0 in range(0, int(used.numel()), item_groups):
                     if bool(used[g0 : g0 + item_groups].any()):
                         rows.append((s, c0, c1, g0))
+                        g1 = min(g0 + item_groups, gu)
+                        t = torch.arange(c0, c1)
+                        span = torch.zeros(self.tile_chunk, 2, dtype=torch.int64)
+                        span[: c1 - c0, 0] = group_base[t] + prefix[t, g0]
+                        span[: c1 - c0, 1] = group_base[t] + prefix[t, g1]
+                        spans.append(span)
             ranges.append((first, len(rows)))
         items = torch.tensor(rows if rows else [(0, 0, 0, 0)], dtype=torch.int32)[: len(rows)]
+        span_t = torch.stack(spans) if spans else torch.zeros(1, self.tile_chunk, 2, dtype=torch.int64)
         out = (items.to(self.device).contiguous(), torch.tensor(ranges, dtype=torch.int32).to(self.device),
-               item_groups, len(rows))
+               item_groups, len(rows), span_t.to(torch.int32).to(self.device).contiguous())
         self._v_items_cache[rows_pad] = out
         return out
 
@@ -188,7 +202,7 @@ class CompressedBatch:
         q_len = query.shape[2]
         n_exact = key.shape[2]
         rows_pad = min(128, _round_up(self.q_heads * q_len, 16))
-        v_items, v_seq, item_groups, n_v = self.value_items(rows_pad)
+        v_items, v_seq, item_groups, n_v, v_spans = self.value_items(rows_pad)
         w = self._workspace(q_len, n_exact, rows_pad, n_v, item_groups)
         a = _lib.AttendArgs()
         ks, vs = self.keys, self.values
@@ -214,6 +228,7 @@ class CompressedBatch:
         a.rows_pad, a.grid_k, a.grid_v = rows_pad, 0, 0
         a.out, a.out_f32, a.status = out.data_ptr(), int(out.dtype == torch.float32), self.status.data_ptr()
         a.k_max_planes, a.v_max_planes = ks.max_planes, vs.max_planes
+        a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
         return a
 
     def attend_layer(self, layer: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,

@@ -98,6 +98,8 @@ typedef struct dkv_attend_args {
   int* status;                   /* device int32 */
   int32_t k_max_planes;          /* largest plane count of any key block (16 = raw blocks present) */
   int32_t v_max_planes;          /* the same for the value stream */
+  const int32_t* v_item_ranges;  /* [n_v_items][v_tile_chunk][2]: per tile, the descriptor range inside the item's groups */
+  int32_t v_tile_chunk;          /* value tiles per item (at most) */
 } dkv_attend_args;
 
 /* One attention layer, all four stages below in order.
