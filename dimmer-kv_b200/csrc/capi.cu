@@ -257,6 +257,57 @@ int dkv_attend_layer(const dkv_attend_args* a, void* stream) {
   return DKV_OK;
 }
 
+int dkv_importance(const dkv_importance_args* a, void* stream) {
+  if (a == nullptr || a->scores == nullptr || a->imp_compressed == nullptr) return DKV_ERR_ARGS;
+  dkv::ImportanceParams p{};
+  p.scores = a->scores;
+  p.seq_score_off = a->seq_score_off;
+  p.seq_m = a->seq_m;
+  p.seq_k_base = a->seq_k_base;
+  p.row_stats = a->row_stats;
+  p.p_exact = a->p_exact;
+  p.n_seq = a->n_seq;
+  p.n_q_heads = a->n_q_heads;
+  p.q_len = a->q_len;
+  p.n_exact = a->n_exact;
+  p.imp_compressed = a->imp_compressed;
+  p.imp_exact = a->imp_exact;
+  return dkv::run_importance(p, a->max_m, static_cast<cudaStream_t>(stream));
+}
+
+int dkv_topk(const dkv_topk_args* a, void* stream) {
+  if (a == nullptr || a->importance == nullptr || a->positions == nullptr || a->out == nullptr) return DKV_ERR_ARGS;
+  dkv::TopkParams p{};
+  p.importance = a->importance;
+  p.positions = a->positions;
+  p.seq_k_base = a->seq_k_base;
+  p.seq_m = a->seq_m;
+  p.counts = a->counts;
+  p.out_offset = a->out_offset;
+  p.n_seq = a->n_seq;
+  p.out = a->out;
+  p.status = a->status;
+  return dkv::run_topk(p, a->max_k, static_cast<cudaStream_t>(stream));
+}
+
+int dkv_refine_merge(const dkv_refine_args* a, void* stream) {
+  if (a == nullptr || a->hot_code == nullptr || a->out_code == nullptr) return DKV_ERR_ARGS;
+  dkv::RefineParams p{};
+  p.hot_code = a->hot_code;
+  p.hot_tiles = reinterpret_cast<const TileDesc*>(a->hot_tiles);
+  p.hot_groups = reinterpret_cast<const GroupDesc*>(a->hot_groups);
+  p.hot_tile = a->hot_tile;
+  p.hot_row = a->hot_row;
+  p.cold_words = a->cold_words;
+  p.cold_headers = a->cold_headers;
+  p.n_selected = a->n_selected;
+  p.n_groups = a->n_groups;
+  p.out_groups = reinterpret_cast<const GroupDesc*>(a->out_groups);
+  p.out_code = a->out_code;
+  p.status = a->status;
+  return dkv::run_refine(p, static_cast<cudaStream_t>(stream));
+}
+
 int dkv_unpack(const dkv_unpack_args* a, void* stream) {
   if (a == nullptr || a->code == nullptr || a->tiles == nullptr || a->groups == nullptr || a->out == nullptr)
     return DKV_ERR_ARGS;

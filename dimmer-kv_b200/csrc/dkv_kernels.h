@@ -56,7 +56,7 @@ struct SoftmaxParams {
   int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact;
   float scaling;
   float* row_stats;               // [n_seq][n_q_heads][q_len][4]: max, 1/sum, compressed mass, 0
-  float* p_exact;                 // [n_seq][n_q_heads][q_len][n_exact]
+  float* p_exact;                 // [n_seq][n_q_heads][q_len][n_exact], fp32 (unrounded)
 };
 int run_softmax_stats(const SoftmaxParams& p, cudaStream_t stream);
 
@@ -116,5 +116,47 @@ struct UnpackParams {
   int* status;
 };
 int run_unpack(const UnpackParams& p, cudaStream_t stream);
+
+// Question-time scoring, selection and refinement (question.cu).
+struct ImportanceParams {
+  const float* scores;
+  const int64_t* seq_score_off;
+  const int32_t* seq_m;
+  const int32_t* seq_k_base;      // first importance slot of each conversation
+  const float* row_stats;
+  const float* p_exact;
+  int n_seq, n_q_heads, q_len, n_exact;
+  float* imp_compressed;          // [sum of seq_m], one slot per score (score order), accumulated
+  float* imp_exact;               // [n_seq][n_exact], accumulated
+};
+int run_importance(const ImportanceParams& p, int max_m, cudaStream_t stream);
+
+struct TopkParams {
+  const float* importance;        // [sum of seq_m] slots, score order
+  const int32_t* positions;       // position of every slot, < 0 = not selectable
+  const int32_t* seq_k_base;
+  const int32_t* seq_m;
+  const int32_t* counts;          // [n_seq] tokens to select
+  const int32_t* out_offset;      // [n_seq]
+  int n_seq;
+  int32_t* out;                   // selected positions, ascending per conversation
+  int* status;
+};
+int run_topk(const TopkParams& p, int max_k, cudaStream_t stream);
+
+struct RefineParams {
+  const uint8_t* hot_code;
+  const TileDesc* hot_tiles;
+  const GroupDesc* hot_groups;
+  const int32_t* hot_tile;        // [n_selected] hot tile of each selected token
+  const int32_t* hot_row;         // [n_selected] its row in that tile
+  const uint64_t* cold_words;     // [n_selected][n_groups][8] plane words of the full codes
+  const uint32_t* cold_headers;   // [n_selected][n_groups] f16 low | f16 mult << 16
+  int n_selected, n_groups;
+  const GroupDesc* out_groups;    // [ceil(n_selected / 128)][n_groups] refined block descriptors
+  uint8_t* out_code;
+  int* status;
+};
+int run_refine(const RefineParams& p, cudaStream_t stream);
 
 }  // namespace dkv

@@ -92,7 +92,10 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const Finali
         const int64_t srow = (static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi;
         o += mean * p.row_stats[srow * 4 + 2];
         const float* pe = p.p_exact + srow * p.n_exact;
-        for (int e = 0; e < p.n_exact; ++e) o += pe[e] * __bfloat162float(vex[static_cast<int64_t>(e) * D]);
+        // Exact probabilities are kept unrounded (question-time scoring sums them); the value product uses
+        // them rounded to the cache dtype, as the reference does (compressed_attention.py:128, 135).
+        for (int e = 0; e < p.n_exact; ++e)
+          o += __bfloat162float(__float2bfloat16_rn(pe[e])) * __bfloat162float(vex[static_cast<int64_t>(e) * D]);
         const int64_t oi = ((static_cast<int64_t>(s) * p.q_len + qi) * p.n_q_heads + hq) * D + d;
         if (p.out_f32)
           static_cast<float*>(p.out)[oi] = o;

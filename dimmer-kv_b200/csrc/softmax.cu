@@ -105,10 +105,11 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const So
   __syncthreads();
   const float mx = red_m[0], inv = red_l[0];
   // The reference casts the probabilities to the cache dtype before the value products
-  // (compressed_attention.py:127-128, 130): exact probabilities and the compressed mass used by
-  // the mean term are sums of bf16-rounded probabilities here too.
+  // (compressed_attention.py:127-128, 130): the compressed mass used by the mean term is a sum of
+  // bf16-rounded probabilities. Exact probabilities are stored in fp32 (the finalize kernel rounds
+  // them at use; question-time scoring sums them unrounded, as dimmer.py:64-66 does).
   for (int e = tid; e < p.n_exact; e += blockDim.x)
-    p.p_exact[static_cast<int64_t>(row) * p.n_exact + e] = bf16_round(expf(se[e] - mx) * inv);
+    p.p_exact[static_cast<int64_t>(row) * p.n_exact + e] = expf(se[e] - mx) * inv;
   float mass = 0.f;
   for (int64_t n = tid; n < m_s; n += blockDim.x) {
     const float x = sc[n];

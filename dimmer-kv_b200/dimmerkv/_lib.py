@@ -21,7 +21,8 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
                  107: "timed out draining async work", 110: "descriptor out of bounds"}
 
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
-           "dkv_unpack", "dkv_version", "dkv_status_string")
+           "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
+           "dkv_version", "dkv_status_string")
 
 
 class AttendArgs(ctypes.Structure):
@@ -57,6 +58,37 @@ class UnpackArgs(ctypes.Structure):
     ]
 
 
+class ImportanceArgs(ctypes.Structure):
+    """Mirror of ``dkv_importance_args``."""
+
+    _fields_ = [
+        ("scores", c_void_p), ("seq_score_off", c_void_p), ("seq_m", c_void_p), ("seq_k_base", c_void_p),
+        ("row_stats", c_void_p), ("p_exact", c_void_p), ("n_seq", c_int32), ("n_q_heads", c_int32),
+        ("q_len", c_int32), ("n_exact", c_int32), ("max_m", c_int32), ("imp_compressed", c_void_p),
+        ("imp_exact", c_void_p),
+    ]
+
+
+class TopkArgs(ctypes.Structure):
+    """Mirror of ``dkv_topk_args``."""
+
+    _fields_ = [
+        ("importance", c_void_p), ("positions", c_void_p), ("seq_k_base", c_void_p), ("seq_m", c_void_p),
+        ("counts", c_void_p), ("out_offset", c_void_p), ("n_seq", c_int32), ("max_k", c_int32), ("out", c_void_p),
+        ("status", c_void_p),
+    ]
+
+
+class RefineArgs(ctypes.Structure):
+    """Mirror of ``dkv_refine_args``."""
+
+    _fields_ = [
+        ("hot_code", c_void_p), ("hot_tiles", c_void_p), ("hot_groups", c_void_p), ("hot_tile", c_void_p),
+        ("hot_row", c_void_p), ("cold_words", c_void_p), ("cold_headers", c_void_p), ("n_selected", c_int32),
+        ("n_groups", c_int32), ("out_groups", c_void_p), ("out_code", c_void_p), ("status", c_void_p),
+    ]
+
+
 _LIB = None
 
 
@@ -78,6 +110,10 @@ def lib():
             fn.restype = c_int32
         handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
         handle.dkv_unpack.restype = c_int32
+        for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs)):
+            fn = getattr(handle, name)
+            fn.argtypes = [ctypes.POINTER(st), c_void_p]
+            fn.restype = c_int32
         handle.dkv_version.argtypes = []
         handle.dkv_version.restype = c_int32
         handle.dkv_status_string.argtypes = [c_int32]

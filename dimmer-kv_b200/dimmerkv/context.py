@@ -46,8 +46,8 @@ def _stable_order(rung: torch.Tensor, kept: torch.Tensor) -> torch.Tensor:
     return idx[order]
 
 
-def conversation_streams(conv: ConversationCodes) -> tuple[StreamCodes, StreamCodes, torch.Tensor]:
-    """(key stream, value stream, key order) of one conversation in the reference's token order."""
+def conversation_streams(conv: ConversationCodes) -> tuple[StreamCodes, StreamCodes, torch.Tensor, torch.Tensor]:
+    """(key stream, value stream, key order, value order) of one conversation in the reference's token order."""
     k, v = conv.key, conv.value
     kept_k = k.rung >= 0
     kept_v = (v.rung >= 0) & kept_k
@@ -59,8 +59,29 @@ def conversation_streams(conv: ConversationCodes) -> tuple[StreamCodes, StreamCo
                              aux=(conv.start + order_k).to(torch.int32), kind=k.kind)
     value_stream = StreamCodes(planes=v.planes[order_v], index=v.index[order_v], header=v.header[order_v],
                                aux=position[order_v].to(torch.int32), kind=v.kind)
-    return key_stream, value_stream, order_k
+    return key_stream, value_stream, order_k, order_v
 
+
+@dataclass
+class ColdTier:
+    """Full-precision planes of every middle token of one stream of one conversation, kept in pinned host
+    memory (the progressive codec's cold tier, scripts/progressive.py:15-19, already inflated): for each
+    union group of the batch's stream, the 8 plane words of the token's 8-bit code and its header."""
+
+    words: torch.Tensor    # int64 [M, Gu, 8], pinned
+    headers: torch.Tensor  # int32 [M, Gu], pinned
+    hot_planes: torch.Tensor | None = None  # uint8 [M, Gu]: planes already in the hot tier (for byte counts)
+
+
+def plane_words(codes: torch.Tensor) -> torch.Tensor:
+    """uint8 codes [N, G, 64] -> int64 [N, G, 8]: plane j holds bit (7 - j) of every component."""
+    n, g, _ = codes.shape
+    weights = (2 ** torch.arange(8, device=codes.device, dtype=torch.int32)).to(torch.int32)
+    out = torch.empty(n, g, 8, dtype=torch.int64, device=codes.device)
+    for j in range(8):
+        bits = ((codes.to(torch.int32) >> (7 - j)) & 1).view(n, g, 8, 8)
+        out[:, :, j] = (bits * weights).sum(dim=-1).to(torch.uint8).contiguous().view(torch.int64).view(n, g)
+    return out
 
 def rope_tables(model, tokens: int, device, dtype=torch.bfloat16) -> tuple[torch.Tensor, torch.Tensor]:
     """cos, sin [tokens, head_dim // 2] from the model's own rotary embedding (kvtc.py:32-37),
@@ -81,10 +102,12 @@ class CompressedBatch:
 
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
-                 device=None, dtype=torch.bfloat16, tile_chunk: int = 16):
+                 device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None):
         """``basis[kind]``: [F, F] (or [F, >= union]) float basis, columns = PCA components (the codec's
         ``stream.basis``); ``mean[kind]``: [F] shared or [n_conv, F] per conversation; ``cos/sin``:
-        [positions, head_dim // 2] tables (``rope_tables``)."""
+        [positions, head_dim // 2] tables (``rope_tables``); ``union[kind]`` (optional) fixes the coefficient
+        groups a stream covers (by default, the groups holding a plane for some token; a cold tier whose
+        refined tokens use more groups needs them all)."""
         if dtype != torch.bfloat16:
             raise NotImplementedError("the sm_100a kernels of this build compute in bf16 only")
         self.lib = _lib.lib()
@@ -98,8 +121,10 @@ class CompressedBatch:
 
         streams = [conversation_streams(c) for c in conversations]
         self.key_orders = [s[2] for s in streams]
-        self.keys: PackedStream = pack_streams([s[0] for s in streams])
-        self.values: PackedStream = pack_streams([s[1] for s in streams])
+        self.value_orders = [s[3] for s in streams]
+        union = union or {}
+        self.keys: PackedStream = pack_streams([s[0] for s in streams], union.get("key"))
+        self.values: PackedStream = pack_streams([s[1] for s in streams], union.get("value"))
         self.seq_m = torch.tensor([e - b for b, e in self.keys.seq_tokens], dtype=torch.int32, device=self.device)
 
         # Bases restricted to the union components, in the layouts the kernels read.
@@ -134,6 +159,22 @@ class CompressedBatch:
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.timer = None  # optional callable(kind, fn) wrapping launches (used by the bench)
+        self.scoring = False
+        self.imp_compressed = None
+        self.imp_exact = None
+        self.extra_value_tiles: list = []  # (seq, first tile, end tile) appended by refine
+        self.refined_tokens = [0] * self.n_seq
+        self._refined_key_tokens: list = []  # (seq, first stream token, end) appended by refine
+        self._refined_pos = [torch.zeros(0, dtype=torch.int64) for _ in range(self.n_seq)]
+        self._score_cache = None
+
+    def _rebuild_key_items(self):
+        nblocks = self.n_cols // self.k_block
+        cost = self.keys.tile_blocks.repeat_interleave(nblocks) if self.keys.n_tiles else torch.zeros(0)
+        items = torch.arange(self.keys.n_tiles * nblocks, dtype=torch.int64)
+        if items.numel():
+            items = items[torch.sort(cost, descending=True, stable=True).indices]
+        self.k_items = items.to(torch.int32).to(self.device)
 
     # ------------------------------------------------------------------ set-up helpers
     def _means(self, mean: torch.Tensor):
@@ -156,8 +197,12 @@ class CompressedBatch:
             prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
         group_base = self.values.tiles[:, 4].to(torch.int64).cpu()
         rows, ranges, spans = [], [], []
-        for s, (t0, t1) in enumerate(self.values.seq_tiles):
-            first = len(rows)
+        tile_ranges = [[(t0, t1)] for t0, t1 in self.values.seq_tiles]
+        for s, t0, t1 in self.extra_value_tiles:
+            tile_ranges[s].append((t0, t1))
+        for s, seq_ranges in enumerate(tile_ranges):
+          first = len(rows)
+          for t0, t1 in seq_ranges:
             for c0 in range(t0, t1, self.tile_chunk):
                 c1 = min(t1, c0 + self.tile_chunk)
                 used = present[c0:c1].any(dim=0) if c1 > c0 else torch.zeros(0, dtype=torch.bool)
@@ -170,7 +215,7 @@ class CompressedBatch:
                         span[: c1 - c0, 0] = group_base[t] + prefix[t, g0]
                         span[: c1 - c0, 1] = group_base[t] + prefix[t, g1]
                         spans.append(span)
-            ranges.append((first, len(rows)))
+          ranges.append((first, len(rows)))
         items = torch.tensor(rows if rows else [(0, 0, 0, 0)], dtype=torch.int32)[: len(rows)]
         span_t = torch.stack(spans) if spans else torch.zeros(1, self.tile_chunk, 2, dtype=torch.int64)
         out = (items.to(self.device).contiguous(), torch.tensor(ranges, dtype=torch.int32).to(self.device),
@@ -253,6 +298,8 @@ class CompressedBatch:
                        args, stream)
         else:
             _lib.check(self.lib.dkv_attend_layer(args, stream), "dkv_attend_layer")
+        if self.scoring:
+            self._accumulate_importance(args, stream)
         self._keep = (query, key, value, mask, out, args)  # alive until the kernels have read them
         return out
 
@@ -262,6 +309,231 @@ class CompressedBatch:
 
     def check_status(self) -> None:
         _lib.check_device_status(self.status)
+
+    # ------------------------------------------------------------------ question time
+    def begin_scoring(self) -> None:
+        """Accumulate, during the next forward passes, the attention every context token receives
+        (question_importance, scripts/progressive.py:239-254)."""
+        self.scoring = True
+        _, _, pos = self._score_layout()
+        self.imp_compressed = torch.zeros(max(1, pos.numel()), dtype=torch.float32, device=self.device)
+        self.imp_exact = None
+
+    def end_scoring(self):
+        self.scoring = False
+        return self.imp_compressed, self.imp_exact
+
+    def _score_layout(self):
+        """Per conversation, its compressed tokens in score order (the hot stream's tokens, then the tokens
+        refined so far): (first slot per conversation on the device, the same on the host, the RoPE position
+        of every slot on the device, -1 for hidden hot copies). Importance is accumulated per slot."""
+        if self._score_cache is None:
+            m = self.seq_m.cpu().to(torch.int64)
+            base = torch.cumsum(m, 0) - m
+            parts = []
+            for s, (k0, k1) in enumerate(self.keys.seq_tokens):
+                parts.append(self.keys.aux[k0:k1])
+                parts.extend(self.keys.aux[t0:t1] for t0, t1 in self._refined_ranges(s))
+            pos = torch.cat(parts) if parts else torch.zeros(0, dtype=torch.int32, device=self.device)
+            self._score_cache = (base.to(torch.int32).to(self.device), base, pos.to(torch.int32).contiguous())
+        return self._score_cache
+
+    def _accumulate_importance(self, args, stream) -> None:
+        n_exact = int(args.n_exact)
+        if self.imp_exact is None or self.imp_exact.shape[1] != n_exact:
+            self.imp_exact = torch.zeros(self.n_seq, n_exact, dtype=torch.float32, device=self.device)
+        base, _, _ = self._score_layout()
+        a = _lib.ImportanceArgs(args.scores, args.seq_score_off, args.seq_m, base.data_ptr(), args.row_stats,
+                                args.p_exact, self.n_seq, self.q_heads, int(args.q_len), n_exact,
+                                int(self.seq_m.max()) if self.n_seq else 0, self.imp_compressed.data_ptr(),
+                                self.imp_exact.data_ptr())
+        _lib.check(self.lib.dkv_importance(a, stream), "dkv_importance")
+
+    def importance_by_position(self, s: int, context_length: int) -> torch.Tensor:
+        """Importance of conversation ``s`` over positions [0, context_length): compressed tokens by their
+        RoPE position, exact context tokens (sinks, then the recent window) by theirs."""
+        start, end = self.spans[s]
+        out = torch.zeros(context_length, dtype=torch.float32, device=self.device)
+        _, base_h, score_pos = self._score_layout()
+        b, m = int(base_h[s]), int(self.seq_m[s])
+        pos = score_pos[b:b + m].to(torch.int64)
+        keep = (pos >= 0) & (pos < context_length)
+        out.index_add_(0, pos[keep], self.imp_compressed[b:b + m][keep])
+        if self.imp_exact is not None:
+            exact_pos = torch.cat([torch.arange(start), torch.arange(end, context_length)]).to(self.device)
+            n = min(exact_pos.numel(), self.imp_exact.shape[1])
+            out.index_add_(0, exact_pos[:n], self.imp_exact[s, :n])
+        return out
+
+    def _refined_ranges(self, s: int):
+        return [(b, e) for (ss, b, e) in self._refined_key_tokens if ss == s]
+
+    def select_top(self, counts: list[int]) -> list[torch.Tensor]:
+        """Top ``counts[s]`` compressed tokens of every conversation by the accumulated importance (ties by
+        lowest position); returns their positions, ascending (methods.py:246-247)."""
+        if self.imp_compressed is None:
+            raise RuntimeError("select_top needs the importance of a scored forward (begin_scoring)")
+        base, _, score_pos = self._score_layout()
+        counts_t = torch.tensor(counts, dtype=torch.int32)
+        if bool((counts_t > self.seq_m.cpu()).any()):
+            raise ValueError("a count exceeds the conversation's compressed tokens")
+        offsets = (torch.cumsum(counts_t, 0) - counts_t).to(torch.int32)  # the kernel reads int32
+        out = torch.zeros(max(1, int(counts_t.sum())), dtype=torch.int32, device=self.device)
+        counts_d, offsets_d = counts_t.to(self.device), offsets.to(self.device)
+        a = _lib.TopkArgs(self.imp_compressed.data_ptr(), score_pos.data_ptr(), base.data_ptr(),
+                          self.seq_m.data_ptr(), counts_d.data_ptr(), offsets_d.data_ptr(), self.n_seq,
+                          max(counts) if counts else 0, out.data_ptr(), self.status.data_ptr())
+        _lib.check(self.lib.dkv_topk(a, torch.cuda.current_stream(self.device).cuda_stream), "dkv_topk")
+        result = out.cpu()  # synchronises: counts_d / offsets_d stay alive until the kernel is done
+        self.check_status()
+        return [result[int(o): int(o) + int(c)].to(torch.int64) for o, c in zip(offsets, counts_t)]
+
+    def refine(self, selected: list[torch.Tensor], cold: list[dict], side_stream=None) -> int:
+        """Merge the cold planes of the ``selected`` positions of every conversation into the batch: the
+        tokens are hidden in the hot tier and appended as full-precision (8-plane) tiles
+        (ProgressiveCache.refine, scripts/progressive.py:224-236). ``cold[s][kind]`` is the conversation's
+        ColdTier. Returns the bytes fetched from the cold tier under the reference's accounting."""
+        if len(selected) != self.n_seq or len(cold) != self.n_seq:
+            raise ValueError("refine needs one selection and one cold tier per conversation")
+        for s, sel in enumerate(selected):
+            start, end = self.spans[s]
+            sel_h = sel.to(torch.int64).cpu()
+            if bool(((sel_h < start) | (sel_h >= end)).any()):
+                raise ValueError(f"conversation {s}: a selected position is outside the compressed span")
+            if sel_h.unique().numel() != sel_h.numel() or bool(torch.isin(sel_h, self._refined_pos[s]).any()):
+                raise ValueError(f"conversation {s}: a selected position is repeated or already refined")
+        fetched = 0
+        stream = side_stream or torch.cuda.Stream(self.device)
+        main = torch.cuda.current_stream(self.device)
+        for kind in ("key", "value"):
+            packed = self.keys if kind == "key" else self.values
+            orders = self.key_orders if kind == "key" else self.value_orders
+            gu = int(packed.union.numel())
+            hot_tile, hot_row, words, headers, aux, per_seq = [], [], [], [], [], []
+            for s, sel in enumerate(selected):
+                if sel.numel() == 0:
+                    per_seq.append(0)
+                    continue
+                start, _ = self.spans[s]
+                mid = (sel.to(torch.int64) - start).cpu()
+                order = orders[s].cpu()
+                inverse = torch.full((int(order.max()) + 1 if order.numel() else 0,), -1, dtype=torch.int64)
+                inverse[order] = torch.arange(order.numel())
+                local = inverse[mid]
+                if bool((local < 0).any()):
+                    raise ValueError("a selected token is not in the compressed stream")
+                t0 = packed.seq_tiles[s][0]
+                hot_tile.append(t0 + local // 128)
+                hot_row.append(local % 128)
+                ct = cold[s][kind]
+                staging = torch.empty(mid.numel(), gu, 8, dtype=torch.int64).pin_memory()
+                torch.index_select(ct.words, 0, mid, out=staging)
+                hstage = torch.empty(mid.numel(), gu, dtype=torch.int32).pin_memory()
+                torch.index_select(ct.headers, 0, mid, out=hstage)
+                words.append(staging)
+                headers.append(hstage)
+                if ct.hot_planes is not None:
+                    hp = ct.hot_planes[mid].to(torch.int64)
+                    fetched += int(((8 - hp) * 8 + 4 * (hp == 0)).sum())
+                if kind == "key":
+                    aux.append(sel.to(torch.int32))
+                else:
+                    base = int(self.seq_m[s]) + 0
+                    aux.append(torch.arange(base, base + mid.numel(), dtype=torch.int32))
+                per_seq.append(mid.numel())
+            n_sel = sum(per_seq)
+            if n_sel == 0:
+                continue
+            # Cold planes to the device on a side stream (pinned -> device copies).
+            with torch.cuda.stream(stream):
+                words_d = torch.cat(words).to(self.device, non_blocking=True)
+                headers_d = torch.cat(headers).to(self.device, non_blocking=True)
+            main.wait_stream(stream)
+            # Layout of the refined tiles: per conversation, tiles of up to 128 selected tokens, every union
+            # group holding 8 planes.
+            old_code = packed.code.numel()
+            tiles_new, groups_new, offs = [], [], old_code
+            token_base = packed.n_tokens
+            group_base = int(packed.groups.shape[0])
+            for s, n in enumerate(per_seq):
+                for j0 in range(0, n, 128):
+                    n_t = min(128, n - j0)
+                    score_base = int(self.seq_m[s]) + j0 if kind == "key" else 0
+                    tiles_new.append([s, token_base, n_t, gu, group_base, score_base, 0, 0])
+                    block = ((n_t * 4 + 7) // 8 * 8 + 8 * n_t * 8 + 15) // 16 * 16
+                    for g in range(gu):
+                        first = [0] * 8 + [n_t] * 8
+                        groups_new.append((g, offs, block, first))
+                        offs += block
+                    token_base += n_t
+                    group_base += gu
+            desc = torch.zeros(len(groups_new), 32, dtype=torch.uint8)
+            d32 = desc.view(torch.int32)
+            for i, (g, off, nb, first) in enumerate(groups_new):
+                d32[i, 0], d32[i, 1], d32[i, 2] = g, off, nb
+                d32[i, 3] = 0 | (8 << 8)  # progressive codes, 8 planes
+                desc[i, 16:32] = torch.tensor(first, dtype=torch.uint8)
+            desc_d = desc.to(self.device)
+            code = torch.zeros(offs + 16, dtype=torch.uint8, device=self.device)
+            code[:old_code] = packed.code
+            # Selected tokens in refined-tile order (the loop above walks conversations in order).
+            ht = torch.cat(hot_tile).to(torch.int32).to(self.device)
+            hr = torch.cat(hot_row).to(torch.int32).to(self.device)
+            # The merge kernel indexes output descriptors as tile * n_groups + group with tiles of 128 tokens
+            # per conversation; launch it per conversation.
+            done, g_done = 0, 0
+            for s, n in enumerate(per_seq):
+                if n == 0:
+                    continue
+                n_tiles_s = (n + 127) // 128
+                a = _lib.RefineArgs(packed.code.data_ptr(), packed.tiles.data_ptr(), packed.groups.data_ptr(),
+                                    ht[done:].data_ptr(), hr[done:].data_ptr(), words_d[done:].data_ptr(),
+                                    headers_d[done:].data_ptr(), n, gu, desc_d[g_done:].data_ptr(), code.data_ptr(),
+                                    self.status.data_ptr())
+                _lib.check(self.lib.dkv_refine_merge(a, main.cuda_stream), "dkv_refine_merge")
+                done += n
+                g_done += n_tiles_s * gu
+            torch.cuda.synchronize(self.device)
+            self.check_status()
+            # Append the refined tiles to the stream.
+            first_new_tile = packed.n_tiles
+            packed.code = code
+            packed.tiles = torch.cat([packed.tiles, torch.tensor(tiles_new, dtype=torch.int32, device=self.device)])
+            packed.groups = torch.cat([packed.groups, desc_d])
+            packed.aux = torch.cat([packed.aux, torch.cat(aux).to(self.device)])
+            packed.present = torch.cat([packed.present, torch.ones(len(tiles_new), gu, dtype=torch.bool)])
+            packed.tile_blocks = torch.cat([packed.tile_blocks, torch.full((len(tiles_new),), gu, dtype=torch.int64)])
+            packed.max_planes = max(packed.max_planes, 8)
+            if kind == "key":
+                # Hide the hot copies: their scores become -inf, so their value entries weigh 0 too.
+                seq_of_sel = torch.cat([torch.full((n,), s_, dtype=torch.int64) for s_, n in enumerate(per_seq) if n])
+                seq_tok0 = torch.tensor([b_ for b_, _ in packed.seq_tokens], dtype=torch.int64)
+                seq_tile0 = torch.tensor([t0_ for t0_, _ in packed.seq_tiles], dtype=torch.int64)
+                local = (ht.cpu().to(torch.int64) - seq_tile0[seq_of_sel]) * 128 + hr.cpu().to(torch.int64)
+                packed.aux[(seq_tok0[seq_of_sel] + local).to(self.device)] = -1
+            else:
+                t = first_new_tile
+                for s, n in enumerate(per_seq):
+                    if n:
+                        nt = (n + 127) // 128
+                        self.extra_value_tiles.append((s, t, t + nt))
+                        t += nt
+        # Score-order lengths grow by the refined tokens.
+        k_counts = [sel.numel() for sel in selected]
+        tok = self.keys.n_tokens - sum(k_counts)
+        for s, n in enumerate(k_counts):
+            if n:
+                self._refined_key_tokens.append((s, tok, tok + n))
+                tok += n
+                self.refined_tokens[s] += n
+        self.seq_m = self.seq_m + torch.tensor(k_counts, dtype=torch.int32, device=self.device)
+        self._rebuild_key_items()
+        self._v_items_cache.clear()
+        self._work = {}
+        self._score_cache = None
+        for s, sel in enumerate(selected):
+            self._refined_pos[s] = torch.cat([self._refined_pos[s], sel.to(torch.int64).cpu()])
+        return fetched
 
     # ------------------------------------------------------------------ accounting
     def code_bytes(self) -> int:

@@ -151,6 +151,56 @@ typedef struct dkv_unpack_args {
 } dkv_unpack_args;
 int dkv_unpack(const dkv_unpack_args* args, void* stream);
 
+/* Question-time importance: adds, for every context token, the attention probability it receives from
+ * every query head and question row of one layer (call once per layer after the softmax statistics).
+ * Replaces the scoring branch of dimmer_attention (scripts/dimmer.py:62-75) summed by
+ * question_importance (scripts/progressive.py:239-254). */
+typedef struct dkv_importance_args {
+  const float* scores;           /* the layer's score buffer (dkv_attend_args.scores) */
+  const int64_t* seq_score_off;
+  const int32_t* seq_m;
+  const int32_t* seq_k_base;     /* [n_seq] first importance slot of each conversation */
+  const float* row_stats;
+  const float* p_exact;
+  int32_t n_seq, n_q_heads, q_len, n_exact, max_m;
+  float* imp_compressed;         /* [sum of seq_m] accumulated, one slot per score (score order) */
+  float* imp_exact;              /* [n_seq][n_exact] accumulated */
+} dkv_importance_args;
+int dkv_importance(const dkv_importance_args* args, void* stream);
+
+/* Top-k token selection per conversation, ties by lowest position; positions out in ascending order.
+ * Replaces importance[start:end].topk(count) (scripts/methods.py:246-247). */
+typedef struct dkv_topk_args {
+  const float* importance;       /* [sum of seq_m] slots, score order */
+  const int32_t* positions;      /* position of every slot, < 0 = not selectable */
+  const int32_t* seq_k_base;
+  const int32_t* seq_m;
+  const int32_t* counts;         /* [n_seq] */
+  const int32_t* out_offset;     /* [n_seq] */
+  int32_t n_seq, max_k;
+  int32_t* out;
+  int* status;
+} dkv_topk_args;
+int dkv_topk(const dkv_topk_args* args, void* stream);
+
+/* Merge of refined tokens: the hot planes of every selected token (from its packed hot block) and its
+ * cold planes (staged from pinned host memory) written as new 8-plane blocks.
+ * Replaces the full-precision re-decode of ProgressiveCache.refine (scripts/progressive.py:224-236). */
+typedef struct dkv_refine_args {
+  const uint8_t* hot_code;
+  const dkv_tile* hot_tiles;
+  const dkv_group* hot_groups;
+  const int32_t* hot_tile;       /* [n_selected] */
+  const int32_t* hot_row;        /* [n_selected] */
+  const uint64_t* cold_words;    /* [n_selected][n_groups][8] */
+  const uint32_t* cold_headers;  /* [n_selected][n_groups] */
+  int32_t n_selected, n_groups;
+  const dkv_group* out_groups;   /* [ceil(n_selected / 128)][n_groups] */
+  uint8_t* out_code;
+  int* status;
+} dkv_refine_args;
+int dkv_refine_merge(const dkv_refine_args* args, void* stream);
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int dkv_version(void);
 

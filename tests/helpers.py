@@ -76,3 +76,52 @@ def exact_kv(fix: dict, inputs: dict, layer: int, q: int, dtype: str):
         sub = mask[0, 0, :, e - q:]
         sub[causal] = finfo_min
     return k, v, mask
+
+
+def exact_cache(inputs: dict, fix: dict, model, device="cpu"):
+    """HF cache of the exact tokens (sinks + recent window) of both layers, in bf16."""
+    from transformers import DynamicCache
+
+    start, end = (int(v) for v in fix["span"])
+    layers = []
+    for layer in range(tm.TINY["num_hidden_layers"]):
+        k = torch.from_numpy(f32_from_bits(inputs["keys"][layer]))
+        v = torch.from_numpy(f32_from_bits(inputs["values"][layer]))
+        layers.append((torch.cat([k[:, :start], k[:, end:]], 1)[None].to(device, torch.bfloat16),
+                       torch.cat([v[:, :start], v[:, end:]], 1)[None].to(device, torch.bfloat16)))
+    return DynamicCache(layers, config=model.config)
+
+
+def oracle_question_importance(model, ctx: OracleContext, inputs: dict, fix: dict, device="cpu", ours=None):
+    """question_importance (scripts/progressive.py:239-254) with the oracle's direct attention: one forward
+    of the question ids over the exact cache, the oracle computing every layer's probabilities from the
+    layer's own query / exact keys. ``ours(module, query, key, value, mask, scaling)``, when given, supplies
+    the layer outputs instead (so that a kernel under test sees exactly the inputs the oracle sees)."""
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, eager_mask
+
+    from oracle.attention import importance_from_probs
+
+    start, end = (int(v) for v in fix["span"])
+    tokens = end + tm.RECENT
+    acc = np.zeros(tokens)
+
+    def probe(module, query, key, value, attention_mask, scaling, **kw):
+        mask = attention_mask.float().cpu().numpy() if attention_mask is not None else None
+        out, p_c, p_e = ctx.attend(module.layer_idx, query.float().cpu().numpy(), key.float().cpu().numpy(),
+                                   value.float().cpu().numpy(), mask, scaling, return_probs=True)
+        exact_pos = np.concatenate([np.arange(start), np.arange(end, tokens),
+                                    np.arange(tokens, tokens + query.shape[2])])
+        acc[:] += importance_from_probs(p_c, p_e, ctx.order, start, exact_pos, tokens)
+        if ours is not None:
+            return ours(module, query, key, value, attention_mask, scaling), None
+        return torch.from_numpy(out).to(query.device, query.dtype).contiguous(), None
+
+    AttentionInterface.register("dkv_oracle_probe", probe)
+    AttentionMaskInterface.register("dkv_oracle_probe", eager_mask)
+    model.set_attn_implementation("dkv_oracle_probe")
+    ids = tm.question_ids()[None].to(device)
+    with torch.inference_mode():
+        model(input_ids=ids, past_key_values=exact_cache(inputs, fix, model, device),
+              position_ids=torch.arange(tokens, tokens + ids.shape[1], device=device)[None])
+    return acc

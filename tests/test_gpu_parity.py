@@ -89,7 +89,7 @@ def test_unpack_bit_exact(golden):
         tok = _prog_tokens(fix, inputs, kind)
         start, end = (int(v) for v in fix["span"])
         conv = ConversationCodes(start, end, tok, tok)
-        ks, _, order = conversation_streams(conv)
+        ks, _, order, _ = conversation_streams(conv)
         packed = pack_streams([ks])
         for bf16 in (0, 1):
             out = torch.zeros(packed.n_tokens, packed.width, dtype=torch.bfloat16 if bf16 else torch.float32, device=DEV)

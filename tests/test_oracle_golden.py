@@ -5,7 +5,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from helpers import exact_kv, f16_from_bits, f32_from_bits, oracle_context, prog_decoded
+from helpers import exact_kv, f16_from_bits, f32_from_bits, oracle_context, oracle_question_importance, prog_decoded
 from oracle import codes as oc
 from oracle.attention import topk_lowest_index
 
@@ -94,6 +94,24 @@ def test_topk_matches_reference(golden):
     start, end = (int(v) for v in fix["span"])
     imp = fix["importance"][start:end]
     ours = np.sort(topk_lowest_index(imp, int(fix["count"])) + start)
+    assert np.array_equal(ours, np.sort(fix["top"]))
+
+
+def test_oracle_importance_matches_reference(golden):
+    """Direct attention over the hot codes scores the question like the reference's eager forward over its
+    rebuilt hot cache (question_importance, scripts/progressive.py:239-254): values within 1e-3 relative
+    (the reference rounds rebuilt keys once, the direct path rounds operands), the same top set."""
+    import torch
+
+    import tinymodel as tm
+
+    inputs, fix = golden("tiny_inputs"), golden("tiny_prog")
+    start, end = (int(v) for v in fix["span"])
+    ctx = oracle_context(fix, inputs, "bf16", True)
+    acc = oracle_question_importance(tm.build_model(torch.bfloat16, "cpu"), ctx, inputs, fix)
+    ref = fix["importance"]
+    assert np.allclose(acc, ref, rtol=1e-3, atol=1e-5)
+    ours = np.sort(topk_lowest_index(acc[start:end], int(fix["count"])) + start)
     assert np.array_equal(ours, np.sort(fix["top"]))
 
 

@@ -31,7 +31,7 @@ def test_pack_progressive_roundtrip(golden):
     _, decoded, _ = prog_decoded(fix, inputs)
     start, end = (int(v) for v in fix["span"])
     conv = ConversationCodes(start, end, _prog_tokens(fix, inputs, "key"), _prog_tokens(fix, inputs, "value"))
-    ks, vs, order_k = conversation_streams(conv)
+    ks, vs, order_k, _ = conversation_streams(conv)
     packed = pack_streams([ks])
     dense = _unpack(packed, packed.width)
     union = packed.union.numpy()
@@ -51,7 +51,7 @@ def test_pack_raw_roundtrip(golden):
     tokens = from_coefficients(coeff, rung)
     start, end = (int(v) for v in fix["span"])
     conv = ConversationCodes(start, end, tokens, tokens)
-    ks, _, order_k = conversation_streams(conv)
+    ks, _, order_k, _ = conversation_streams(conv)
     packed = pack_streams([ks])
     dense = _unpack(packed, packed.width)
     union = packed.union.numpy()
