@@ -53,6 +53,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=None,
                    help="build the model with this many layers (same per-layer shapes; for small profiling cases)")
+    p.add_argument("--kernels-only", action="store_true",
+                   help="profiling case: no model; random keys/values compressed by the same rules, every layer's "
+                        "dkv_attend_layer on random queries (prints a line with \"mode\": \"kernels-only\")")
     return p.parse_args()
 
 
@@ -157,6 +160,148 @@ def exact_cache(model, convs):
     return DynamicCache(list(zip(keys, values)), config=model.config)
 
 
+def build_codes_only(cfg: dict, seqs: int, seed: int, device):
+    """The workload's codes without a model: seeded Gaussian keys/values stand in for the prefill, then the
+    same compression rules (basis, quantisation, plane counts, budget) as build_workload."""
+    import torch
+
+    from dimmerkv import synthetic
+    from dimmerkv.context import CompressedBatch
+
+    arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
+    layers, kv, hd, hq = arch["num_hidden_layers"], arch["num_key_value_heads"], arch["head_dim"], \
+        arch["num_attention_heads"]
+    features = layers * kv * hd
+    rank = cfg["max_groups"] * 64
+    bases = {kind: synthetic.seeded_basis(features, rank, 1000 + seed * 2 + i, device)
+             for i, kind in enumerate(("key", "value"))}
+    g = torch.Generator().manual_seed(10_000 + seed)
+    gd = torch.Generator(device=device).manual_seed(20_000 + seed)
+    lengths = torch.randint(cfg["tmin"], cfg["tmax"] + 1, (seqs,), generator=g).tolist()
+    max_t = max(lengths)
+    pos = torch.arange(max_t + 4096, dtype=torch.float32, device=device)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, hd, 2, dtype=torch.float32, device=device) / hd))
+    ang = pos[:, None] * inv
+    cos_h, sin_h = torch.cos(ang), torch.sin(ang)
+    cos_f, sin_f = torch.cat([cos_h, cos_h], 1), torch.cat([sin_h, sin_h], 1)
+    convs = []
+    for t in lengths:
+        keys = [torch.randn(1, kv, t, hd, generator=gd, device=device).to(torch.bfloat16) for _ in range(layers)]
+        values = [torch.randn(1, kv, t, hd, generator=gd, device=device).to(torch.bfloat16) for _ in range(layers)]
+        with torch.inference_mode():
+            conv = synthetic.compress_conversation(keys, values, cos_f[:t], sin_f[:t], bases, cfg["budget"], g,
+                                                   cfg["max_groups"])
+        del keys, values
+        convs.append(conv)
+    mean = {kind: torch.stack([cv.mean[kind] for cv in convs]) for kind in ("key", "value")}
+    batch = CompressedBatch([cv.codes for cv in convs], layers=layers, kv_heads=kv, head_dim=hd, q_heads=hq,
+                            basis=bases, mean=mean, cos=cos_h.to(torch.bfloat16), sin=sin_h.to(torch.bfloat16),
+                            device=device)
+    for cv in convs:
+        cv.codes = None
+    return batch, convs, lengths
+
+
+def step_work(batch, convs, layers: int):
+    """Algorithmic work of one decode step: (key_scores FLOPs per layer launch, code bytes per step).
+    Key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per layer; both streams' hot codes re-read once per layer."""
+    flops_layer, code_bytes_step = 0, 0
+    for cv in convs:
+        flops_layer += 2 * cv.busy_key * cv.groups * 64 * batch.n_cols + 2 * cv.middle * batch.q_heads * batch.head_dim
+        code_bytes_step += cv.hot_bytes * layers
+    return flops_layer, code_bytes_step
+
+
+class StageTimer:
+    """CUDA events around each of the four kernels of every dkv_attend_layer call (on the launching stream)."""
+
+    NAMES = ("key_scores", "softmax_stats", "value_weights", "finalize")
+
+    def __init__(self, batch, stream):
+        self.batch, self.stream, self.events = batch, stream, []
+
+    def __call__(self, layer, call, a, s):
+        import torch
+
+        from dimmerkv import _lib
+
+        if self.batch.q_heads * int(a.q_len) > a.rows_pad:
+            raise RuntimeError("stage timing expects one row chunk per layer")
+        lib = self.batch.lib
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record(self.stream)
+        for i, fn in enumerate((lib.dkv_key_scores, lib.dkv_softmax_stats, lib.dkv_value_weights, lib.dkv_finalize)):
+            _lib.check(fn(a, s), self.NAMES[i])
+            ev[i + 1].record(self.stream)
+        self.events.append(ev)
+
+    def key_ms(self):
+        return [ev[0].elapsed_time(ev[1]) for ev in self.events]
+
+    def stage_ms(self, steps: int):
+        return {name: round(sum(ev[i].elapsed_time(ev[i + 1]) for ev in self.events) / steps, 3)
+                for i, name in enumerate(self.NAMES)}
+
+
+def roofline(flops_layer: int, key_ms: list) -> dict:
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    peak_name = "of measured (bf16_tflops_sustained)" if peaks else "of fallback"
+    key_avg_ms = statistics.mean(key_ms) if key_ms else float("nan")
+    achieved = flops_layer / (key_avg_ms / 1e3) / 1e12
+    traffic = None
+    prof = ROOT / "profiles" / "key_scores_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("bytes_per_launch")
+    return {"bound": "tensor", "kernel": "key_scores (tcgen05 key rebuild + RoPE + QK)",
+            "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tf, 4), "peak_source": peak_name,
+            "avg_launch_ms": round(key_avg_ms, 4), "launches": len(key_ms),
+            "algorithmic_flop_per_launch": flops_layer, "traffic": traffic}
+
+
+def run_kernels(args, cfg, device) -> dict:
+    """Profiling case: every layer's dkv_attend_layer over the packed codes, random queries, no model."""
+    import torch
+
+    seqs = args.seqs or cfg["seqs"]
+    batch, convs, lengths = build_codes_only(cfg, seqs, args.seed, device)
+    layers, hq, hd, kv = batch.layers, batch.q_heads, batch.head_dim, batch.kv_heads
+    g = torch.Generator(device=device).manual_seed(args.seed + 1)
+    q = torch.randn(seqs, hq, 1, hd, generator=g, device=device).to(torch.bfloat16)
+    ek = [torch.cat([cv.exact_keys[l] for cv in convs]) for l in range(layers)]
+    ev = [torch.cat([cv.exact_values[l] for cv in convs]) for l in range(layers)]
+    stream = torch.cuda.current_stream(device)
+    timer = StageTimer(batch, stream)
+
+    def step():
+        for layer in range(layers):
+            batch.attend_layer(layer, q, ek[layer], ev[layer], None, hd ** -0.5)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    batch.check_status()
+    batch.timer = timer
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    batch.timer = None
+    batch.check_status()
+    elapsed = start.elapsed_time(end) / 1e3
+    flops_layer, code_bytes_step = step_work(batch, convs, layers)
+    return {"mode": "kernels-only", "config": {"workload": cfg["workload"] + " (attention kernels only, no model)",
+                                               "conversations": seqs, "context_mean": sum(lengths) / len(lengths)},
+            "ms_per_step": round(elapsed / args.steps * 1e3, 3), "steps": args.steps, "warmup": args.warmup,
+            "attention_tok_s": round(seqs * args.steps / elapsed, 2),
+            "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
+            "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
+            "gpu_launches": len(timer.events) * 4}
+
+
 # ----------------------------------------------------------------------------- runs
 def run_ours(args, cfg, rank, world, device):
     import torch
@@ -169,13 +314,7 @@ def run_ours(args, cfg, rank, world, device):
     model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed + 7919 * rank, device, args.layers)
     setup_s = time.time() - t0
     layers = model.config.num_hidden_layers
-    # Algorithmic work of one step (SURVEY-style count): key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per
-    # layer for the key_scores launch; code bytes of both streams re-read once per layer.
-    flops_layer = 0
-    code_bytes_step = 0
-    for cv in convs:
-        flops_layer += 2 * cv.busy_key * cv.groups * 64 * batch.n_cols + 2 * cv.middle * batch.q_heads * batch.head_dim
-        code_bytes_step += cv.hot_bytes * layers
+    flops_layer, code_bytes_step = step_work(batch, convs, layers)
 
     cache = exact_cache(model, convs)
     ids = torch.randint(0, model.config.vocab_size, (seqs, 1), device=device,
@@ -184,25 +323,7 @@ def run_ours(args, cfg, rank, world, device):
     dimmer.STATE.compressed = batch
     stream = torch.cuda.current_stream(device)
 
-    # Per-launch timing of every stage: CUDA events on the launching stream around each kernel.
-    key_events = []
-
-    def timed_layer(layer, call, a, s):
-        from dimmerkv import _lib
-
-        if batch.q_heads * int(a.q_len) > a.rows_pad:
-            raise RuntimeError("bench timing expects one row chunk per layer")
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-        ev[0].record(stream)
-        _lib.check(batch.lib.dkv_key_scores(a, s), "dkv_key_scores")
-        ev[1].record(stream)
-        _lib.check(batch.lib.dkv_softmax_stats(a, s), "dkv_softmax_stats")
-        ev[2].record(stream)
-        _lib.check(batch.lib.dkv_value_weights(a, s), "dkv_value_weights")
-        ev[3].record(stream)
-        _lib.check(batch.lib.dkv_finalize(a, s), "dkv_finalize")
-        ev[4].record(stream)
-        key_events.append(ev)
+    timer = StageTimer(batch, stream)  # CUDA events around every kernel launch of the timed steps
 
     def step(ids_, pos_):
         out = model(input_ids=ids_, past_key_values=cache, position_ids=pos_, use_cache=True)
@@ -216,8 +337,7 @@ def run_ours(args, cfg, rank, world, device):
         batch.check_status()
         if world > 1:
             dist.barrier()
-        batch.timer = timed_layer
-        key_events.clear()
+        batch.timer = timer
         with ClockSampler(device.index if device.index is not None else 0) as clocks:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize(device)
@@ -232,9 +352,8 @@ def run_ours(args, cfg, rank, world, device):
         batch.timer = None
         batch.check_status()
         elapsed = start.elapsed_time(end) / 1e3
-        key_ms = [ev[0].elapsed_time(ev[1]) for ev in key_events]
-        stage_ms = {name: sum(ev[i].elapsed_time(ev[i + 1]) for ev in key_events) / args.steps
-                    for i, name in enumerate(("key_scores", "softmax_stats", "value_weights", "finalize"))}
+        key_ms = timer.key_ms()
+        stage_ms = timer.stage_ms(args.steps)
 
     t = torch.tensor([elapsed], device=device, dtype=torch.float64)
     if world > 1:
@@ -265,15 +384,6 @@ def run_ours(args, cfg, rank, world, device):
 
     result = None
     if rank == 0:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
-        peak_name = "of measured (bf16_tflops_sustained)" if peaks else "of fallback"
-        key_avg_ms = statistics.mean(key_ms) if key_ms else float("nan")
-        achieved = flops_layer / (key_avg_ms / 1e3) / 1e12
-        traffic = None
-        prof = ROOT / "profiles" / "key_scores_traffic.json"
-        if prof.exists():
-            traffic = json.loads(prof.read_text()).get("bytes_per_launch")
         clk = clocks.summary()
         tokps = world * seqs * args.steps / elapsed_max
         result = {
@@ -286,13 +396,9 @@ def run_ours(args, cfg, rank, world, device):
                        "budget": cfg["budget"], "parallelism": f"conversation-parallel x{world}",
                        "l2": "inputs larger than L2 (codes re-read per layer, > 1 GB per layer)"},
             "code_read_gbs": round(code_bytes_step / (elapsed_max / args.steps) / 1e9, 2),
-            "roofline": {"bound": "tensor", "kernel": "key_scores (tcgen05 key rebuild + RoPE + QK)",
-                         "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak_tf, 4), "peak_source": peak_name,
-                         "avg_launch_ms": round(key_avg_ms, 4), "launches": len(key_ms),
-                         "algorithmic_flop_per_launch": flops_layer, "traffic": traffic},
+            "roofline": roofline(flops_layer, key_ms),
             "clocks": clk,
-            "stage_ms_per_step": {k: round(v, 3) for k, v in stage_ms.items()},
+            "stage_ms_per_step": stage_ms,
             "gpu_launches": len(key_ms) * 4,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
@@ -425,6 +531,11 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(minutes=10), device_id=device)
     try:
+        if args.kernels_only:
+            if world > 1:
+                raise SystemExit("--kernels-only is a 1-GPU profiling case")
+            print(json.dumps(run_kernels(args, cfg, device)), flush=True)
+            return
         result = run_ours(args, cfg, rank, world, device)
         if result is not None:
             print(json.dumps(result), flush=True)

@@ -136,6 +136,10 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   p.scaling = a->scaling;
   p.max_planes = a->k_max_planes;
   p.status = a->status;
+  p.cta_begin = a->k_cta_begin;
+  p.item_order = a->k_item_order;
+  if ((a->k_item_order != nullptr && a->k_cta_begin == nullptr) || (a->k_cta_begin != nullptr && a->grid_k <= 0))
+    return DKV_ERR_ARGS;
   const int grid = a->grid_k > 0 ? a->grid_k : (a->n_k_items < sm_count() ? a->n_k_items : sm_count());
   return dkv::run_key_scores(map, p, nb, grid, static_cast<cudaStream_t>(stream));
 }
@@ -186,6 +190,10 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
   p.n_rows_pad = a->rows_pad;
   p.partial = a->partial;
   p.status = a->status;
+  p.cta_begin = a->v_cta_begin;
+  p.item_order = a->v_item_order;
+  if ((a->v_item_order != nullptr && a->v_cta_begin == nullptr) || (a->v_cta_begin != nullptr && a->grid_v <= 0))
+    return DKV_ERR_ARGS;
   const int grid = a->grid_v > 0 ? a->grid_v : (a->n_v_items < sm_count() ? a->n_v_items : sm_count());
   return dkv::run_value_weights(p, grid, static_cast<cudaStream_t>(stream));
 }
@@ -216,6 +224,8 @@ static int finalize_rows(const dkv_attend_args* a, int row_begin, int n_rows, vo
   p.n_cols = a->n_kv_heads * a->head_dim;
   p.out = a->out;
   p.out_f32 = a->out_f32;
+  p.vpart = a->vpart;
+  if (a->vpart == nullptr) return DKV_ERR_ARGS;
   return dkv::run_finalize(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -238,6 +248,11 @@ int dkv_finalize(const dkv_attend_args* a, void* stream) {
   const int rows = a->n_q_heads * a->q_len;
   if (rows > a->rows_pad) return DKV_ERR_CONFIG;  // multi-chunk rows go through dkv_attend_layer
   return finalize_rows(a, 0, rows, stream);
+}
+
+int64_t dkv_vpart_floats(int32_t v_width, int32_t n_seq, int32_t rows_pad, int32_t head_dim) {
+  if (v_width < 0 || n_seq < 0 || rows_pad < 0 || head_dim < 0) return -1;
+  return static_cast<int64_t>(dkv::finalize_chunks(v_width)) * n_seq * rows_pad * head_dim;
 }
 
 int dkv_attend_layer(const dkv_attend_args* a, void* stream) {

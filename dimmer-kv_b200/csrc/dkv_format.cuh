@@ -90,6 +90,34 @@ __device__ __forceinline__ GroupRegs stashed_group(const uint8_t* slot_end) {
   return group_from_words(src[0], src[1]);
 }
 
+// The work items one CTA processes: with a static schedule, the list order[cta_begin[b] ..
+// cta_begin[b+1]) (order NULL: the list positions themselves); without one, every gridDim.x-th item
+// from blockIdx.x. at() returns -1 for an entry outside [0, n_items), which the caller reports.
+struct ItemRange {
+  int k, end, step, n_items;
+  const int32_t* order;
+
+  __device__ __forceinline__ ItemRange(const int32_t* cta_begin, const int32_t* item_order, int n) {
+    n_items = n;
+    if (cta_begin != nullptr) {
+      k = max(0, __ldg(cta_begin + blockIdx.x));
+      end = __ldg(cta_begin + blockIdx.x + 1);
+      step = 1;
+      order = item_order;
+      if (order == nullptr) end = min(end, n);
+    } else {
+      k = blockIdx.x;
+      end = n;
+      step = gridDim.x;
+      order = nullptr;
+    }
+  }
+  __device__ __forceinline__ int at(int kk) const {
+    const int it = order != nullptr ? __ldg(order + kk) : kk;
+    return (it >= 0 && it < n_items) ? it : -1;
+  }
+};
+
 // Byte j (0..15, runtime) of the 'first' table.
 __device__ __forceinline__ uint32_t first_at(const GroupRegs& g, int j) {
   const uint32_t lo = (j & 4) ? g.first4[1] : g.first4[0];
@@ -98,89 +126,130 @@ __device__ __forceinline__ uint32_t first_at(const GroupRegs& g, int j) {
 }
 
 // Plane count of tile token r for this group: the number of planes j with first[j] <= r (the
-// table is non-decreasing and holds n_tokens past max_planes), four bytes per SIMD compare.
+// table is non-decreasing and holds n_tokens past max_planes). Four bytes per subtraction: with
+// r, first[j] <= 128, byte (0x80 | r) - first[j] never borrows and keeps its top bit iff r >= first[j].
 __device__ __forceinline__ int planes_of(const GroupRegs& g, int r, int n_tokens) {
   if (r >= n_tokens) return 0;
-  const uint32_t rr = static_cast<uint32_t>(r) * 0x01010101u;
-  return (__popc(__vcmpgeu4(rr, g.first4[0])) + __popc(__vcmpgeu4(rr, g.first4[1])) +
-          __popc(__vcmpgeu4(rr, g.first4[2])) + __popc(__vcmpgeu4(rr, g.first4[3]))) >> 3;
+  const uint32_t rr = (static_cast<uint32_t>(r) * 0x01010101u) | 0x80808080u;
+  return __popc((rr - g.first4[0]) & 0x80808080u) + __popc((rr - g.first4[1]) & 0x80808080u) +
+         __popc((rr - g.first4[2]) & 0x80808080u) + __popc((rr - g.first4[3]) & 0x80808080u);
 }
 
-// Spread the four bits (4b .. 4b+3) of a plane word into bit s of four bytes.
-__device__ __forceinline__ uint32_t spread4(uint32_t w, int b, uint32_t s) {
-  return ((((w >> (4 * b)) & 0xFu) * (0x204081u << s)) & (0x01010101u << s));
+// Bit order of a plane word: in each 32-bit half, bit 8k + b holds component 4b + k (byte k holds
+// components k, k+4, ..., k+28). gather_plane drops the 32 bits of one half-word into bit s of the
+// per-component bytes: byte k of acc[b] collects component 4b + k. Rotating left by s and then right
+// by b moves bit 8k + b to 8k + s (and no other bit there), so each group of four components costs
+// one rotate and one masked OR.
+__device__ __forceinline__ void gather_plane(uint32_t (&acc)[8], uint32_t w, uint32_t s) {
+  const uint32_t ws = __funnelshift_l(w, w, s);
+  const uint32_t mask = 0x01010101u << s;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) acc[b] |= __funnelshift_r(ws, ws, b) & mask;
+}
+
+// Plane words of a token with exactly M planes: all M loads are issued before any is used (one
+// memory latency instead of M), then each is gathered into the per-component bytes.
+template <int M>
+__device__ __forceinline__ void gather_fixed(const uint8_t* blk, const GroupRegs& g, uint32_t n, uint32_t ru, int h,
+                                             uint32_t seg, uint32_t (&acc)[8]) {
+  uint32_t w[M];
+#pragma unroll
+  for (int j = 0; j < M; ++j) {
+    const uint32_t fj = (g.first4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+    w[j] = *reinterpret_cast<const uint32_t*>(blk + seg + (ru - fj) * 8u + 4u * h);
+    seg += (n - fj) * 8u;
+  }
+#pragma unroll
+  for (int j = 0; j < M; ++j) gather_plane(acc, w[j], static_cast<uint32_t>(M - 1 - j));
+}
+
+// Index bits of the 32 components of half h of token r: byte k of acc[b] = index of component 4b + k
+// (raw bf16: acc the high byte, acc_lo the low byte). Returns the token's plane count m (0: no planes;
+// acc untouched). Tokens of a tile are sorted by plane count, so the switch is warp-uniform almost
+// everywhere.
+__device__ __forceinline__ int gather_index(const uint8_t* blk, const GroupRegs& g, int n_tokens, int r, int h,
+                                            uint32_t (&acc)[8], uint32_t (&acc_lo)[8]) {
+  const int m = planes_of(g, r, n_tokens);
+  if (m == 0) return 0;
+  const uint32_t n = static_cast<uint32_t>(n_tokens);
+  const uint32_t ru = static_cast<uint32_t>(r);
+  const uint32_t f0 = g.first4[0] & 0xFFu;
+  const uint32_t seg = ((n - f0) * 4u + 7u) & ~7u;
+  switch (m) {
+    case 1: gather_fixed<1>(blk, g, n, ru, h, seg, acc); break;
+    case 2: gather_fixed<2>(blk, g, n, ru, h, seg, acc); break;
+    case 3: gather_fixed<3>(blk, g, n, ru, h, seg, acc); break;
+    case 4: gather_fixed<4>(blk, g, n, ru, h, seg, acc); break;
+    case 5: gather_fixed<5>(blk, g, n, ru, h, seg, acc); break;
+    case 6: gather_fixed<6>(blk, g, n, ru, h, seg, acc); break;
+    case 7: gather_fixed<7>(blk, g, n, ru, h, seg, acc); break;
+    case 8: gather_fixed<8>(blk, g, n, ru, h, seg, acc); break;
+    default: {
+      // Raw bf16 (m == 16): planes 0..7 carry the high byte, 8..15 the low byte.
+      uint32_t sg = seg;
+      for (int j = 0; j < kMaxPlanes; ++j) {
+        const uint32_t fj = first_at(g, j);
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + sg + (ru - fj) * 8u + 4u * h);
+        sg += (n - fj) * 8u;
+        if (j < 8)
+          gather_plane(acc, w, static_cast<uint32_t>(7 - j));
+        else
+          gather_plane(acc_lo, w, static_cast<uint32_t>(15 - j));
+      }
+    }
+  }
+  return m;
 }
 
 // Decode 32 components (half h of the 64-component group) of token r from a block that starts
 // at `blk` (shared or global memory). `out` receives 16 packed bf16x2 words (components 32h..32h+31).
-// Only the token's own planes are visited; the float arithmetic is the reference's, in float32
-// with no contraction, then rounded to bf16 (the reference's .to(dtype), compressed_attention.py:76).
+// Only the token's own planes are visited. The value is the reference's float32 arithmetic then
+// rounded to bf16 (the reference's .to(dtype), compressed_attention.py:76):
+//   progressive (idx + 0.5) * mult / 2^m + low, ladder idx * mult + low.
+// For m <= 8 the product is exact in float32 ((idx + 0.5) has at most 9 significant bits and
+// mult / 2^m at most 11, an f16 value scaled by a power of two), so one fused multiply-add rounds
+// exactly once, like the reference's separate multiply (exact) and add.
 __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs& g, int n_tokens, int r, int h,
                                             uint32_t (&out)[16]) {
-  const int m = planes_of(g, r, n_tokens);
+  uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  uint32_t lo[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int m = gather_index(blk, g, n_tokens, r, h, acc, lo);
   if (m == 0) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) out[i] = 0u;
     return;
   }
-  const uint32_t n = static_cast<uint32_t>(n_tokens);
-  const uint32_t f0 = first_at(g, 0);
-  uint32_t seg = ((n - f0) * 4u + 7u) & ~7u;
   if (m == kMaxPlanes) {
-    // Raw bf16: planes 0..7 carry the high byte, 8..15 the low byte.
-    uint32_t hi[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lo[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < kMaxPlanes; ++j) {
-      const uint32_t fj = first_at(g, j);
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + seg + (static_cast<uint32_t>(r) - fj) * 8u + 4u * h);
-      seg += (n - fj) * 8u;
-      const uint32_t s = 7u - static_cast<uint32_t>(j & 7);
-      if (j < 8) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) hi[b] |= spread4(w, b, s);
-      } else {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) lo[b] |= spread4(w, b, s);
-      }
-    }
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      out[2 * b] = __byte_perm(lo[b], hi[b], 0x5140);
-      out[2 * b + 1] = __byte_perm(lo[b], hi[b], 0x7362);
+      out[2 * b] = __byte_perm(lo[b], acc[b], 0x5140);
+      out[2 * b + 1] = __byte_perm(lo[b], acc[b], 0x7362);
     }
     return;
   }
-  // Gather the m index bits of every component into the bytes of acc[b] (components 4b..4b+3).
-  uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int j = 0; j < m; ++j) {
-    const uint32_t fj = first_at(g, j);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + seg + (static_cast<uint32_t>(r) - fj) * 8u + 4u * h);
-    seg += (n - fj) * 8u;
-    const uint32_t s = static_cast<uint32_t>(m - 1 - j);
-#pragma unroll
-    for (int b = 0; b < 8; ++b) acc[b] |= spread4(w, b, s);
-  }
   // Header: f16 low, f16 mult.
+  const uint32_t f0 = first_at(g, 0);
   const uint32_t hdr = *reinterpret_cast<const uint32_t*>(blk + (static_cast<uint32_t>(r) - f0) * 4u);
   const float low = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr & 0xFFFFu)));
   const float mult = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr >> 16)));
-  // progressive: (idx + 0.5) * (span * 2^-m)  == ((idx + 0.5) * span) / 2^m exactly (power-of-two scaling)
-  // ladder:      idx * scale
   const bool prog = (g.kind == kKindProgressive);
-  const float scale = prog ? __fmul_rn(mult, __int_as_float((127 - m) << 23)) : mult;
+  const float scale = prog ? __fmul_rn(mult, __int_as_float((127 - m) << 23)) : mult;  // exact (power of two)
   const float bias = prog ? 8388607.5f : 8388608.0f;  // float(0x4B000000 | idx) - bias = idx (+ 0.5)
   if (m <= 2) {
-    // At most four distinct values: decode them once (same arithmetic), then every output pair is
-    // one byte permute selecting bf16 halves: pair (idx0, idx1) <- selector 0x1010 + 34*(idx0 | idx1 << 8).
+    // At most four distinct values: decode them once, then every output pair is one byte permute
+    // selecting bf16 halves of (t0, t1 | t2, t3): the selector of pair (i0, i1) is
+    // 0x1010 + 34 * (i0 | i1 << 8), computed for two pairs at once (each byte stays below 256).
     float t[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) t[i] = __fadd_rn(__fmul_rn(__fsub_rn(8388608.0f + i, bias), scale), low);
+    for (int i = 0; i < 4; ++i) t[i] = __fmaf_rn(__fsub_rn(8388608.0f + i, bias), scale, low);
     __nv_bfloat162 v01 = __floats2bfloat162_rn(t[0], t[1]);
     __nv_bfloat162 v23 = __floats2bfloat162_rn(t[2], t[3]);
-    const uint32_t lo = *reinterpret_cast<uint32_t*>(&v01), hi = *reinterpret_cast<uint32_t*>(&v23);
+    const uint32_t tlo = *reinterpret_cast<uint32_t*>(&v01), thi = *reinterpret_cast<uint32_t*>(&v23);
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      out[2 * b] = __byte_perm(lo, hi, 0x1010u + 34u * (acc[b] & 0xFFFFu));
-      out[2 * b + 1] = __byte_perm(lo, hi, 0x1010u + 34u * (acc[b] >> 16));
+      const uint32_t sel = acc[b] * 34u + 0x10101010u;
+      out[2 * b] = __byte_perm(tlo, thi, sel);
+      out[2 * b + 1] = __byte_perm(tlo, thi, sel >> 16);
     }
     return;
   }
@@ -190,7 +259,7 @@ __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs&
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float x = __uint_as_float(__byte_perm(acc[b], 0x4B000000u, 0x7440u | k));
-      v[k] = __fadd_rn(__fmul_rn(__fsub_rn(x, bias), scale), low);
+      v[k] = __fmaf_rn(__fsub_rn(x, bias), scale, low);
     }
     __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
     __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
@@ -202,29 +271,22 @@ __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs&
 // float32 variant of the decoder (used by the standalone unpack kernel).
 __device__ __forceinline__ void decode_half_f32(const uint8_t* blk, const GroupRegs& g, int n_tokens, int r, int h,
                                                 float (&out)[32]) {
-  const int m = planes_of(g, r, n_tokens);
+  uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  uint32_t lo[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int m = gather_index(blk, g, n_tokens, r, h, acc, lo);
   if (m == 0 || m == kMaxPlanes) {
-    uint32_t packed[16];
-    decode_half(blk, g, n_tokens, r, h, packed);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      out[2 * i] = __uint_as_float(packed[i] << 16);
-      out[2 * i + 1] = __uint_as_float(packed[i] & 0xFFFF0000u);
+    for (int b = 0; b < 8; ++b) {
+      // Raw bf16 widened to float32 (zero when there are no planes: acc and lo are zero).
+      const uint32_t p0 = __byte_perm(lo[b], acc[b], 0x5140), p1 = __byte_perm(lo[b], acc[b], 0x7362);
+      out[4 * b] = __uint_as_float(p0 << 16);
+      out[4 * b + 1] = __uint_as_float(p0 & 0xFFFF0000u);
+      out[4 * b + 2] = __uint_as_float(p1 << 16);
+      out[4 * b + 3] = __uint_as_float(p1 & 0xFFFF0000u);
     }
     return;
   }
-  const uint32_t n = static_cast<uint32_t>(n_tokens);
   const uint32_t f0 = first_at(g, 0);
-  uint32_t seg = ((n - f0) * 4u + 7u) & ~7u;
-  uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int j = 0; j < m; ++j) {
-    const uint32_t fj = first_at(g, j);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + seg + (static_cast<uint32_t>(r) - fj) * 8u + 4u * h);
-    seg += (n - fj) * 8u;
-    const uint32_t s = static_cast<uint32_t>(m - 1 - j);
-#pragma unroll
-    for (int b = 0; b < 8; ++b) acc[b] |= spread4(w, b, s);
-  }
   const uint32_t hdr = *reinterpret_cast<const uint32_t*>(blk + (static_cast<uint32_t>(r) - f0) * 4u);
   const float low = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr & 0xFFFFu)));
   const float mult = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr >> 16)));
@@ -236,7 +298,7 @@ __device__ __forceinline__ void decode_half_f32(const uint8_t* blk, const GroupR
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float x = __uint_as_float(__byte_perm(acc[b], 0x4B000000u, 0x7440u | k));
-      out[4 * b + k] = __fadd_rn(__fmul_rn(__fsub_rn(x, bias), scale), low);
+      out[4 * b + k] = __fmaf_rn(__fsub_rn(x, bias), scale, low);
     }
   }
 }

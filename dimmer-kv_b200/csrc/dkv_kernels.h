@@ -42,6 +42,8 @@ struct KeyScoreParams {
   float scaling;
   int max_planes;                 // largest plane count of any key block (> 8: raw blocks present)
   int* status;
+  const int32_t* cta_begin;       // optional static schedule (see ValueWeightParams)
+  const int32_t* item_order;
 };
 int run_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int nb, int grid, cudaStream_t stream);
 
@@ -81,6 +83,8 @@ struct ValueWeightParams {
   int row_begin, n_rows, n_rows_pad;  // rows = q_head * q_len + qi; N of the MMA = n_rows_pad
   float* partial;                 // [n_items][n_rows_pad][item_groups * 64]
   int* status;
+  const int32_t* cta_begin;       // optional static schedule: CTA b takes item_order[cta_begin[b] .. cta_begin[b+1])
+  const int32_t* item_order;
 };
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream);
 
@@ -100,7 +104,9 @@ struct FinalizeParams {
   int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact, layer, n_cols;
   void* out;                      // [n_seq][q_len][n_q_heads][head_dim]
   int out_f32;                    // fp32 output instead of bf16
+  float* vpart;                   // [finalize_chunks(r_v)][n_seq][n_rows_pad][head_dim]
 };
+int finalize_chunks(int r_v);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);
 
 // Standalone ragged bit-plane unpack (unpack.cu).

@@ -4,119 +4,160 @@
 //   out_c = sum(p_c) * mean_v + (p_c @ C_v) @ B_v[layer, head]     (values never decoded)
 //   out   = out_c + p_e @ V_exact
 // The probability-weighted coefficients p_c @ C_v arrive as per-item partial sums from
-// value_weights.cu; this kernel reduces them, applies the value basis of the layer for one KV
-// head and writes the output in the HF layout [batch, q_len, q_heads, head_dim] (bf16).
+// value_weights.cu. Two kernels:
+//   vbasis  : one CTA per (chunk of 128 basis components, KV head, block of 8 conversations). The
+//             CTA stages its basis slice [128 components x head_dim] in shared memory, reduces the
+//             items' partial sums of those components for its conversations and multiplies them by
+//             the slice: the layer's value basis is read once per 8 conversations instead of once per
+//             conversation. Output: per-chunk partial outputs [chunks][conversations][rows][head_dim].
+//   combine : sums the chunks in a fixed order (deterministic), adds the mean term and the exact
+//             tokens, and writes the HF layout [batch, q_len, q_heads, head_dim].
 #include "dkv_kernels.h"
 
 namespace dkv {
 
 namespace {
 constexpr int kFinalizeThreads = 256;
-}
+constexpr int kCombineThreads = 128;
+constexpr int kRChunk = 128;   // basis components per vbasis CTA
+constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
+}  // namespace
 
-__global__ void __launch_bounds__(kFinalizeThreads) finalize_kernel(const FinalizeParams p) {
-  extern __shared__ float w[];  // [G][r_v] weighted coefficients of one query row, then reduction scratch
-  const int n_kv = p.n_q_heads / p.q_per_kv;
-  const int s = blockIdx.x / n_kv;
-  const int kvh = blockIdx.x % n_kv;
+__global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block) {
+  extern __shared__ float smem_f[];
   const int D = p.head_dim;
+  const int D2 = D / 2;
   const int G = p.q_per_kv;
-  const int R = p.r_v;
-  const int parts = blockDim.x / (D / 2);   // component slices
-  const int d2 = threadIdx.x % (D / 2);     // output dims 2*d2, 2*d2+1
-  const int part = threadIdx.x / (D / 2);
-  const int d = threadIdx.x;                // output dim of the final combine (threads 0 .. D-1)
-  float* red = w + G * R;  // [parts][G][D]
+  const int chunk = blockIdx.x, kvh = blockIdx.y;
+  const int s0 = blockIdx.z * seq_block;
+  const int n_s = min(seq_block, p.n_seq - s0);
+  const int r0 = chunk * kRChunk;
+  const int rlo = max(p.row_begin, kvh * G * p.q_len);
+  const int rhi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  const int nr = rhi - rlo;
+  if (nr <= 0 || n_s <= 0) return;
+  __nv_bfloat162* bs = reinterpret_cast<__nv_bfloat162*>(smem_f);  // [kRChunk][D/2]
+  float* ws = smem_f + kRChunk * D2;                                // [n_s][nr][kRChunk]
+  const int tid = threadIdx.x;
   const int item_cols = p.item_groups * 64;
 
-  for (int qi = 0; qi < p.q_len; ++qi) {
-    // Only rows computed by the matching value_weights call.
-    bool any = false;
-    for (int j = 0; j < G; ++j) {
-      const int row = (kvh * G + j) * p.q_len + qi - p.row_begin;
-      any |= (row >= 0 && row < p.n_rows);
+  // Basis slice of this KV head: rows r0 .. r0+127 of [layer][r_v][n_cols], columns kvh*D .. +D.
+  const __nv_bfloat162* bsrc =
+      reinterpret_cast<const __nv_bfloat162*>(p.basis_v + static_cast<int64_t>(p.layer) * p.r_v * p.n_cols) +
+      kvh * D2;
+  for (int i = tid; i < kRChunk * D2; i += kFinalizeThreads) {
+    const int r = i / D2, dp = i % D2;
+    bs[i] = (r0 + r < p.r_v) ? bsrc[static_cast<int64_t>(r0 + r) * (p.n_cols / 2) + dp]
+                             : __floats2bfloat162_rn(0.f, 0.f);
+  }
+  // Weighted coefficients of the block's conversations: every element sums its conversation's items
+  // that cover this chunk (independent loads, in item order).
+  for (int i = tid; i < n_s * nr * kRChunk; i += kFinalizeThreads) {
+    const int sl = i / (nr * kRChunk);
+    const int rr = (i / kRChunk) % nr, c = i % kRChunk;
+    const int s = s0 + sl;
+    float acc = 0.f;
+    for (int it = p.seq_items[2 * s], it1 = p.seq_items[2 * s + 1]; it < it1; ++it) {
+      const int cb = p.items[4 * it + 3] * 64;
+      if (r0 < cb || r0 >= cb + item_cols) continue;  // the item does not cover this chunk
+      acc += p.partial[(static_cast<int64_t>(it) * p.n_rows_pad + (rlo - p.row_begin + rr)) * item_cols + (r0 - cb) + c];
     }
-    if (!any) continue;
-    for (int i = threadIdx.x; i < G * R; i += blockDim.x) w[i] = 0.f;
-    __syncthreads();
-    const int it0 = p.seq_items[2 * s], it1 = p.seq_items[2 * s + 1];
-    for (int it = it0; it < it1; ++it) {
-      const int g0 = p.items[4 * it + 3];
-      for (int j = 0; j < G; ++j) {
-        const int row = (kvh * G + j) * p.q_len + qi - p.row_begin;
-        if (row < 0 || row >= p.n_rows) continue;
-        const float* src = p.partial + (static_cast<int64_t>(it) * p.n_rows_pad + row) * item_cols;
-        for (int c = threadIdx.x; c < item_cols; c += blockDim.x) {
-          const int col = g0 * 64 + c;
-          if (col < R) w[j * R + col] += src[c];
-        }
-      }
+    ws[i] = acc;
+  }
+  __syncthreads();
+  const int dp = tid % D2;
+  const int rg = tid / D2;
+  const int n_rg = kFinalizeThreads / D2;
+  for (int j = rg; j < n_s * nr; j += n_rg) {
+    const float* w = ws + j * kRChunk;
+    float ax = 0.f, ay = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < kRChunk; ++c) {
+      const float2 b = __bfloat1622float2(bs[c * D2 + dp]);
+      ax = fmaf(w[c], b.x, ax);
+      ay = fmaf(w[c], b.y, ay);
     }
-    __syncthreads();
-    // Value basis of this KV head: each thread owns two adjacent output dims (one bf16x2 load per
-    // component) and a slice of the components; slices are summed through shared memory.
-    float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-    const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(
-        p.basis_v + static_cast<int64_t>(p.layer) * R * p.n_cols + kvh * D + 2 * d2);
-    const int64_t bstride = p.n_cols / 2;
-#pragma unroll 4
-    for (int r = part; r < R; r += parts) {
-      const float2 b = __bfloat1622float2(bv[static_cast<int64_t>(r) * bstride]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (j < G) {
-          const float wv = w[j * R + r];
-          acc[j][0] += wv * b.x;
-          acc[j][1] += wv * b.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j < G) {
-        red[(part * G + j) * D + 2 * d2] = acc[j][0];
-        red[(part * G + j) * D + 2 * d2 + 1] = acc[j][1];
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x < D) {
-      const float mean = __bfloat162float(p.mean_v[static_cast<int64_t>(s) * p.mean_seq_stride +
-                                                   static_cast<int64_t>(p.layer) * p.n_cols + kvh * D + d]);
-      const __nv_bfloat16* vex = p.exact_v + (static_cast<int64_t>(s) * n_kv + kvh) * p.n_exact * D + d;
-      for (int j = 0; j < G; ++j) {
-        const int hq = kvh * G + j;
-        const int row = hq * p.q_len + qi - p.row_begin;
-        if (row < 0 || row >= p.n_rows) continue;
-        float o = 0.f;
-        for (int q2 = 0; q2 < parts; ++q2) o += red[(q2 * G + j) * D + d];
-        const int64_t srow = (static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi;
-        o += mean * p.row_stats[srow * 4 + 2];
-        const float* pe = p.p_exact + srow * p.n_exact;
-        // Exact probabilities are kept unrounded (question-time scoring sums them); the value product uses
-        // them rounded to the cache dtype, as the reference does (compressed_attention.py:128, 135).
-        for (int e = 0; e < p.n_exact; ++e)
-          o += __bfloat162float(__float2bfloat16_rn(pe[e])) * __bfloat162float(vex[static_cast<int64_t>(e) * D]);
-        const int64_t oi = ((static_cast<int64_t>(s) * p.q_len + qi) * p.n_q_heads + hq) * D + d;
-        if (p.out_f32)
-          static_cast<float*>(p.out)[oi] = o;
-        else
-          static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
-      }
-    }
-    __syncthreads();
+    const int s = s0 + j / nr, rr = j % nr;
+    float2* dst = reinterpret_cast<float2*>(
+        p.vpart + ((static_cast<int64_t>(chunk) * p.n_seq + s) * p.n_rows_pad + (rlo - p.row_begin + rr)) * D);
+    dst[dp] = make_float2(ax, ay);
   }
 }
 
+// One CTA per (conversation, KV head); a thread per output dim of every row of the head.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const FinalizeParams p, int n_chunks) {
+  const int G = p.q_per_kv;
+  const int n_kv = p.n_q_heads / G;
+  const int s = blockIdx.x / n_kv, kvh = blockIdx.x % n_kv;
+  const int D = p.head_dim;
+  const int rlo = max(p.row_begin, kvh * G * p.q_len);
+  const int rhi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  for (int i = threadIdx.x; i < (rhi - rlo) * D; i += blockDim.x) {
+    const int row = rlo + i / D, d = i % D;
+    const int lr = row - p.row_begin;
+    const int hq = row / p.q_len, qi = row % p.q_len;
+    // Chunks summed in a fixed order with independent loads in flight.
+    const float* vp = p.vpart + (static_cast<int64_t>(s) * p.n_rows_pad + lr) * D + d;
+    const int64_t cstride = static_cast<int64_t>(p.n_seq) * p.n_rows_pad * D;
+    float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int ch = 0;
+    for (; ch + 8 <= n_chunks; ch += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) part[u] += vp[(ch + u) * cstride];
+    }
+    float tail = 0.f;
+    for (; ch < n_chunks; ++ch) tail += vp[ch * cstride];
+    float o = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7])) + tail;
+    const int64_t srow = (static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi;
+    const float mean = __bfloat162float(
+        p.mean_v[static_cast<int64_t>(s) * p.mean_seq_stride + static_cast<int64_t>(p.layer) * p.n_cols + kvh * D + d]);
+    o += mean * p.row_stats[srow * 4 + 2];
+    // Exact probabilities are kept unrounded (question-time scoring sums them); the value product uses
+    // them rounded to the cache dtype, as the reference does (compressed_attention.py:128, 135).
+    const float* pe = p.p_exact + srow * p.n_exact;
+    const __nv_bfloat16* vex = p.exact_v + (static_cast<int64_t>(s) * n_kv + kvh) * p.n_exact * D + d;
+    float ex[4] = {0.f, 0.f, 0.f, 0.f};
+    int e = 0;
+    for (; e + 4 <= p.n_exact; e += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        ex[u] += __bfloat162float(__float2bfloat16_rn(pe[e + u])) *
+                 __bfloat162float(vex[static_cast<int64_t>(e + u) * D]);
+    }
+    float ex_tail = 0.f;
+    for (; e < p.n_exact; ++e)
+      ex_tail += __bfloat162float(__float2bfloat16_rn(pe[e])) * __bfloat162float(vex[static_cast<int64_t>(e) * D]);
+    o += ((ex[0] + ex[1]) + (ex[2] + ex[3])) + ex_tail;
+    const int64_t oi = ((static_cast<int64_t>(s) * p.q_len + qi) * p.n_q_heads + hq) * D + d;
+    if (p.out_f32)
+      static_cast<float*>(p.out)[oi] = o;
+    else
+      static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
+  }
+}
+
+int finalize_chunks(int r_v) { return (r_v + kRChunk - 1) / kRChunk; }
+
 int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
-  if (p.q_per_kv > 4 || p.head_dim > 256 || kFinalizeThreads % p.head_dim != 0) return kDkvErrConfig;
-  const int parts = kFinalizeThreads / (p.head_dim / 2);
-  const int smem = (p.q_per_kv * p.r_v + parts * p.q_per_kv * p.head_dim) * 4;
-  if (smem > 227 * 1024) return kDkvErrConfig;
-  if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (p.head_dim % 64 != 0 || p.head_dim > 256 || p.q_per_kv < 1 || p.n_q_heads % p.q_per_kv != 0 ||
+      p.vpart == nullptr || p.item_groups % 2 != 0 || p.n_rows > p.n_rows_pad)
+    return kDkvErrConfig;
+  if (p.n_seq == 0 || p.n_rows == 0) return kDkvOk;
+  // Rows of one KV head inside this call: at most q_per_kv * q_len and at most n_rows.
+  const int nr_max = min(p.n_rows, p.q_per_kv * p.q_len);
+  const int basis_bytes = kRChunk * p.head_dim / 2 * 4;
+  const int per_seq = nr_max * kRChunk * 4;
+  const int seq_block = min(kSeqBlock, (200 * 1024 - basis_bytes) / per_seq);
+  if (seq_block < 1) return kDkvErrConfig;
+  const int smem = basis_bytes + seq_block * per_seq;
+  if (cudaFuncSetAttribute(vbasis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kDkvErrCuda;
-  const int grid = p.n_seq * (p.n_q_heads / p.q_per_kv);
-  if (grid == 0) return kDkvOk;
-  finalize_kernel<<<grid, kFinalizeThreads, smem, stream>>>(p);
+  const int n_chunks = finalize_chunks(p.r_v);
+  const int n_kv = p.n_q_heads / p.q_per_kv;
+  vbasis_kernel<<<dim3(n_chunks, n_kv, (p.n_seq + seq_block - 1) / seq_block), kFinalizeThreads, smem, stream>>>(
+      p, seq_block);
+  if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
+  combine_kernel<<<p.n_seq * n_kv, kCombineThreads, 0, stream>>>(p, n_chunks);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

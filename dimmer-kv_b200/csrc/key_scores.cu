@@ -52,31 +52,35 @@ struct KeySmem {
 // Walks the (item, group) sequence of this CTA; the producer keeps two of these (code blocks, basis
 // tiles) and the decode and MMA roles one each, so every role sees the same order.
 struct GroupCursor {
-  int it;           // index into p.items (strided by gridDim.x)
+  ItemRange ir;     // this CTA's items
+  int k;            // position in ir
   int gi;           // group within the item's tile
   int n_groups, group_base, nblk;
 
+  __device__ __forceinline__ GroupCursor(const ItemRange& r) : ir(r), k(r.k), gi(0), n_groups(0), group_base(0), nblk(0) {}
+
   __device__ __forceinline__ void load(const KeyScoreParams& p, int nblocks) {
-    while (it < p.n_items) {
+    while (k < ir.end) {
+      const int it = ir.at(k);
+      if (it < 0) {
+        record_error(p.status, kErrBadDescriptor);
+        k = ir.end;
+        return;
+      }
       const int item = p.items[it];
       const TileDesc& t = p.tiles[item / nblocks];
       n_groups = t.n_groups;
       group_base = t.group_base;
       nblk = item % nblocks;
       if (n_groups > 0) return;
-      it += gridDim.x;
+      k += ir.step;
     }
   }
-  __device__ __forceinline__ void begin(const KeyScoreParams& p, int nblocks) {
-    it = blockIdx.x;
-    gi = 0;
-    load(p, nblocks);
-  }
-  __device__ __forceinline__ bool done(const KeyScoreParams& p) const { return it >= p.n_items; }
+  __device__ __forceinline__ bool done() const { return k >= ir.end; }
   __device__ __forceinline__ void advance(const KeyScoreParams& p, int nblocks) {
     if (++gi >= n_groups) {
       gi = 0;
-      it += gridDim.x;
+      k += ir.step;
       load(p, nblocks);
     }
   }
@@ -120,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nblocks = p.n_cols / NB;
+  const ItemRange items(p.cta_begin, p.item_order, p.n_items);
 
   if (tid == 0) {
     for (int i = 0; i < kStagesC; ++i) {
@@ -148,14 +153,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tensormap(&bmap);
-      GroupCursor cc, cb;
-      cc.begin(p, nblocks);
-      cb.begin(p, nblocks);
+      GroupCursor cc(items), cb(items);
+      cc.load(p, nblocks);
+      cb.load(p, nblocks);
       uint32_t c_iter = 0, b_iter = 0;
       uint64_t idle_since = 0;
-      while ((!cc.done(p) || !cb.done(p)) && !*abort_flag) {
+      while ((!cc.done() || !cb.done()) && !*abort_flag) {
         bool progress = false;
-        if (!cc.done(p)) {
+        if (!cc.done()) {
           const int cs = c_iter % kStagesC;
           if (c_iter < kStagesC || mbar_test_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1)) {
             const GroupDesc* gd = &p.groups[cc.group_base + cc.gi];
@@ -174,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             progress = true;
           }
         }
-        if (!cb.done(p)) {
+        if (!cb.done()) {
           const int sb = b_iter % kStagesB;
           if (b_iter < kStagesB || mbar_test_wait(&b_empty[sb], ((b_iter / kStagesB) - 1) & 1)) {
             const uint32_t group = __ldg(&p.groups[cb.group_base + cb.gi].group);
@@ -204,7 +209,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t a_iter = 0, b_iter = 0, item_iter = 0;
-      for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+      for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+        const int it = items.at(k);
+        if (it < 0) {
+          record_error(p.status, kErrBadDescriptor);
+          *abort_flag = 1;
+          break;
+        }
         const int item = p.items[it];
         const TileDesc tile = p.tiles[item / nblocks];
         if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
@@ -251,7 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = u & 127;
     const int h = u >> 7;
     uint32_t c_iter = 0, a_iter = 0;
-    for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+    for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+      const int it = items.at(k);
+      if (it < 0) {
+        record_error(p.status, kErrBadDescriptor);
+        *abort_flag = 1;
+        break;
+      }
       const int item = p.items[it];
       const TileDesc tile = p.tiles[item / nblocks];
       for (int gi = 0; gi < tile.n_groups; ++gi) {
@@ -291,7 +308,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int head_half = (warp - 10) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t item_iter = 0;
-    for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+    for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+      const int it = items.at(k);
+      if (it < 0) {
+        record_error(p.status, kErrBadDescriptor);
+        *abort_flag = 1;
+        break;
+      }
       const int item = p.items[it];
       const int ti = item / nblocks, nblk = item % nblocks;
       const TileDesc tile = p.tiles[ti];

@@ -59,7 +59,10 @@ extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_sc
   const size_t exact_bytes = align256(rows * static_cast<size_t>(args->n_exact) * sizeof(float));
   const size_t partial_bytes = align256(static_cast<size_t>(args->n_v_items) * args->rows_pad *
                                         args->v_item_groups * 64 * sizeof(float));
-  const size_t total = scores_bytes + stats_bytes + exact_bytes + partial_bytes;
+  const int64_t vpart_floats = dkv_vpart_floats(args->v_width, args->n_seq, args->rows_pad, args->head_dim);
+  if (vpart_floats < 0) return DKV_ERR_ARGS;
+  const size_t vpart_bytes = align256(static_cast<size_t>(vpart_floats) * sizeof(float));
+  const size_t total = scores_bytes + stats_bytes + exact_bytes + partial_bytes + vpart_bytes;
   if (total > kStaticScratchBytes) return DKV_ERR_SCRATCH;
   void* base = nullptr;
   const int rc = static_scratch_address(&base);
@@ -70,5 +73,6 @@ extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_sc
   a.row_stats = reinterpret_cast<float*>(p + scores_bytes);
   a.p_exact = reinterpret_cast<float*>(p + scores_bytes + stats_bytes);
   a.partial = reinterpret_cast<float*>(p + scores_bytes + stats_bytes + exact_bytes);
+  a.vpart = reinterpret_cast<float*>(p + scores_bytes + stats_bytes + exact_bytes + partial_bytes);
   return dkv_attend_layer(&a, stream);
 }

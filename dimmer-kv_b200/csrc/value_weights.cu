@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   const uint32_t idesc = idesc_f16(128, NR, true, /*a_mn=*/true, /*b_mn=*/false);
   const int item_cols = p.item_groups * 64;
   const int n_pairs = p.item_groups / 2;
+  const ItemRange items(p.cta_begin, p.item_order, p.n_items);
 
   if (tid == 0) {
     for (int i = 0; i < kCodeSlots; ++i) {
@@ -114,7 +115,13 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
     // ------------------------------------------------------------ producer: descriptors, code blocks
     if (lane == 0) {
       uint32_t c_iter = 0, d_iter = 0;
-      for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+      for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+        const int it = items.at(k);
+        if (it < 0) {
+          record_error(p.status, kErrBadDescriptor);
+          *abort_flag = 1;
+          break;
+        }
         const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2];
         for (int t = tb; t < te && !*abort_flag; ++t) {
           const int d0 = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
@@ -166,7 +173,13 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
-      for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+      for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+        const int it = items.at(k);
+        if (it < 0) {
+          record_error(p.status, kErrBadDescriptor);
+          *abort_flag = 1;
+          break;
+        }
         const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
         if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
           *abort_flag = 1;
@@ -226,7 +239,13 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
     const int r = u & 127;  // token row (decode) / token column (P)
     const int h = u >> 7;   // component half (decode) / row half (P)
     uint32_t c_iter = 0, a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
-    for (int it = blockIdx.x; it < p.n_items && !*abort_flag; it += gridDim.x) {
+    for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+      const int it = items.at(k);
+      if (it < 0) {
+        record_error(p.status, kErrBadDescriptor);
+        *abort_flag = 1;
+        break;
+      }
       const int s = p.items[4 * it], tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
       const int64_t m_s = p.seq_m[s];
       const float* sc = p.scores + p.seq_score_off[s];

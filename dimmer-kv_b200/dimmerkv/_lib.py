@@ -22,7 +22,7 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
 
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
-           "dkv_version", "dkv_status_string")
+           "dkv_vpart_floats", "dkv_version", "dkv_status_string")
 
 
 class AttendArgs(ctypes.Structure):
@@ -46,6 +46,8 @@ class AttendArgs(ctypes.Structure):
         ("out", c_void_p), ("out_f32", c_int32), ("status", c_void_p),
         ("k_max_planes", c_int32), ("v_max_planes", c_int32),
         ("v_item_ranges", c_void_p), ("v_tile_chunk", c_int32),
+        ("vpart", c_void_p),
+        ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
     ]
 
 
@@ -114,6 +116,8 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(st), c_void_p]
             fn.restype = c_int32
+        handle.dkv_vpart_floats.argtypes = [c_int32, c_int32, c_int32, c_int32]
+        handle.dkv_vpart_floats.restype = c_int64
         handle.dkv_version.argtypes = []
         handle.dkv_version.restype = c_int32
         handle.dkv_status_string.argtypes = [c_int32]

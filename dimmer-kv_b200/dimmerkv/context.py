@@ -18,7 +18,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .planes import GROUP, KIND_PROGRESSIVE, PackedStream, StreamCodes, pack_streams
+from .planes import GROUP, KIND_PROGRESSIVE, WORD_COMPONENT, PackedStream, StreamCodes, pack_streams
 
 
 @dataclass
@@ -74,12 +74,14 @@ class ColdTier:
 
 
 def plane_words(codes: torch.Tensor) -> torch.Tensor:
-    """uint8 codes [N, G, 64] -> int64 [N, G, 8]: plane j holds bit (7 - j) of every component."""
+    """uint8 codes [N, G, 64] -> int64 [N, G, 8]: plane j holds bit (7 - j) of every component, in the
+    plane-word bit order of the packed stream (planes.WORD_COMPONENT)."""
     n, g, _ = codes.shape
     weights = (2 ** torch.arange(8, device=codes.device, dtype=torch.int32)).to(torch.int32)
+    word_component = torch.tensor(WORD_COMPONENT, dtype=torch.int64, device=codes.device)
     out = torch.empty(n, g, 8, dtype=torch.int64, device=codes.device)
     for j in range(8):
-        bits = ((codes.to(torch.int32) >> (7 - j)) & 1).view(n, g, 8, 8)
+        bits = ((codes[..., word_component].to(torch.int32) >> (7 - j)) & 1).view(n, g, 8, 8)
         out[:, :, j] = (bits * weights).sum(dim=-1).to(torch.uint8).contiguous().view(torch.int64).view(n, g)
     return out
 
@@ -95,6 +97,28 @@ def rope_tables(model, tokens: int, device, dtype=torch.bfloat16) -> tuple[torch
 
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
+
+
+def lpt_schedule(costs: list, n_cta: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Longest-processing-time-first assignment of work items to ``n_cta`` persistent CTAs: items in
+    descending cost, each to the CTA with the least load so far. Returns (cta_begin int32 [n_cta + 1],
+    item_order int32 [n]): CTA b processes item_order[cta_begin[b] : cta_begin[b + 1]], heaviest first."""
+    import heapq
+
+    n = len(costs)
+    n_cta = max(1, min(n_cta, n)) if n else 1
+    order = sorted(range(n), key=lambda i: -costs[i])
+    heap = [(0.0, b) for b in range(n_cta)]
+    lists = [[] for _ in range(n_cta)]
+    for i in order:
+        load, b = heapq.heappop(heap)
+        lists[b].append(i)
+        heapq.heappush(heap, (load + costs[i], b))
+    begin = [0]
+    for lst in lists:
+        begin.append(begin[-1] + len(lst))
+    flat = [i for lst in lists for i in lst]
+    return torch.tensor(begin, dtype=torch.int32), torch.tensor(flat, dtype=torch.int32)
 
 
 class CompressedBatch:
@@ -147,14 +171,10 @@ class CompressedBatch:
         self.sin = sin.to(self.device, dtype).contiguous()
         self.tile_chunk = tile_chunk
 
-        # Key work items: every tile x column block, heaviest first.
+        # Key work items: every tile x column block, scheduled over the SMs.
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.k_block = 512 if self.n_cols % 512 == 0 else (256 if self.n_cols % 256 == 0 else 128)
-        nblocks = self.n_cols // self.k_block
-        cost = self.keys.tile_blocks.repeat_interleave(nblocks) if self.keys.n_tiles else torch.zeros(0)
-        items = torch.arange(self.keys.n_tiles * nblocks, dtype=torch.int64)
-        if items.numel():
-            items = items[torch.sort(cost, descending=True, stable=True).indices]
-        self.k_items = items.to(torch.int32).to(self.device)
+        self._rebuild_key_items()
         self._v_items_cache: dict[int, tuple] = {}
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -169,12 +189,14 @@ class CompressedBatch:
         self._score_cache = None
 
     def _rebuild_key_items(self):
+        """Key work items (tile x column block), dealt to the CTAs by estimated cost (blocks to rebuild
+        plus the epilogue, about four blocks' worth), longest first to the least loaded CTA; k_items
+        holds them CTA by CTA and k_cta_begin delimits each CTA's list."""
         nblocks = self.n_cols // self.k_block
         cost = self.keys.tile_blocks.repeat_interleave(nblocks) if self.keys.n_tiles else torch.zeros(0)
-        items = torch.arange(self.keys.n_tiles * nblocks, dtype=torch.int64)
-        if items.numel():
-            items = items[torch.sort(cost, descending=True, stable=True).indices]
-        self.k_items = items.to(torch.int32).to(self.device)
+        cta_begin, order = lpt_schedule((cost.to(torch.float64) + 4.0).tolist(), self.sm_count)
+        self.k_items = order.to(self.device)  # item = tile * nblocks + column block
+        self.k_cta_begin = cta_begin.to(self.device)
 
     # ------------------------------------------------------------------ set-up helpers
     def _means(self, mean: torch.Tensor):
@@ -185,8 +207,11 @@ class CompressedBatch:
 
     def value_items(self, rows_pad: int):
         """Value work items for an MMA width: (items [n, 4], seq ranges [n_seq, 2], groups per item, n,
-        descriptor ranges [n, tile_chunk, 2]). An item is (conversation, run of <= tile_chunk value tiles,
-        first union group); for each of its tiles the descriptor range covering the item's groups."""
+        descriptor ranges [n, tile_chunk, 2], per-CTA schedule (cta_begin, item_order)). An item is
+        (conversation, run of <= tile_chunk value tiles, first union group); for each of its tiles the
+        descriptor range covering the item's groups. Runs are cut to a common estimated cost (decoded
+        groups plus the per-tile probability build) and dealt to the CTAs longest first, each to the
+        least loaded one, so that the persistent CTAs finish together."""
         if rows_pad in self._v_items_cache:
             return self._v_items_cache[rows_pad]
         item_groups = min(64, 2 * (512 // rows_pad))
@@ -196,30 +221,41 @@ class CompressedBatch:
         if gu:
             prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
         group_base = self.values.tiles[:, 4].to(torch.int64).cpu()
-        rows, ranges, spans = [], [], []
         tile_ranges = [[(t0, t1)] for t0, t1 in self.values.seq_tiles]
         for s, t0, t1 in self.extra_value_tiles:
             tile_ranges[s].append((t0, t1))
+        ranges_g = [(g0, min(g0 + item_groups, gu)) for g0 in range(0, gu, item_groups)]
+        # Estimated cost of (tile, group range): decoded groups + ~0.75 group of probability build.
+        counts = [(prefix[:, g1] - prefix[:, g0]).tolist() for g0, g1 in ranges_g]
+        total = sum(sum(c) for c in counts) + 0.75 * present.shape[0] * max(1, len(ranges_g))
+        target = max(4.0, total / (4 * self.sm_count))
+        rows, ranges, spans, costs = [], [], [], []
         for s, seq_ranges in enumerate(tile_ranges):
-          first = len(rows)
-          for t0, t1 in seq_ranges:
-            for c0 in range(t0, t1, self.tile_chunk):
-                c1 = min(t1, c0 + self.tile_chunk)
-                used = present[c0:c1].any(dim=0) if c1 > c0 else torch.zeros(0, dtype=torch.bool)
-                for g0 in range(0, int(used.numel()), item_groups):
-                    if bool(used[g0 : g0 + item_groups].any()):
-                        rows.append((s, c0, c1, g0))
-                        g1 = min(g0 + item_groups, gu)
-                        t = torch.arange(c0, c1)
-                        span = torch.zeros(self.tile_chunk, 2, dtype=torch.int64)
-                        span[: c1 - c0, 0] = group_base[t] + prefix[t, g0]
-                        span[: c1 - c0, 1] = group_base[t] + prefix[t, g1]
-                        spans.append(span)
-          ranges.append((first, len(rows)))
+            first = len(rows)
+            for t0, t1 in seq_ranges:
+                for ri, (g0, g1) in enumerate(ranges_g):
+                    cnt = counts[ri]
+                    c0, acc, used = t0, 0.0, False
+                    for t in range(t0, t1):
+                        acc += cnt[t] + 0.75
+                        used |= cnt[t] > 0
+                        if t + 1 == t1 or t + 1 - c0 == self.tile_chunk or acc >= target:
+                            if used:
+                                rows.append((s, c0, t + 1, g0))
+                                tt = torch.arange(c0, t + 1)
+                                span = torch.zeros(self.tile_chunk, 2, dtype=torch.int64)
+                                span[: t + 1 - c0, 0] = group_base[tt] + prefix[tt, g0]
+                                span[: t + 1 - c0, 1] = group_base[tt] + prefix[tt, g1]
+                                spans.append(span)
+                                costs.append(acc + 1.0)
+                            c0, acc, used = t + 1, 0.0, False
+            ranges.append((first, len(rows)))
         items = torch.tensor(rows if rows else [(0, 0, 0, 0)], dtype=torch.int32)[: len(rows)]
         span_t = torch.stack(spans) if spans else torch.zeros(1, self.tile_chunk, 2, dtype=torch.int64)
+        cta_begin, order = lpt_schedule(costs, self.sm_count)
         out = (items.to(self.device).contiguous(), torch.tensor(ranges, dtype=torch.int32).to(self.device),
-               item_groups, len(rows), span_t.to(torch.int32).to(self.device).contiguous())
+               item_groups, len(rows), span_t.to(torch.int32).to(self.device).contiguous(),
+               (cta_begin.to(self.device), order.to(self.device)))
         self._v_items_cache[rows_pad] = out
         return out
 
@@ -237,6 +273,9 @@ class CompressedBatch:
                 "p_exact": torch.empty(max(1, rows * max(1, n_exact)), dtype=torch.float32, device=self.device),
                 "partial": torch.empty(max(1, n_v_items * rows_pad * item_groups * GROUP), dtype=torch.float32,
                                        device=self.device),
+                "vpart": torch.empty(max(1, int(self.lib.dkv_vpart_floats(self.v_width, self.n_seq, rows_pad,
+                                                                          self.head_dim))),
+                                     dtype=torch.float32, device=self.device),
             }
             self._work = {key: w}
         return w
@@ -247,7 +286,7 @@ class CompressedBatch:
         q_len = query.shape[2]
         n_exact = key.shape[2]
         rows_pad = min(128, _round_up(self.q_heads * q_len, 16))
-        v_items, v_seq, item_groups, n_v, v_spans = self.value_items(rows_pad)
+        v_items, v_seq, item_groups, n_v, v_spans, (v_cta, v_order) = self.value_items(rows_pad)
         w = self._workspace(q_len, n_exact, rows_pad, n_v, item_groups)
         a = _lib.AttendArgs()
         ks, vs = self.keys, self.values
@@ -274,6 +313,9 @@ class CompressedBatch:
         a.out, a.out_f32, a.status = out.data_ptr(), int(out.dtype == torch.float32), self.status.data_ptr()
         a.k_max_planes, a.v_max_planes = ks.max_planes, vs.max_planes
         a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
+        a.vpart = w["vpart"].data_ptr()
+        a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
+        a.v_cta_begin, a.v_item_order, a.grid_v = v_cta.data_ptr(), v_order.data_ptr(), int(v_cta.numel()) - 1
         return a
 
     def attend_layer(self, layer: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,

@@ -10,7 +10,10 @@ plane plus a 4-byte (low, span) header per group holding at least one plane
 - per (tile, group) block: headers of the tokens holding >= 1 plane, then for every plane j one
   64-bit word per token holding it. Because tokens are sorted by precision, the holders of
   plane j are a suffix of the tile; ``first[j]`` records where it starts;
-- blocks are 16-byte aligned and sized for cp.async.bulk.
+- blocks are 16-byte aligned and sized for cp.async.bulk;
+- inside a plane word, component c sits at bit 32*(c // 32) + 8*(c % 4) + (c % 32) // 4: in each
+  32-bit half, byte k holds components k, k+4, ..., k+28. One rotate and one masked OR per four
+  components then drop a plane's bits into per-component bytes (the decoder, dkv_format.cuh).
 
 m = 16 planes stores a bf16 value bit by bit ("raw"), which is how the kvtc ladder's exact rung
 (scripts/kvtc.py:258-259) and any coefficient given only as a float are carried.
@@ -28,6 +31,8 @@ MAX_PLANES = 16
 KIND_PROGRESSIVE = 0
 KIND_LADDER = 1
 RAW = 16
+# WORD_COMPONENT[p]: the component stored at bit p of a plane word (the inverse of the bit order above).
+WORD_COMPONENT = [32 * (p // 32) + 4 * (p % 8) + (p % 32) // 8 for p in range(GROUP)]
 
 
 @dataclass
@@ -160,6 +165,7 @@ def pack_streams(convs: list[StreamCodes], union: torch.Tensor | None = None) ->
         code32[off // 4] = HDR[tok, grp]
     # Plane words, most significant plane first (in slices to bound the temporaries).
     weights = (2 ** torch.arange(8, device=device, dtype=torch.int32)).to(torch.int32)
+    word_component = torch.tensor(WORD_COMPONENT, dtype=torch.int64, device=device)
     chunk = 1 << 21
     for j in range(MAX_PLANES):
         tok_all, grp_all = torch.nonzero(P > j, as_tuple=True)
@@ -170,7 +176,8 @@ def pack_streams(convs: list[StreamCodes], union: torch.Tensor | None = None) ->
             t_ = tile_of[tok]
             m = P[tok, grp]
             shift = (m - 1 - j).to(torch.int32)
-            bits = (IDX[tok, grp].to(torch.int32) >> shift[:, None]) & 1                # [K, 64]
+            bits = (IDX[tok, grp].to(torch.int32) >> shift[:, None]) & 1                # [K, 64] by component
+            bits = bits[:, word_component]                                              # [K, 64] by word bit
             packed = (bits.view(-1, 8, 8) * weights).sum(dim=-1).to(torch.uint8)       # [K, 8]
             words = packed.contiguous().view(torch.int64).view(-1)
             off = offsets[t_, grp] + seg_off[j][t_, grp] + (row_of[tok] - first[j][t_, grp]) * 8

@@ -100,7 +100,19 @@ typedef struct dkv_attend_args {
   int32_t v_max_planes;          /* the same for the value stream */
   const int32_t* v_item_ranges;  /* [n_v_items][v_tile_chunk][2]: per tile, the descriptor range inside the item's groups */
   int32_t v_tile_chunk;          /* value tiles per item (at most) */
+  /* value-basis stage scratch: dkv_vpart_floats(v_width, n_seq, rows_pad, head_dim) floats */
+  float* vpart;
+  /* Optional static schedules (NULL: items are dealt round-robin over the grid). CTA b of the key
+   * (value) kernel processes items k_item_order[k_cta_begin[b] .. k_cta_begin[b+1]) (item order NULL:
+   * items k_cta_begin[b] .. k_cta_begin[b+1]); grid_k (grid_v) must then equal the number of lists. */
+  const int32_t* k_cta_begin;    /* [grid_k + 1] */
+  const int32_t* k_item_order;   /* [n_k_items] */
+  const int32_t* v_cta_begin;    /* [grid_v + 1] */
+  const int32_t* v_item_order;   /* [n_v_items] */
 } dkv_attend_args;
+
+/* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
+int64_t dkv_vpart_floats(int32_t v_width, int32_t n_seq, int32_t rows_pad, int32_t head_dim);
 
 /* One attention layer, all four stages below in order.
  * Replaces CompressedContext.attend (scripts/compressed_attention.py:113-137), batched over
@@ -127,7 +139,7 @@ int dkv_finalize(const dkv_attend_args* args, void* stream);
 /* dkv_attend_layer for callers that cannot allocate device memory. No counterpart in the reference.
  * Callers inside another framework's memory manager (which owns every device allocation and forbids
  * cudaMalloc / cudaFree) or in latency-critical loops pass the same arguments as to
- * dkv_attend_layer except the four scratch pointers (scores, row_stats, p_exact, partial), which are
+ * dkv_attend_layer except the five scratch pointers (scores, row_stats, p_exact, partial, vpart), which are
  * ignored; the scratch comes from a fixed 32 MiB array declared by the library in device memory.
  * n_scores = sum over conversations of n_q_heads * q_len * seq_m[s]. Returns DKV_ERR_SCRATCH, having
  * launched nothing, when the scratch would not fit. The first call on a device looks up the array's

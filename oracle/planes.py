@@ -17,11 +17,18 @@ Layout (per stream; all little-endian):
 A token's plane count m is the number of j with first[j] <= t. Plane j holds bit
 (m-1-j) of the m-bit index (most significant first). m = 16 stores the 16 bits of
 a bf16 value directly ("raw", the exact rung of the kvtc ladder).
+Bit order inside a plane word: component c sits at bit 32*(c // 32) + 8*(c % 4) + (c % 32) // 4,
+i.e. in each 32-bit half, byte k holds components k, k+4, ..., k+28 (bits 0..7).
 Decoding: progressive  v = low + (idx + 0.5) * mult / 2^m   (progressive.py:51-54)
           ladder       v = idx * mult + low                 (kvtc.py:78)
 """
 
 from __future__ import annotations
+
+
+def bit_of_component(c: int) -> int:
+    """Bit of the 64-bit plane word that holds component c (0..63)."""
+    return 32 * (c // 32) + 8 * (c % 4) + (c % 32) // 4
 
 import numpy as np
 
@@ -60,7 +67,7 @@ def unpack_tile_group(code: np.ndarray, gdesc: np.ndarray, n_tokens: int) -> tup
             w = int(words[i])
             shift = int(m[t]) - 1 - j
             for c in range(GROUP):
-                idx[t, c] |= ((w >> c) & 1) << shift
+                idx[t, c] |= ((w >> bit_of_component(c)) & 1) << shift
     values = np.zeros((n_tokens, GROUP), dtype=np.float32)
     for t in range(first[0], n_tokens):
         mt = int(m[t])
