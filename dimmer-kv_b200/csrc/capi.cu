@@ -104,10 +104,12 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   if (a->n_k_items == 0) return DKV_OK;
   const int n_cols = a->n_kv_heads * a->head_dim;
   const int nb = a->k_block_cols;
+  const bool pairs = a->k_pairs != nullptr;
   if ((nb != 128 && nb != 256 && nb != 512) || n_cols % nb != 0 || nb % a->head_dim != 0) return DKV_ERR_CONFIG;
+  if (pairs && nb != 512) return DKV_ERR_CONFIG;  // CTA pairs: 512 columns per item, 128-row basis boxes
   CUtensorMap map;
   rc = basis_map(a->k_basis, static_cast<uint64_t>(a->n_layers) * n_cols, static_cast<uint64_t>(a->k_width),
-                 nb > 256 ? 256u : static_cast<uint32_t>(nb), &map);
+                 pairs ? 128u : (nb > 256 ? 256u : static_cast<uint32_t>(nb)), &map);
   if (rc != DKV_OK) return rc;
   dkv::KeyScoreParams p{};
   p.code = a->k_code;
@@ -140,6 +142,14 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   p.item_order = a->k_item_order;
   if ((a->k_item_order != nullptr && a->k_cta_begin == nullptr) || (a->k_cta_begin != nullptr && a->grid_k <= 0))
     return DKV_ERR_ARGS;
+  p.pairs = a->k_pairs;
+  p.pair_groups = a->k_pair_groups;
+  if (pairs && a->k_pair_groups == nullptr) return DKV_ERR_ARGS;
+  if (pairs) {
+    // Two CTAs per cluster; grid_k counts the schedule's lists (one per cluster).
+    const int clusters = a->grid_k > 0 ? a->grid_k : sm_count() / 2;
+    return dkv::run_key_scores_pair(map, p, 2 * clusters, static_cast<cudaStream_t>(stream));
+  }
   const int grid = a->grid_k > 0 ? a->grid_k : (a->n_k_items < sm_count() ? a->n_k_items : sm_count());
   return dkv::run_key_scores(map, p, nb, grid, static_cast<cudaStream_t>(stream));
 }

@@ -97,18 +97,21 @@ struct ItemRange {
   int k, end, step, n_items;
   const int32_t* order;
 
-  __device__ __forceinline__ ItemRange(const int32_t* cta_begin, const int32_t* item_order, int n) {
+  __device__ __forceinline__ ItemRange(const int32_t* cta_begin, const int32_t* item_order, int n)
+      : ItemRange(cta_begin, item_order, n, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x)) {}
+  // List `b` of `nb` (a cluster of CTAs shares one list).
+  __device__ __forceinline__ ItemRange(const int32_t* cta_begin, const int32_t* item_order, int n, int b, int nb) {
     n_items = n;
     if (cta_begin != nullptr) {
-      k = max(0, __ldg(cta_begin + blockIdx.x));
-      end = __ldg(cta_begin + blockIdx.x + 1);
+      k = max(0, __ldg(cta_begin + b));
+      end = __ldg(cta_begin + b + 1);
       step = 1;
       order = item_order;
       if (order == nullptr) end = min(end, n);
     } else {
-      k = blockIdx.x;
+      k = b;
       end = n;
-      step = gridDim.x;
+      step = nb;
       order = nullptr;
     }
   }

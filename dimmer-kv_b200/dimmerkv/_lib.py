@@ -48,6 +48,7 @@ class AttendArgs(ctypes.Structure):
         ("v_item_ranges", c_void_p), ("v_tile_chunk", c_int32),
         ("vpart", c_void_p),
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
+        ("k_pairs", c_void_p), ("k_pair_groups", c_void_p),
     ]
 
 

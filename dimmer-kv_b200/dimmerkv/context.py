@@ -126,12 +126,14 @@ class CompressedBatch:
 
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
-                 device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None):
+                 device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None,
+                 pair_keys: bool = True):
         """``basis[kind]``: [F, F] (or [F, >= union]) float basis, columns = PCA components (the codec's
         ``stream.basis``); ``mean[kind]``: [F] shared or [n_conv, F] per conversation; ``cos/sin``:
         [positions, head_dim // 2] tables (``rope_tables``); ``union[kind]`` (optional) fixes the coefficient
         groups a stream covers (by default, the groups holding a plane for some token; a cold tier whose
-        refined tokens use more groups needs them all)."""
+        refined tokens use more groups needs them all); ``pair_keys`` runs the key kernel on CTA pairs
+        (two SMs per item, half the basis traffic each)."""
         if dtype != torch.bfloat16:
             raise NotImplementedError("the sm_100a kernels of this build compute in bf16 only")
         self.lib = _lib.lib()
@@ -173,7 +175,11 @@ class CompressedBatch:
 
         # Key work items: every tile x column block, scheduled over the SMs.
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.k_block = 512 if self.n_cols % 512 == 0 else (256 if self.n_cols % 256 == 0 else 128)
+        self.pair_keys = pair_keys and self.n_cols % 512 == 0
+        if self.pair_keys:
+            self.k_block = 512
+        else:
+            self.k_block = 512 if self.n_cols % 512 == 0 else (256 if self.n_cols % 256 == 0 else 128)
         self._rebuild_key_items()
         self._v_items_cache: dict[int, tuple] = {}
         self._work: dict = {}
@@ -189,12 +195,52 @@ class CompressedBatch:
         self._score_cache = None
 
     def _rebuild_key_items(self):
-        """Key work items (tile x column block), dealt to the CTAs by estimated cost (blocks to rebuild
-        plus the epilogue, about four blocks' worth), longest first to the least loaded CTA; k_items
-        holds them CTA by CTA and k_cta_begin delimits each CTA's list."""
+        """Key work items and their schedule. With CTA pairs (the default when the key columns split
+        into blocks of 512): neighbouring key tiles of a conversation are paired, an item is (pair,
+        block of 512 columns), and the lists go to the clusters of two CTAs. Otherwise an item is
+        (tile, block of k_block columns) for one CTA. Items are dealt longest first (estimated cost:
+        coefficient groups to rebuild plus the epilogue) to the least loaded list."""
+        tb = self.keys.tile_blocks if self.keys.n_tiles else torch.zeros(0, dtype=torch.int64)
+        if self.pair_keys:
+            ranges = [[(t0, t1)] for t0, t1 in self.keys.seq_tiles]
+            for s, t0, t1 in getattr(self, "_refined_key_tiles", []):
+                ranges[s].append((t0, t1))
+            pairs = []
+            for seq_ranges in ranges:
+                for t0, t1 in seq_ranges:
+                    for t in range(t0, t1, 2):
+                        pairs.append((t, t + 1 if t + 1 < t1 else -1))
+            nblocks = self.n_cols // 512
+            present = self.keys.present
+            gb = self.keys.tiles[:, 4].to(torch.int64).cpu()
+            prefix = torch.zeros(present.shape[0], present.shape[1] + 1, dtype=torch.int64)
+            prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
+            rows, entries, n_entries = [], [], 0
+            for t0, t1 in pairs:
+                p0 = present[t0]
+                p1 = present[t1] if t1 >= 0 else torch.zeros_like(p0)
+                groups = torch.nonzero(p0 | p1).flatten()
+                d0 = torch.where(p0[groups], gb[t0] + prefix[t0, groups], torch.full_like(groups, -1))
+                d1 = torch.where(p1[groups], gb[max(t1, 0)] + prefix[max(t1, 0), groups], torch.full_like(groups, -1))
+                rows.append((t0, t1, int(groups.numel()), n_entries))
+                n_entries += int(groups.numel())
+                entries.append(torch.stack([groups, d0, d1, torch.zeros_like(groups)], dim=1))
+            pair_t = torch.tensor(rows if rows else [(-1, -1, 0, 0)], dtype=torch.int32)
+            entry_t = torch.cat(entries).to(torch.int32) if entries else torch.zeros(1, 4, dtype=torch.int32)
+            self.k_pair_groups = entry_t.contiguous().to(self.device)
+            if rows:
+                cost = (pair_t[:, 2].to(torch.float64) + 4.0).repeat_interleave(nblocks)
+            else:
+                cost = torch.zeros(0, dtype=torch.float64)
+            cta_begin, order = lpt_schedule(cost.tolist(), max(1, self.sm_count // 2))
+            self.k_pairs = pair_t.to(self.device)
+            self.k_items = order.to(self.device)  # item = pair * nblocks + column block
+            self.k_cta_begin = cta_begin.to(self.device)
+            return
         nblocks = self.n_cols // self.k_block
-        cost = self.keys.tile_blocks.repeat_interleave(nblocks) if self.keys.n_tiles else torch.zeros(0)
+        cost = tb.repeat_interleave(nblocks) if self.keys.n_tiles else torch.zeros(0)
         cta_begin, order = lpt_schedule((cost.to(torch.float64) + 4.0).tolist(), self.sm_count)
+        self.k_pairs = None
         self.k_items = order.to(self.device)  # item = tile * nblocks + column block
         self.k_cta_begin = cta_begin.to(self.device)
 
@@ -315,6 +361,8 @@ class CompressedBatch:
         a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
         a.vpart = w["vpart"].data_ptr()
         a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
+        a.k_pairs = self.k_pairs.data_ptr() if self.k_pairs is not None else None
+        a.k_pair_groups = self.k_pair_groups.data_ptr() if self.k_pairs is not None else None
         a.v_cta_begin, a.v_item_order, a.grid_v = v_cta.data_ptr(), v_order.data_ptr(), int(v_cta.numel()) - 1
         return a
 
@@ -560,6 +608,15 @@ class CompressedBatch:
                         nt = (n + 127) // 128
                         self.extra_value_tiles.append((s, t, t + nt))
                         t += nt
+            if kind == "key":
+                t = first_new_tile
+                refined_tiles = getattr(self, "_refined_key_tiles", [])
+                for s, n in enumerate(per_seq):
+                    if n:
+                        nt = (n + 127) // 128
+                        refined_tiles.append((s, t, t + nt))
+                        t += nt
+                self._refined_key_tiles = refined_tiles
         # Score-order lengths grow by the refined tokens.
         k_counts = [sel.numel() for sel in selected]
         tok = self.keys.n_tokens - sum(k_counts)

@@ -109,6 +109,15 @@ typedef struct dkv_attend_args {
   const int32_t* k_item_order;   /* [n_k_items] */
   const int32_t* v_cta_begin;    /* [grid_v + 1] */
   const int32_t* v_item_order;   /* [n_v_items] */
+  /* Key kernel on CTA pairs (two SMs of a TPC per item, half the basis traffic per SM): [n_pairs][4] =
+   * key tile of the even CTA, key tile of the odd CTA (-1: none), number of distinct groups of the two
+   * tiles, first entry in k_pair_groups. k_items = pair * (n_cols / 512) + column block,
+   * k_block_cols = 512, and a schedule (if any) with one list per pair of CTAs (grid_k = number of
+   * lists). NULL: one CTA per item. */
+  const int32_t* k_pairs;
+  /* [entries][4]: per pair, the sorted union of its tiles' groups as (union group, k_groups index of
+   * the even CTA's block or -1, of the odd CTA's block or -1, 0). */
+  const int32_t* k_pair_groups;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
