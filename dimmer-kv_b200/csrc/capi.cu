@@ -173,6 +173,8 @@ int dkv_softmax_stats(const dkv_attend_args* a, void* stream) {
   p.scaling = a->scaling;
   p.row_stats = a->row_stats;
   p.p_exact = a->p_exact;
+  if (a->softmax_mode < 0 || a->softmax_mode > 2) return DKV_ERR_ARGS;
+  p.mode = a->softmax_mode;
   return dkv::run_softmax_stats(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -265,7 +267,23 @@ int64_t dkv_vpart_floats(int32_t v_width, int32_t n_seq, int32_t rows_pad, int32
   return static_cast<int64_t>(dkv::finalize_chunks(v_width)) * n_seq * rows_pad * head_dim;
 }
 
+int dkv_attend_tail(const dkv_attend_args* a, void* stream) {
+  int rc = check_common(a);
+  if (rc != DKV_OK) return rc;
+  const int rows = a->n_q_heads * a->q_len;
+  if (a->rows_pad < 16 || a->rows_pad > 128 || a->rows_pad % 16) return DKV_ERR_CONFIG;
+  for (int r0 = 0; r0 < rows; r0 += a->rows_pad) {
+    const int n = rows - r0 < a->rows_pad ? rows - r0 : a->rows_pad;
+    rc = value_weights_rows(a, r0, n, stream);
+    if (rc != DKV_OK) return rc;
+    rc = finalize_rows(a, r0, n, stream);
+    if (rc != DKV_OK) return rc;
+  }
+  return DKV_OK;
+}
+
 int dkv_attend_layer(const dkv_attend_args* a, void* stream) {
+  if (a != nullptr && a->softmax_mode != 0) return DKV_ERR_ARGS;  // split-K runs the stages one by one
   int rc = dkv_key_scores(a, stream);
   if (rc != DKV_OK) return rc;
   rc = dkv_softmax_stats(a, stream);

@@ -63,7 +63,11 @@ struct SoftmaxParams {
   float scaling;
   float* row_stats;               // [n_seq][n_q_heads][q_len][4]: max, 1/sum, compressed mass, 0
   float* p_exact;                 // [n_seq][n_q_heads][q_len][n_exact], fp32 (unrounded)
+  int mode;                       // kSoftmaxFull, kSoftmaxLocal or kSoftmaxGlobal
 };
+constexpr int kSoftmaxFull = 0;
+constexpr int kSoftmaxLocal = 1;   // row_stats <- (max, sum of exponentials) of this shard
+constexpr int kSoftmaxGlobal = 2;  // row_stats[0..1] hold the merged (max, 1 / sum); fills mass, p_exact
 int run_softmax_stats(const SoftmaxParams& p, cudaStream_t stream);
 
 // Probability-weighted value coefficients (value_weights.cu).

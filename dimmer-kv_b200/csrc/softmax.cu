@@ -5,6 +5,10 @@
 // Instead of materialising probabilities for the compressed tokens, each (conversation, query
 // head, query row) gets its row maximum, 1 / sum of exponentials and the probability mass of the
 // compressed part; the exact tokens' probabilities are written out (there are few of them).
+// Split-K over GPUs (one conversation's tokens sharded): mode kSoftmaxLocal writes each row's local
+// (max, sum of exponentials); after the shards are merged into the global (max, 1 / sum), mode
+// kSoftmaxGlobal computes the compressed mass and the exact-token probabilities with them, so every
+// shard rounds its probabilities exactly as one softmax over all tokens would.
 #include <cfloat>
 #include <cmath>
 #include "dkv_kernels.h"
@@ -98,11 +102,24 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const So
     float mx = mc;
     for (int e = 0; e < p.n_exact; ++e) mx = fmaxf(mx, se[e]);
     float sum = (mc == -INFINITY) ? 0.f : lc * expf(mc - mx);
-    for (int e = 0; e < p.n_exact; ++e) sum += expf(se[e] - mx);
+    for (int e = 0; e < p.n_exact; ++e) sum += (mx == -INFINITY) ? 0.f : expf(se[e] - mx);
+    float* st = p.row_stats + static_cast<int64_t>(row) * 4;
+    if (p.mode == kSoftmaxLocal) {
+      // Split-K, first pass: this shard's (max, sum of exponentials); the caller merges the shards.
+      st[0] = mx;
+      st[1] = sum;
+      st[2] = 0.f;
+      st[3] = 0.f;
+    } else if (p.mode == kSoftmaxGlobal) {
+      // Split-K, second pass: the merged (max, 1 / sum) over every shard.
+      mx = st[0];
+      sum = 1.f / st[1];
+    }
     red_m[0] = mx;
     red_l[0] = 1.f / sum;
   }
   __syncthreads();
+  if (p.mode == kSoftmaxLocal) return;
   const float mx = red_m[0], inv = red_l[0];
   // The reference casts the probabilities to the cache dtype before the value products
   // (compressed_attention.py:127-128, 130): the compressed mass used by the mean term is a sum of

@@ -21,6 +21,7 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
                  107: "timed out draining async work", 110: "descriptor out of bounds"}
 
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
+           "dkv_attend_tail",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
            "dkv_vpart_floats", "dkv_version", "dkv_status_string")
 
@@ -48,7 +49,7 @@ class AttendArgs(ctypes.Structure):
         ("v_item_ranges", c_void_p), ("v_tile_chunk", c_int32),
         ("vpart", c_void_p),
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
-        ("k_pairs", c_void_p), ("k_pair_groups", c_void_p),
+        ("k_pairs", c_void_p), ("k_pair_groups", c_void_p), ("softmax_mode", c_int32),
     ]
 
 
@@ -107,7 +108,8 @@ def lib():
             raise DimmerKVError(f"{LIB_PATH} is missing: build it with dimmer-kv_b200/build_lib.py "
                                 "(there is no CPU fallback)")
         handle = ctypes.CDLL(str(LIB_PATH))
-        for name in ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize"):
+        for name in ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
+                     "dkv_attend_tail"):
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(AttendArgs), c_void_p]
             fn.restype = c_int32

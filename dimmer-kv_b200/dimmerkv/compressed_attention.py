@@ -40,12 +40,19 @@ class CompressedContext:
                                                 codec.last_choice[kind].to(device))
         conv = ConversationCodes(start, end, _to(codes["key"], device), _to(codes["value"], device))
         cos, sin = rope_tables(model, max(tokens, end) + 1, device, dtype)
+        # A progressive codec's cold tier can refine any group: cover them all.
+        self._progressive = getattr(codec, "last_cache", None)
+        union = None
+        if self._progressive is not None:
+            groups = torch.arange(codes["key"].planes.shape[1])
+            union = {"key": groups, "value": groups}
         self.batch = CompressedBatch(
             [conv], layers=self.layers, kv_heads=self.heads, head_dim=self.head_dim,
             q_heads=model.config.num_attention_heads,
             basis={k: codec.streams[k].basis for k in ("key", "value")},
             mean={k: codec.streams[k].mean for k in ("key", "value")},
-            cos=cos, sin=sin, device=device, dtype=dtype)
+            cos=cos, sin=sin, device=device, dtype=dtype, union=union)
+        self._cold = None
         # Exact tokens in an ordinary cache: sinks then the recent window (compressed_attention.py:86-88).
         exact_keys = [torch.cat([k[..., :start, :], k[..., end:, :]], dim=2) for k in keys]
         exact_values = [torch.cat([v[..., :start, :], v[..., end:, :]], dim=2) for v in values]
@@ -68,6 +75,31 @@ class CompressedContext:
     def attend(self, module, query, key, value, attention_mask, scaling):
         """Same contract as an HF attention function: returns (output [B, T, H, D], None)."""
         return self.batch.attend(module, query, key, value, attention_mask, scaling)
+
+    # ----- question time (progressive codes): question_importance + top-k + refine on the codes
+    def question_importance(self, tail_ids: torch.Tensor, context_length: int) -> torch.Tensor:
+        """question_importance (progressive.py:239-254) over the packed planes: [context_length]."""
+        from .question import question_importance_direct
+
+        ids = tail_ids if tail_ids.dim() == 2 else tail_ids[None]
+        return question_importance_direct(self.model, self.batch, self.exact_cache, ids.to(self.batch.device),
+                                          [context_length])[0]
+
+    def select_top(self, fraction: float) -> torch.Tensor:
+        """Top max(1, round(fraction * middle)) middle tokens by the last question_importance, ties by
+        lowest position (methods.py:246-247); ascending positions."""
+        from .question import refine_count
+
+        return self.batch.select_top([refine_count(fraction, self.end - self.start)])[0]
+
+    def refine(self, tokens: torch.Tensor) -> int:
+        """Merge the cold planes of middle ``tokens`` (absolute positions) into the context
+        (ProgressiveCache.refine, progressive.py:224-236); returns the bytes fetched."""
+        if self._progressive is None:
+            raise RuntimeError("refine needs a progressive codec (prog@) with a cold tier")
+        if self._cold is None:
+            self._cold = self._progressive.cold_tiers()
+        return self.batch.refine([tokens.to(torch.int64)], [self._cold])
 
 
 def _to(t: TokenCodes, device) -> TokenCodes:

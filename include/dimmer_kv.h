@@ -118,6 +118,11 @@ typedef struct dkv_attend_args {
   /* [entries][4]: per pair, the sorted union of its tiles' groups as (union group, k_groups index of
    * the even CTA's block or -1, of the odd CTA's block or -1, 0). */
   const int32_t* k_pair_groups;
+  /* dkv_softmax_stats mode: 0 one softmax over this call's tokens; for one conversation split over GPUs
+   * (split-K), 1 writes row_stats[0..1] = this shard's (max, sum of exponentials), and 2 takes
+   * row_stats[0..1] = the merged (max, 1 / sum) and fills the compressed mass and p_exact.
+   * dkv_attend_layer requires 0. */
+  int32_t softmax_mode;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
@@ -140,6 +145,10 @@ int dkv_softmax_stats(const dkv_attend_args* args, void* stream);
 /* Stage 3: probabilities (bf16, as the reference rounds them) times value coefficients (tcgen05).
  * Replaces the per-block einsum of compressed_attention.py:132-133. */
 int dkv_value_weights(const dkv_attend_args* args, void* stream);
+
+/* Stages 3 and 4 for every chunk of rows_pad rows (the part of dkv_attend_layer after the softmax
+ * statistics; split-K callers run it after merging the shards' statistics). */
+int dkv_attend_tail(const dkv_attend_args* args, void* stream);
 
 /* Stage 4: value basis per head + mean + exact-token values -> output.
  * Replaces compressed_attention.py:130-131, 134-137. */

@@ -124,6 +124,39 @@ class OracleContext:
         return output
 
 
+def attend_split(ctx: "OracleContext", layer: int, query, key, value, attention_mask, scaling, stats=None):
+    """Split-K restatement over a shard of the compressed tokens (this context) plus, on the shard that
+    holds them, the exact tokens. stats=None: per-row (max, sum of exponentials) [rows, 2], rows in
+    (batch, query head, query row) order. stats=(max, 1 / sum) merged over all shards: the shard's share
+    of the layer output [B, q, Hq, D], probabilities normalised globally and rounded as in attend."""
+    f = ctx.f
+    q = round_dtype(np.asarray(query, np.float32), ctx.dtype).astype(f)
+    k = round_dtype(np.asarray(key, np.float32), ctx.dtype).astype(f)
+    v = round_dtype(np.asarray(value, np.float32), ctx.dtype).astype(f)
+    batch, q_heads, q_len, dim = q.shape
+    groups = q_heads // ctx.heads
+    gq = q.reshape(batch, ctx.heads, groups, q_len, dim)
+    scores_c = np.einsum("bhgqd,hnd->bhgqn", gq, ctx.keys(layer)) * scaling
+    scores_e = np.einsum("bhgqd,bhnd->bhgqn", gq, k) * scaling
+    if attention_mask is not None and scores_e.shape[-1]:
+        scores_e = scores_e + np.asarray(attention_mask, f)[:, :, None]
+    middle = scores_c.shape[-1]
+    allsc = np.concatenate([scores_c, scores_e], axis=-1)
+    if stats is None:
+        mx = allsc.max(axis=-1)
+        return np.stack([mx, np.exp(allsc - mx[..., None]).sum(axis=-1)], axis=-1).reshape(-1, 2)
+    m_g, inv_g = (np.asarray(x, f).reshape(batch, ctx.heads, groups, q_len, 1) for x in stats)
+    probs = np.exp(allsc - m_g) * inv_g
+    p_c = round_dtype(probs[..., :middle].astype(np.float32), ctx.dtype).astype(f)
+    p_e = round_dtype(probs[..., middle:].astype(np.float32), ctx.dtype).astype(f)
+    out_c = p_c.sum(axis=-1, keepdims=True) * ctx.mean["value"][layer].reshape(1, ctx.heads, 1, 1, dim)
+    layer_basis = ctx.basis["value"][:, layer].reshape(-1, ctx.heads, ctx.head_dim)
+    weighted = np.einsum("bhgqn,nr->bhgqr", p_c[..., ctx.value_index], ctx.coeff["value"][ctx.rows["value"]])
+    out_c = out_c + np.einsum("bhgqr,rhd->bhgqd", weighted, layer_basis)
+    out_e = np.einsum("bhgqn,bhnd->bhgqd", p_e, v)
+    return (out_c + out_e).reshape(batch, q_heads, q_len, dim).transpose(0, 2, 1, 3)
+
+
 def importance_from_probs(p_c: np.ndarray, p_e: np.ndarray, order: np.ndarray, start: int,
                           exact_positions: np.ndarray, context_length: int) -> np.ndarray:
     """One layer's contribution to question_importance (dimmer.py:62-75, progressive.py:254).

@@ -125,3 +125,34 @@ def oracle_question_importance(model, ctx: OracleContext, inputs: dict, fix: dic
         model(input_ids=ids, past_key_values=exact_cache(inputs, fix, model, device),
               position_ids=torch.arange(tokens, tokens + ids.shape[1], device=device)[None])
     return acc
+
+
+def tiny_checkpoints(directory, inputs: dict):
+    """kvtc.pt / progressive.pt files equal to the ones the golden generator fit (rebuilt from the
+    fixture: seeded bases, means, ladder rungs, progressive orders)."""
+    from pathlib import Path
+
+    directory = Path(directory)
+    saved = {"model": "tiny", "layers": tm.TINY["num_hidden_layers"], "heads": tm.TINY["num_key_value_heads"],
+             "head_dim": tm.TINY["head_dim"], "group": tm.GROUP, "sinks": tm.SINKS}
+    orders = {"model": "tiny", "kvtc": "kvtc.pt"}
+    bases = tiny_bases(inputs)
+    for kind in ("key", "value"):
+        saved[kind] = {"mean": torch.from_numpy(inputs[f"mean_{kind}"]), "basis": torch.from_numpy(bases[kind]),
+                       "rungs": torch.from_numpy(inputs[f"rungs_{kind}"]),
+                       "rung_bytes": [int(x) for x in inputs[f"rung_bytes_{kind}"]]}
+        orders[kind] = {"planes": torch.from_numpy(inputs[f"order_planes_{kind}"]),
+                        "prefix_bytes": torch.from_numpy(inputs[f"order_prefix_{kind}"]),
+                        "rungs": [int(x) for x in inputs[f"order_rungs_{kind}"]]}
+    torch.save(saved, directory / "kvtc.pt")
+    torch.save(orders, directory / "progressive.pt")
+    return directory / "kvtc.pt", directory / "progressive.pt"
+
+
+def tiny_cache(inputs: dict, device="cpu"):
+    """Per-layer bf16 keys / values [1, kv_heads, tokens, head_dim] of the golden prefill."""
+    keys = [torch.from_numpy(f32_from_bits(inputs["keys"][l]))[None].to(device, torch.bfloat16)
+            for l in range(inputs["keys"].shape[0])]
+    values = [torch.from_numpy(f32_from_bits(inputs["values"][l]))[None].to(device, torch.bfloat16)
+              for l in range(inputs["values"].shape[0])]
+    return keys, values

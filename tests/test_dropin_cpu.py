@@ -1,0 +1,80 @@
+"""The drop-in host API (Methods, ProgressiveCodec / ProgressiveCache, KVTCCodec) against the
+reference's own outputs on the golden inputs (CPU; no kernels)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import tinymodel as tm
+from dimmerkv import dimmer
+from dimmerkv.methods import Methods
+from helpers import f16_from_bits, tiny_cache, tiny_checkpoints
+
+
+@pytest.fixture(scope="module")
+def tiny_model():
+    model = tm.build_model(torch.bfloat16, "cpu")
+    dimmer.install(model)
+    return model
+
+
+def _methods(tmp_path, inputs, model):
+    kvtc, prog = tiny_checkpoints(tmp_path, inputs)
+    return Methods("tiny", tmp_path / "none", tmp_path / "none", torch.device("cpu"), tm.RECENT, model=model,
+                   kvtc=kvtc, progressive=prog)
+
+
+def test_prog_encode_refine_match_reference(golden, tmp_path, tiny_model):
+    inputs, fix = golden("tiny_inputs"), golden("tiny_prog")
+    methods = _methods(tmp_path, inputs, tiny_model)
+    keys, values = tiny_cache(inputs)
+    with torch.inference_mode():
+        compressed = methods.apply(str(fix["name"]), keys, values, {})
+        codec = methods.codec("prog")
+        stored = codec.last_cache
+        assert compressed.used_bytes == int(fix["hot_bytes"])
+        assert stored.cold_bytes == int(fix["cold_bytes"]) and stored.budget_bytes == int(fix["budget_bytes"])
+        assert (stored.start, stored.end) == tuple(int(v) for v in fix["span"])
+        for kind in ("key", "value"):
+            s = stored.stores[kind]
+            assert np.array_equal(s.codes.numpy(), fix[f"codes_{kind}"])
+            assert np.array_equal(s.low.numpy(), f16_from_bits(fix[f"low_{kind}"]))
+            assert np.array_equal(s.span.numpy(), f16_from_bits(fix[f"lowspan_{kind}"]))
+            assert np.array_equal(s.hot_pieces.numpy(), fix[f"hot_pieces_{kind}"])
+        # The hot codes the direct path packs: planes of each token's prefix, indices = code >> (8 - m).
+        hot = codec.last_codes["key"]
+        planes = inputs["order_planes_key"][fix["hot_pieces_key"]]
+        assert np.array_equal(hot.planes.numpy(), planes)
+        # Question time, reference path: importance -> top-k -> fetched bytes and refined rows.
+        new_keys, new_values, fetched = compressed.refine(tm.question_ids(), keys[0].shape[2])
+    assert fetched == int(fix["fetched"])
+    rows = np.sort(fix["top"])
+    got = np.stack([k[0][:, rows].contiguous().view(torch.int16).numpy().view(np.uint16) for k in new_keys])
+    assert np.array_equal(got, fix["refined_keys"])
+    assert stored.fetched_bytes(torch.from_numpy(rows)) == int(fix["fetched"])
+
+
+def test_dkvtc_compress_matches_reference(golden, tmp_path, tiny_model):
+    inputs, fix = golden("tiny_inputs"), golden("tiny_dkvtc")
+    methods = _methods(tmp_path, inputs, tiny_model)
+    keys, values = tiny_cache(inputs)
+    scores = {"snap": [torch.from_numpy(inputs["snap"][l]) for l in range(inputs["snap"].shape[0])]}
+    with torch.inference_mode():
+        compressed = methods.apply(str(fix["name"]), keys, values, scores)
+    codec = methods.codec("kvtc")
+    assert compressed.used_bytes == int(fix["used_bytes"])
+    assert tuple(codec.last_span) == tuple(int(v) for v in fix["span"])
+    for kind in ("key", "value"):
+        assert np.array_equal(codec.last_choice[kind].numpy(), fix[f"choice_{kind}"])
+        assert np.array_equal(codec.last_coefficients[kind].float().numpy().view(np.uint32),
+                              fix[f"coeff_{kind}"].view(np.uint32))
+
+
+def test_out_of_path_methods_raise(golden, tmp_path, tiny_model):
+    methods = _methods(tmp_path, golden("tiny_inputs"), tiny_model)
+    with pytest.raises(NotImplementedError):
+        methods.apply("pca16/lex8", [], [], {})
+    with pytest.raises(NotImplementedError):
+        methods.codec("lex")
