@@ -36,6 +36,14 @@ CONFIGS = {
                  workload="3B random-init, 64 ragged conversations T~U[4096,16384], 3% hot budget, bs64 decode"),
     "cfg1": dict(arch="1b", seqs=1, tmin=1536, tmax=1536, budget=0.03, max_groups=16,
                  workload="1B random-init, 1 conversation T=1536, 3% hot budget, bs1 decode"),
+    "cfg4": dict(arch="3b", mode="question", seqs=1, tmin=32768, tmax=32768, budget=0.03, max_groups=64,
+                 hot_planes=2, question=64, fraction=0.01, decode=32,
+                 workload="3B random-init, one 32768-token conversation; hot tier planes 1-2 on the budget's "
+                          "groups, cold tier planes 3-8 in pinned host memory; 64-token question, top-1% refine, "
+                          "32 decode steps"),
+    "cfg5": dict(arch="3b", mode="splitk", seqs=1, tmin=131072, tmax=131072, budget=0.02, max_groups=64,
+                 workload="3B random-init, one 131072-token conversation at 2%, codes sharded over the GPUs "
+                          "(split-K, log-sum-exp merge over NCCL), bs1 decode"),
 }
 METRIC = "decode tok/s over compressed KV (3B,16K,bs64)"
 
@@ -302,6 +310,176 @@ def run_kernels(args, cfg, device) -> dict:
             "gpu_launches": len(timer.events) * 4}
 
 
+def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
+    """Model + one prefilled, compressed conversation of cfg["tmin"] tokens."""
+    import torch
+
+    from dimmerkv import dimmer, synthetic
+    from dimmerkv.context import rope_tables
+
+    arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
+    model = synthetic.build_model(arch, device=device, seed=seed)
+    dimmer.install(model)
+    c = model.config
+    features = c.num_hidden_layers * c.num_key_value_heads * c.head_dim
+    rank = cfg["max_groups"] * 64
+    bases = {kind: synthetic.seeded_basis(features, rank, 1000 + seed * 2 + i, device)
+             for i, kind in enumerate(("key", "value"))}
+    g = torch.Generator().manual_seed(10_000 + seed)
+    t = cfg["tmin"]
+    ids = torch.randint(0, c.vocab_size, (1, t), generator=g).to(device)
+    keys, values = synthetic.prefill(model, ids)
+    cos_f, sin_f = synthetic.rope_full(model, t, device)
+    with torch.inference_mode():
+        conv = synthetic.compress_conversation(keys, values, cos_f, sin_f, bases, cfg["budget"], g, cfg["max_groups"],
+                                               fixed_planes=fixed_planes, keep_full=keep_full)
+    del keys, values, cos_f, sin_f
+    cos, sin = rope_tables(model, t + 4096, device)
+    return model, conv, bases, cos, sin
+
+
+def run_question(args, cfg, device) -> dict:
+    """Config 4: question-time refinement on one 32K conversation (hot planes 1-2, cold planes 3-8 in
+    pinned host memory). Timed once after warm-up: the question's scoring forward over the hot planes,
+    the top-1% selection, the cold-plane fetch and merge; then 32 decode steps over the refined codes."""
+    import numpy as np
+    import torch
+
+    from dimmerkv.compressed_attention import greedy_decode_batch
+    from dimmerkv.context import CompressedBatch
+    from dimmerkv.question import cold_tier, question_importance_direct, refine_count
+
+    model, conv, bases, cos, sin = _one_conversation(cfg, args.seed, device, keep_full=True,
+                                                     fixed_planes=cfg["hot_planes"])
+    c = model.config
+    groups = torch.arange(conv.groups)
+    batch = CompressedBatch([conv.codes], layers=c.num_hidden_layers, kv_heads=c.num_key_value_heads,
+                            head_dim=c.head_dim, q_heads=c.num_attention_heads, basis=bases,
+                            mean={k: v for k, v in conv.mean.items()}, cos=cos, sin=sin, device=device,
+                            union={"key": groups, "value": groups})
+    cold = {kind: cold_tier(*conv.full[kind][:3], groups, conv.full[kind][3]) for kind in ("key", "value")}
+    conv.full = None
+    cache = exact_cache(model, [conv])
+    g = torch.Generator().manual_seed(args.seed + 3)
+    tail = torch.randint(0, c.vocab_size, (1, cfg["question"]), generator=g).to(device)
+    tokens = conv.tokens
+    count = refine_count(cfg["fraction"], conv.middle)
+    stream = torch.cuda.current_stream(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    with torch.inference_mode():
+        for _ in range(max(1, args.warmup)):
+            question_importance_direct(model, batch, cache, tail, [tokens])
+        torch.cuda.synchronize(device)
+        ev[0].record(stream)
+        imp = question_importance_direct(model, batch, cache, tail, [tokens])[0]
+        ev[1].record(stream)
+        selected = batch.select_top([count])
+        ev[2].record(stream)
+        fetched = batch.refine(selected, [cold], torch.cuda.Stream(device))
+        ev[3].record(stream)
+        torch.cuda.synchronize(device)
+        batch.check_status()
+        # The selection against the lowest-index rule on the same importance vector (host check).
+        start, end = batch.spans[0]
+        host = imp[start:end].cpu().numpy()
+        rule = np.sort(np.argsort(-host.astype(np.float64), kind="stable")[:count] + start)
+        exact = bool(np.array_equal(selected[0].numpy(), rule))
+        # Answer: the question over the refined codes, then greedy decode steps.
+        from dimmerkv import dimmer
+
+        t0 = time.perf_counter()
+        dimmer.STATE.compressed = batch
+        try:
+            q_pos = torch.arange(tokens, tokens + cfg["question"], device=device)[None]
+            first = model(input_ids=tail, past_key_values=cache, position_ids=q_pos).logits[:, -1].argmax(-1, keepdim=True)
+        finally:
+            dimmer.STATE.compressed = None
+        _, stats = greedy_decode_batch(model, batch, cache, first.cpu(), torch.tensor([[tokens + cfg["question"]]]),
+                                       cfg["decode"])
+        torch.cuda.synchronize(device)
+        answer_s = time.perf_counter() - t0
+        batch.check_status()
+    phases = {"importance": ev[0].elapsed_time(ev[1]), "select": ev[1].elapsed_time(ev[2]),
+              "refine_fetch_merge": ev[2].elapsed_time(ev[3])}
+    total = sum(phases.values())
+    return {"metric": "question-time refinement latency (score + top-1% select + cold-plane merge)",
+            "value": round(total, 3), "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": 1,
+            "warmup": args.warmup, "dtype": "bf16", "data": "synthetic (seeded random-init weights, random ids)",
+            "config": {"workload": cfg["workload"], "context": tokens, "groups": conv.groups, "refined": count},
+            "phases_ms": {k: round(v, 3) for k, v in phases.items()}, "fetched_bytes": fetched,
+            "topk_matches_lowest_index_rule": exact,
+            "answer_after_refine": {"question_tokens": cfg["question"], "decode_steps": cfg["decode"],
+                                    "seconds": round(answer_s, 3), "decode_tok_s": round(cfg["decode"] / answer_s, 2),
+                                    **stats}}
+
+
+class _LocalComm:
+    rank, world = 0, 1
+
+    def all_gather(self, t):
+        return t[None]
+
+    def all_reduce_sum(self, t):
+        return t
+
+
+def run_splitk(args, cfg, rank, world, device) -> dict | None:
+    """Config 5: one 131K-token conversation, its codes sharded over the ranks (split-K). Every rank
+    builds the same model and conversation (same seeds) and keeps its shard; bs1 decode steps, timed
+    between barriers with CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from dimmerkv import dimmer
+    from dimmerkv.parallel import SplitKContext, TorchComm
+
+    model, conv, bases, cos, sin = _one_conversation(cfg, args.seed, device)
+    c = model.config
+    comm = TorchComm() if world > 1 else _LocalComm()
+    ctx = SplitKContext(conv.codes, comm, layers=c.num_hidden_layers, kv_heads=c.num_key_value_heads,
+                        head_dim=c.head_dim, q_heads=c.num_attention_heads, basis=bases, mean=conv.mean,
+                        cos=cos, sin=sin, device=device)
+    conv.codes = None
+    cache = exact_cache(model, [conv])
+    ids = torch.zeros(1, 1, dtype=torch.int64, device=device)
+    pos = torch.tensor([[conv.tokens]], device=device)
+    dimmer.STATE.compressed = ctx
+    stream = torch.cuda.current_stream(device)
+    try:
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                ids = model(input_ids=ids, past_key_values=cache, position_ids=pos).logits[:, -1].argmax(-1, keepdim=True)
+                pos = pos + 1
+            torch.cuda.synchronize(device)
+            if world > 1:
+                dist.barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(device.index or 0) as clocks:
+                start.record(stream)
+                for _ in range(args.steps):
+                    ids = model(input_ids=ids, past_key_values=cache, position_ids=pos).logits[:, -1].argmax(-1, keepdim=True)
+                    pos = pos + 1
+                end.record(stream)
+                torch.cuda.synchronize(device)
+            ctx.check_status()
+    finally:
+        dimmer.STATE.compressed = None
+    elapsed = torch.tensor([start.elapsed_time(end) / 1e3], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    t = float(elapsed.item())
+    if rank != 0:
+        return None
+    code_bytes_step = conv.hot_bytes * c.num_hidden_layers
+    return {"metric": "decode tok/s, one 131K-token conversation split over GPUs (bs1)",
+            "value": round(args.steps / t, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded random-init weights, random ids)",
+            "config": {"workload": cfg["workload"], "context": conv.tokens, "groups": conv.groups,
+                       "parallelism": f"split-K x{world}"},
+            "code_read_gbs": round(code_bytes_step / (t / args.steps) / 1e9, 2), "clocks": clocks.summary()}
+
+
 # ----------------------------------------------------------------------------- runs
 def run_ours(args, cfg, rank, world, device):
     import torch
@@ -536,7 +714,15 @@ def main():
                 raise SystemExit("--kernels-only is a 1-GPU profiling case")
             print(json.dumps(run_kernels(args, cfg, device)), flush=True)
             return
-        result = run_ours(args, cfg, rank, world, device)
+        mode = cfg.get("mode", "batch")
+        if mode == "question":
+            if world > 1:
+                raise SystemExit("cfg4 runs on one GPU")
+            result = run_question(args, cfg, device)
+        elif mode == "splitk":
+            result = run_splitk(args, cfg, rank, world, device)
+        else:
+            result = run_ours(args, cfg, rank, world, device)
         if result is not None:
             print(json.dumps(result), flush=True)
     finally:

@@ -129,18 +129,26 @@ class SyntheticConversation:
     mean: dict              # kind -> [F] float32
     hot_bytes: int          # bytes under the reference's accounting (both streams, middle tokens)
     cpu_codes: dict | None = None  # kind -> numpy (codes, low, span, planes, m) when kept for a CPU sample
+    full: dict | None = None       # kind -> device (codes, low, span, hot planes) for a cold tier
 
 
 def compress_conversation(keys: list[torch.Tensor], values: list[torch.Tensor], cos, sin, bases: dict,
                           budget: float, generator: torch.Generator, max_groups: int,
-                          keep_cpu: bool = False) -> SyntheticConversation:
+                          keep_cpu: bool = False, fixed_planes: int | None = None,
+                          keep_full: bool = False) -> SyntheticConversation:
+    """Compress one prefilled conversation with progressive codes: every middle token's plane count is
+    drawn from PLANE_CHOICES (or ``fixed_planes`` for all), applied to the first G groups, G the largest
+    that fits ``budget``. ``keep_full`` keeps the full 8-bit codes on the device for a cold tier."""
     tokens = keys[0].shape[2]
     start, end = SINKS, tokens - RECENT
     middle = end - start
     features = sum(k.shape[1] * k.shape[3] for k in keys)
-    m = {kind: draw_planes(middle, generator) for kind in ("key", "value")}
+    if fixed_planes is not None:
+        m = {kind: torch.full((middle,), fixed_planes, dtype=torch.int64) for kind in ("key", "value")}
+    else:
+        m = {kind: draw_planes(middle, generator) for kind in ("key", "value")}
     G = budget_groups(tokens, features, budget, m["key"], m["value"], max_groups)
-    streams, means, cpu = {}, {}, {}
+    streams, means, cpu, full = {}, {}, {}, {}
     hot = 0
     for kind, tensors in (("key", keys), ("value", values)):
         matrix = token_matrix(tensors, cos, sin) if kind == "key" else token_matrix(tensors)
@@ -158,11 +166,14 @@ def compress_conversation(keys: list[torch.Tensor], values: list[torch.Tensor], 
         if keep_cpu:
             cpu[kind] = (codes.cpu().numpy(), low.cpu().numpy(), span.cpu().numpy(), planes.cpu().numpy(),
                          m[kind].numpy())
+        if keep_full:
+            full[kind] = (codes, low, span, planes)
         hot += int(G * (8 * m[kind] + 4 * (m[kind] > 0)).sum()) + middle
     exact_k = [torch.cat([k[..., :start, :], k[..., end:, :]], dim=2) for k in keys]
     exact_v = [torch.cat([v[..., :start, :], v[..., end:, :]], dim=2) for v in values]
     return SyntheticConversation(ConversationCodes(start, end, streams["key"], streams["value"]), tokens, middle, G,
-                                 int((m["key"] > 0).sum()), exact_k, exact_v, means, hot, cpu if keep_cpu else None)
+                                 int((m["key"] > 0).sum()), exact_k, exact_v, means, hot, cpu if keep_cpu else None,
+                                 full if keep_full else None)
 
 
 def prefill(model, ids: torch.Tensor, chunk: int = 4096):
