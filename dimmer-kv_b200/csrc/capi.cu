@@ -237,6 +237,7 @@ static int finalize_rows(const dkv_attend_args* a, int row_begin, int n_rows, vo
   p.out = a->out;
   p.out_f32 = a->out_f32;
   p.vpart = a->vpart;
+  p.status = a->status;
   if (a->vpart == nullptr) return DKV_ERR_ARGS;
   return dkv::run_finalize(p, static_cast<cudaStream_t>(stream));
 }

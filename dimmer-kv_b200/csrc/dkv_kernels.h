@@ -113,6 +113,7 @@ struct FinalizeParams {
   void* out;                      // [n_seq][q_len][n_q_heads][head_dim]
   int out_f32;                    // fp32 output instead of bf16
   float* vpart;                   // [finalize_chunks(r_v)][n_seq][n_rows_pad][head_dim]
+  int* status;
 };
 int finalize_chunks(int r_v);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);

@@ -13,14 +13,17 @@
 //   combine : sums the chunks in a fixed order (deterministic), adds the mean term and the exact
 //             tokens, and writes the HF layout [batch, q_len, q_heads, head_dim].
 #include "dkv_kernels.h"
+#include "dkv_ptx.cuh"
 
 namespace dkv {
 
 namespace {
 constexpr int kFinalizeThreads = 256;
 constexpr int kCombineThreads = 128;
+constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA
 constexpr int kRChunk = 128;   // basis components per vbasis CTA
 constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
+constexpr int kMaxCover = 2048;  // items of the CTA's conversations that cover its component chunk
 }  // namespace
 
 __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block) {
@@ -50,19 +53,43 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
     bs[i] = (r0 + r < p.r_v) ? bsrc[static_cast<int64_t>(r0 + r) * (p.n_cols / 2) + dp]
                              : __floats2bfloat162_rn(0.f, 0.f);
   }
-  // Weighted coefficients of the block's conversations: every element sums its conversation's items
-  // that cover this chunk (independent loads, in item order).
+  // Weighted coefficients of the block's conversations. First the items of each conversation that cover
+  // this chunk (in item order), then every element sums them with independent loads.
+  __shared__ int cover[kMaxCover];
+  __shared__ int n_cover[kSeqBlock + 1];
+  if (tid == 0) {
+    int n = 0;
+    for (int sl = 0; sl < n_s; ++sl) {
+      n_cover[sl] = n;
+      for (int it = p.seq_items[2 * (s0 + sl)], it1 = p.seq_items[2 * (s0 + sl) + 1]; it < it1; ++it) {
+        const int cb = p.items[4 * it + 3] * 64;
+        if (r0 >= cb && r0 < cb + item_cols) {
+          if (n == kMaxCover) {  // more covering items than the list holds: report, never drop silently
+            record_error(p.status, kErrBadDescriptor);
+            break;
+          }
+          cover[n++] = it;
+        }
+      }
+    }
+    n_cover[n_s] = n;
+  }
+  __syncthreads();
   for (int i = tid; i < n_s * nr * kRChunk; i += kFinalizeThreads) {
     const int sl = i / (nr * kRChunk);
     const int rr = (i / kRChunk) % nr, c = i % kRChunk;
-    const int s = s0 + sl;
-    float acc = 0.f;
-    for (int it = p.seq_items[2 * s], it1 = p.seq_items[2 * s + 1]; it < it1; ++it) {
-      const int cb = p.items[4 * it + 3] * 64;
-      if (r0 < cb || r0 >= cb + item_cols) continue;  // the item does not cover this chunk
-      acc += p.partial[(static_cast<int64_t>(it) * p.n_rows_pad + (rlo - p.row_begin + rr)) * item_cols + (r0 - cb) + c];
+    const int64_t col = (rlo - p.row_begin + rr) * static_cast<int64_t>(item_cols) + (r0 % item_cols) + c;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int j = n_cover[sl];
+    const int j1 = n_cover[sl + 1];
+    for (; j + 4 <= j1; j += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        acc[u] += p.partial[static_cast<int64_t>(cover[j + u]) * p.n_rows_pad * item_cols + col];
     }
-    ws[i] = acc;
+    float tail = 0.f;
+    for (; j < j1; ++j) tail += p.partial[static_cast<int64_t>(cover[j]) * p.n_rows_pad * item_cols + col];
+    ws[i] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + tail;
   }
   __syncthreads();
   const int dp = tid % D2;
@@ -84,14 +111,16 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
   }
 }
 
-// One CTA per (conversation, KV head); a thread per output dim of every row of the head.
+// One CTA per (conversation, KV head, block of 8 rows of the head); a thread per output dim.
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const FinalizeParams p, int n_chunks) {
   const int G = p.q_per_kv;
   const int n_kv = p.n_q_heads / G;
   const int s = blockIdx.x / n_kv, kvh = blockIdx.x % n_kv;
   const int D = p.head_dim;
-  const int rlo = max(p.row_begin, kvh * G * p.q_len);
-  const int rhi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  const int head_lo = max(p.row_begin, kvh * G * p.q_len);
+  const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  const int rlo = head_lo + blockIdx.y * kCombineRows;
+  const int rhi = min(head_hi, rlo + kCombineRows);
   for (int i = threadIdx.x; i < (rhi - rlo) * D; i += blockDim.x) {
     const int row = rlo + i / D, d = i % D;
     const int lr = row - p.row_begin;
@@ -157,7 +186,9 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   vbasis_kernel<<<dim3(n_chunks, n_kv, (p.n_seq + seq_block - 1) / seq_block), kFinalizeThreads, smem, stream>>>(
       p, seq_block);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
-  combine_kernel<<<p.n_seq * n_kv, kCombineThreads, 0, stream>>>(p, n_chunks);
+  const int rows_per_head = min(p.n_rows, p.q_per_kv * p.q_len);
+  const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + kCombineRows - 1) / kCombineRows);
+  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

@@ -5,12 +5,13 @@
 //   p_c = softmax(...)[..., :middle].to(dtype)
 //   weighted += einsum("bhgqn,nr->bhgqr", p_c[..., block.index], block.coefficients)
 // for a batch of conversations. One work item = (conversation, run of value tiles, range of
-// union groups). For every tile the 8 worker warps
-//   - build P^T (rows = query head x query row, K = the tile's 128 tokens) in bf16 from the
-//     fp32 scores and the softmax statistics (exactly the reference's rounding of p to the
-//     cache dtype), 128B-swizzled K-major;
-//   - decode each pair of coefficient groups into a 128-component x 128-token bf16 tile
-//     (MN-major operand: token rows of 64 components, 128B swizzle).
+// union groups). Two sets of 8 worker warps share every tile:
+//   - both build P^T (rows = query head x query row, K = the tile's 128 tokens; each set half of
+//     the rows) in bf16 from the fp32 scores and the softmax statistics (exactly the reference's
+//     rounding of p to the cache dtype), 128B-swizzled K-major;
+//   - they decode alternate pairs of coefficient groups (pair ordinal k of a tile goes to set
+//     k % 2, into that set's own ring of A tiles) into 128-component x 128-token bf16 tiles
+//     (MN-major operand: token rows of 64 components, 128B swizzle), so two decodes are in flight.
 // The MMA warp accumulates D[128 components, rows] += C^T P^T with tcgen05 (M=128, N=rows,
 // K=16 tokens per instruction) into one TMEM column range per group pair. At the end of the
 // item the accumulators are written to `partial` (fp32), which finalize.cu reduces.
@@ -25,7 +26,7 @@ namespace dkv {
 
 namespace {
 
-constexpr int kVThreads = 384;  // producer, MMA, 2 idle, 8 workers (P build, decode; warps 4-7 also epilogue)
+constexpr int kVThreads = 576;    // producer, MMA, worker set 0 (warps 2-9; 4-7 also epilogue), set 1 (10-17)
 constexpr int kPairTile = 32768;  // two groups x 128 tokens x 128 B
 constexpr int kMaxRangeGroups = 64;
 
@@ -53,7 +54,7 @@ __device__ __forceinline__ int next_pair(const GroupDesc* d, int n, int g0, int&
 }  // namespace
 
 template <bool RAW>
-__global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const ValueWeightParams p) {
+__global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const ValueWeightParams p, int a_slots) {
   using L = ValueSmem<RAW>;
   constexpr int kCodeSlots = L::kCodeSlots;
   constexpr int kCodeSlot = L::kCodeSlot;
@@ -61,24 +62,25 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NR = p.n_rows_pad;  // MMA N (multiple of 16, <= 128)
   const int p_tile = NR * 256;  // two K atoms of 64 tokens
-  uint8_t* a_tiles = smem;                                    // [2][kPairTile]
-  uint8_t* p_tiles = a_tiles + 2 * kPairTile;                 // [2][p_tile]
+  uint8_t* a_tiles = smem;                                              // [2 sets][a_slots][kPairTile]
+  uint8_t* p_tiles = a_tiles + 2 * a_slots * kPairTile;                 // [2][p_tile]
   GroupDesc* descs = reinterpret_cast<GroupDesc*>(p_tiles + 2 * p_tile);  // [2][kMaxRangeGroups]
   float* stats_s = reinterpret_cast<float*>(descs + 2 * kMaxRangeGroups);  // [3][128][2] max, 1/sum
   uint8_t* c_slots = reinterpret_cast<uint8_t*>(stats_s + 3 * 256);        // [kCodeSlots][kCodeSlot]
   uint64_t* bars = reinterpret_cast<uint64_t*>(c_slots + kCodeSlots * kCodeSlot);
   uint64_t* code_full = bars;
   uint64_t* code_empty = code_full + kCodeSlots;
-  uint64_t* a_full = code_empty + kCodeSlots;  // [2]
-  uint64_t* a_empty = a_full + 2;              // [2]
-  uint64_t* p_full = a_empty + 2;              // [2]
+  uint64_t* a_full = code_empty + kCodeSlots;  // [2 sets][2]
+  uint64_t* a_empty = a_full + 4;              // [2 sets][2]
+  uint64_t* p_full = a_empty + 4;              // [2]
   uint64_t* p_empty = p_full + 2;              // [2]
   uint64_t* d_full = p_empty + 2;              // [2]
   uint64_t* d_empty = d_full + 2;              // [2]
   uint64_t* stats_ready = d_empty + 2;         // [3]
   uint64_t* accum_full = stats_ready + 3;
   uint64_t* accum_empty = accum_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_empty + 1);
+  uint64_t* mma_done = accum_empty + 1;        // MMA issuer: its MMAs completed (early exit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -90,19 +92,22 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   if (tid == 0) {
     for (int i = 0; i < kCodeSlots; ++i) {
       mbar_init(&code_full[i], 1);
-      mbar_init(&code_empty[i], 256);
+      mbar_init(&code_empty[i], 256);  // the 256 threads of the set that decodes the block
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&a_full[i], 256);
       mbar_init(&a_empty[i], 1);
-      mbar_init(&p_full[i], 256);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 512);
       mbar_init(&p_empty[i], 1);
       mbar_init(&d_full[i], 1);
-      mbar_init(&d_empty[i], 257);
+      mbar_init(&d_empty[i], 513);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&stats_ready[i], 256);
+    for (int i = 0; i < 3; ++i) mbar_init(&stats_ready[i], 512);
     mbar_init(accum_full, 1);
     mbar_init(accum_empty, 128);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -168,11 +173,22 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           ++d_iter;
         }
       }
+      // Drain: every copy this CTA issued has landed before the CTA can leave.
+      for (int s = 0; s < kCodeSlots && s < static_cast<int>(c_iter); ++s) {
+        const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kCodeSlots);
+        mbar_wait(&code_full[s], (last / kCodeSlots) & 1, p.status, kErrWaitDrain);
+      }
+      for (int s = 0; s < 2 && s < static_cast<int>(d_iter); ++s) {
+        const uint32_t last = d_iter - 1 - ((d_iter - 1 - s) % 2);
+        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
+      uint32_t a_iter[2] = {0, 0};
+      uint32_t p_iter = 0, d_iter = 0, item_iter = 0;
+      bool issued = false;
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
@@ -198,26 +214,29 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             break;
           }
           const GroupDesc* d = descs + db * kMaxRangeGroups;
-          int i = 0, lo, hi, pair;
+          int i = 0, lo, hi, pair, ord = 0;
           while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
-            const int slot = a_iter & 1;
-            if (!mbar_wait(&a_full[slot], (a_iter >> 1) & 1, p.status, kErrWaitA)) {
+            const int set = ord & 1;
+            const int slot = a_iter[set] % a_slots;
+            if (!mbar_wait(&a_full[set * 2 + slot], (a_iter[set] / a_slots) & 1, p.status, kErrWaitA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_base = smem_u32(a_tiles + slot * kPairTile);
+            const uint32_t a_base = smem_u32(a_tiles + (set * a_slots + slot) * kPairTile);
             const uint32_t p_base = smem_u32(p_tiles + pb * p_tile);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint64_t adesc = smem_desc_sw128(a_base + k * 2048, 16384, 1024);
-              const uint64_t bdesc = smem_desc_sw128(p_base + (k >> 2) * (NR * 128) + (k & 3) * 32, 16, 1024);
-              const uint32_t acc = ((started >> pair) & 1u) || k > 0 ? 1u : 0u;
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t adesc = smem_desc_sw128(a_base + kk * 2048, 16384, 1024);
+              const uint64_t bdesc = smem_desc_sw128(p_base + (kk >> 2) * (NR * 128) + (kk & 3) * 32, 16, 1024);
+              const uint32_t acc = ((started >> pair) & 1u) || kk > 0 ? 1u : 0u;
               mma_f16(tmem + pair * NR, adesc, bdesc, idesc, acc);
             }
+            issued = true;
             started |= 1u << pair;
-            mma_commit(&a_empty[slot]);
-            ++a_iter;
+            mma_commit(&a_empty[set * 2 + slot]);
+            ++a_iter[set];
+            ++ord;
           }
           if (!ok) break;
           mma_commit(&p_empty[pb]);
@@ -232,12 +251,19 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         mma_commit(accum_full);
         ++item_iter;
       }
+      if (issued && *abort_flag) {
+        // Early exit: no MMA may still read shared memory or TMEM past this point.
+        mma_commit(mma_done);
+        mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+      }
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ worker warps (P, decode, epilogue)
-    const int u = tid - 128;
-    const int r = u & 127;  // token row (decode) / token column (P)
-    const int h = u >> 7;   // component half (decode) / row half (P)
+  } else {
+    // ------------------------------------------------------------ worker sets (P, decode; warps 4-7 epilogue)
+    const int set = warp >= 10 ? 1 : 0;
+    const int u = tid - (set ? 320 : 64);  // 0..255 within the set
+    const int w = tid - 64;                // 0..511 over both sets
+    const int r = u & 127;                 // token row (decode) / token column (P)
+    const int h = u >> 7;                  // component half (decode) / row quarter within the set's half (P)
     uint32_t c_iter = 0, a_iter = 0, p_iter = 0, d_iter = 0, item_iter = 0;
     for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
       const int it = items.at(k);
@@ -253,25 +279,25 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       // can be at most two items ahead of the slowest one (each P tile waits for the MMA of the tile
       // two before it, which waits for every worker), so three buffers never collide.
       float* st_s = stats_s + (item_iter % 3) * 256;
-      if (u < NR) {
+      if (w < NR) {
         float mx = 0.f, inv = 0.f;
-        if (u < p.n_rows) {
-          const float* st = p.row_stats + (static_cast<int64_t>(s) * p.n_q_heads * p.q_len + p.row_begin + u) * 4;
+        if (w < p.n_rows) {
+          const float* st = p.row_stats + (static_cast<int64_t>(s) * p.n_q_heads * p.q_len + p.row_begin + w) * 4;
           mx = st[0];
           inv = st[1];
         }
-        st_s[2 * u] = mx;
-        st_s[2 * u + 1] = inv;
+        st_s[2 * w] = mx;
+        st_s[2 * w + 1] = inv;
       }
       mbar_arrive(&stats_ready[item_iter % 3]);
       if (!mbar_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kErrWaitA)) {
         *abort_flag = 1;
         break;
       }
-      uint32_t started = 0;
       for (int t = tb; t < te && !*abort_flag; ++t) {
         const TileDesc tile = p.tiles[t];
-        // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype)
+        // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype); set s builds
+        //      rows [s*NR/2, (s+1)*NR/2), thread half h a quarter of them.
         const int pb = p_iter & 1;
         if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
           *abort_flag = 1;
@@ -282,18 +308,19 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const bool tok_ok = r < tile.n_tokens;
           const int sidx = tok_ok ? p.tok_sidx[tile.token_base + r] : 0;
           const int atom = r >> 6, chunk = (r & 63) >> 3, within = (r & 7) * 2;
-          const int rows_half = NR / 2;
-          for (int n0 = h * rows_half; n0 < (h + 1) * rows_half; n0 += 8) {
-            float x[8];
+          const int quarter = NR / 4;
+          const int rb = set * (NR / 2) + h * quarter;
+          for (int n0 = rb; n0 < rb + quarter; n0 += 4) {
+            float x[4];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int n = n0 + k;
-              x[k] = (tok_ok && n < p.n_rows) ? sc[static_cast<int64_t>(p.row_begin + n) * m_s + sidx] : -INFINITY;
+            for (int kk = 0; kk < 4; ++kk) {
+              const int n = n0 + kk;
+              x[kk] = (tok_ok && n < p.n_rows) ? sc[static_cast<int64_t>(p.row_begin + n) * m_s + sidx] : -INFINITY;
             }
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int n = n0 + k;
-              const float prob = (x[k] == -INFINITY) ? 0.f : expf(x[k] - st_s[2 * n]) * st_s[2 * n + 1];
+            for (int kk = 0; kk < 4; ++kk) {
+              const int n = n0 + kk;
+              const float prob = (x[kk] == -INFINITY) ? 0.f : expf(x[kk] - st_s[2 * n]) * st_s[2 * n + 1];
               *reinterpret_cast<__nv_bfloat16*>(pt + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
                   __float2bfloat16_rn(prob);
             }
@@ -302,7 +329,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           mbar_arrive(&p_full[pb]);
           ++p_iter;
         }
-        // ---- coefficient pairs
+        // ---- coefficient pairs: this set takes the pairs of its ordinal parity
         const int db = d_iter & 1;
         const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                       p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
@@ -311,14 +338,21 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           break;
         }
         const GroupDesc* d = descs + db * kMaxRangeGroups;
-        int i = 0, lo, hi, pair;
+        int i = 0, lo, hi, pair, ord = 0;
         while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
-          const int slot = a_iter & 1;
-          if (a_iter >= 2 && !mbar_wait(&a_empty[slot], ((a_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+          const int blocks = (lo >= 0) + (hi >= 0);
+          if ((ord & 1) != set) {  // the other set's pair: skip its code slots
+            c_iter += blocks;
+            ++ord;
+            continue;
+          }
+          const int slot = a_iter % a_slots;
+          if (a_iter >= static_cast<uint32_t>(a_slots) &&
+              !mbar_wait(&a_empty[set * 2 + slot], ((a_iter / a_slots) - 1) & 1, p.status, kErrWaitEmpty)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* a = a_tiles + slot * kPairTile;
+          uint8_t* a = a_tiles + (set * a_slots + slot) * kPairTile;
           for (int half = 0; half < 2; ++half) {
             const int gi = half ? hi : lo;
             uint8_t* dst = a + half * 16384;
@@ -336,25 +370,25 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               ++c_iter;
             } else {
 #pragma unroll
-              for (int k = 0; k < 16; ++k) out[k] = 0u;
+              for (int kk = 0; kk < 16; ++kk) out[kk] = 0u;
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              *reinterpret_cast<uint4*>(dst + sw128_offset(r, 4 * h + k)) =
-                  make_uint4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
+            for (int kk = 0; kk < 4; ++kk)
+              *reinterpret_cast<uint4*>(dst + sw128_offset(r, 4 * h + kk)) =
+                  make_uint4(out[4 * kk], out[4 * kk + 1], out[4 * kk + 2], out[4 * kk + 3]);
           }
           if (*abort_flag) break;
           fence_async_shared();
-          mbar_arrive(&a_full[slot]);
+          mbar_arrive(&a_full[set * 2 + slot]);
           ++a_iter;
-          started |= 1u << pair;
+          ++ord;
         }
         mbar_arrive(&d_empty[db]);
         ++d_iter;
       }
       if (*abort_flag) break;
-      // ---- epilogue (warps 4..7): TMEM -> partial sums
-      if (warp < 8) {
+      // ---- epilogue (warps 4..7, one per TMEM lane quarter): TMEM -> partial sums
+      if (warp >= 4 && warp < 8) {
         if (!mbar_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum)) {
           *abort_flag = 1;
           break;
@@ -363,8 +397,15 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         const int c = (warp - 4) * 32 + lane;  // component within the pair == TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
         float* dst = p.partial + static_cast<int64_t>(it) * NR * item_cols;
+        // Pairs started by either set: the MMA started every pair that has a block in the item.
+        uint32_t live_mask = 0;
+        for (int t = tb; t < te; ++t) {
+          const int d0 = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
+          const int d1 = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1];
+          for (int i2 = d0; i2 < d1; ++i2) live_mask |= 1u << ((static_cast<int>(__ldg(&p.groups[i2].group)) - g0) >> 1);
+        }
         for (int pair2 = 0; pair2 < n_pairs; ++pair2) {
-          const bool live = (started >> pair2) & 1u;
+          const bool live = (live_mask >> pair2) & 1u;
           for (int n0 = 0; n0 < NR; n0 += 16) {
             uint32_t v[16];
             if (live) {
@@ -372,11 +413,11 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               tmem_ld_wait();
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = 0u;
+              for (int i2 = 0; i2 < 16; ++i2) v[i2] = 0u;
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              dst[static_cast<int64_t>(n0 + i) * item_cols + pair2 * 128 + c] = __uint_as_float(v[i]);
+            for (int i2 = 0; i2 < 16; ++i2)
+              dst[static_cast<int64_t>(n0 + i2) * item_cols + pair2 * 128 + c] = __uint_as_float(v[i2]);
           }
         }
         tc_fence_before();
@@ -399,15 +440,17 @@ int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream)
   const bool raw = p.max_planes > 8;
   const int slots = raw ? ValueSmem<true>::kCodeSlots * ValueSmem<true>::kCodeSlot
                         : ValueSmem<false>::kCodeSlots * ValueSmem<false>::kCodeSlot;
-  const int smem = 1024 + 2 * kPairTile + 2 * p.n_rows_pad * 256 + 2 * kMaxRangeGroups * 32 + 3 * 256 * 4 + slots + 40 * 8;
+  const int a_slots = p.n_rows_pad > 64 ? 1 : 2;  // two A tiles per set where the P tiles leave room
+  const int smem = 1024 + 2 * a_slots * kPairTile + 2 * p.n_rows_pad * 256 + 2 * kMaxRangeGroups * 32 + 3 * 256 * 4 +
+                   slots + 48 * 8;
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e = raw ? cudaFuncSetAttribute(value_weights_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
                       : cudaFuncSetAttribute(value_weights_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return kDkvErrCuda;
   if (raw)
-    value_weights_kernel<true><<<grid, kVThreads, smem, stream>>>(p);
+    value_weights_kernel<true><<<grid, kVThreads, smem, stream>>>(p, a_slots);
   else
-    value_weights_kernel<false><<<grid, kVThreads, smem, stream>>>(p);
+    value_weights_kernel<false><<<grid, kVThreads, smem, stream>>>(p, a_slots);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
