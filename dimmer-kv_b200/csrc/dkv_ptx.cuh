@@ -274,6 +274,17 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask
       : "memory");
 }
 
+// Per-warpgroup register budgets (all four warps of a warpgroup execute the same instruction).
+// The budgets of a CTA's warpgroups must fit the registers it was launched with.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }
 
 __device__ __forceinline__ int warp_id() { return static_cast<int>(threadIdx.x >> 5); }

@@ -23,7 +23,7 @@ constexpr int kCombineThreads = 128;
 constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA
 constexpr int kRChunk = 128;   // basis components per vbasis CTA
 constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
-constexpr int kMaxCover = 2048;  // items of the CTA's conversations that cover its component chunk
+constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a component chunk
 }  // namespace
 
 __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block) {
@@ -55,24 +55,33 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
   }
   // Weighted coefficients of the block's conversations. First the items of each conversation that cover
   // this chunk (in item order), then every element sums them with independent loads.
-  __shared__ int cover[kMaxCover];
-  __shared__ int n_cover[kSeqBlock + 1];
-  if (tid == 0) {
-    int n = 0;
-    for (int sl = 0; sl < n_s; ++sl) {
-      n_cover[sl] = n;
-      for (int it = p.seq_items[2 * (s0 + sl)], it1 = p.seq_items[2 * (s0 + sl) + 1]; it < it1; ++it) {
-        const int cb = p.items[4 * it + 3] * 64;
-        if (r0 >= cb && r0 < cb + item_cols) {
-          if (n == kMaxCover) {  // more covering items than the list holds: report, never drop silently
-            record_error(p.status, kErrBadDescriptor);
-            break;
-          }
-          cover[n++] = it;
+  // One warp per conversation builds its list (at most kCoverPerSeq items).
+  __shared__ int cover[kSeqBlock * kCoverPerSeq];
+  __shared__ int n_cover[kSeqBlock];
+  {
+    const int sl = tid >> 5, ln = tid & 31;
+    if (sl < n_s) {
+      const int it0 = p.seq_items[2 * (s0 + sl)], it1 = p.seq_items[2 * (s0 + sl) + 1];
+      int n = 0;
+      for (int base = it0; base < it1; base += 32) {
+        const int it = base + ln;
+        bool hit = false;
+        if (it < it1) {
+          const int cb = p.items[4 * it + 3] * 64;
+          hit = r0 >= cb && r0 < cb + item_cols;
         }
+        const unsigned mask = __ballot_sync(0xffffffffu, hit);
+        const int slot = n + __popc(mask & ((1u << ln) - 1u));
+        if (hit) {
+          if (slot < kCoverPerSeq)
+            cover[sl * kCoverPerSeq + slot] = it;
+          else  // more covering items than the list holds: report, never drop silently
+            record_error(p.status, kErrBadDescriptor);
+        }
+        n += __popc(mask);
       }
+      if (ln == 0) n_cover[sl] = n < kCoverPerSeq ? n : kCoverPerSeq;
     }
-    n_cover[n_s] = n;
   }
   __syncthreads();
   for (int i = tid; i < n_s * nr * kRChunk; i += kFinalizeThreads) {
@@ -80,8 +89,8 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
     const int rr = (i / kRChunk) % nr, c = i % kRChunk;
     const int64_t col = (rlo - p.row_begin + rr) * static_cast<int64_t>(item_cols) + (r0 % item_cols) + c;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int j = n_cover[sl];
-    const int j1 = n_cover[sl + 1];
+    int j = sl * kCoverPerSeq;
+    const int j1 = j + n_cover[sl];
     for (; j + 4 <= j1; j += 4) {
 #pragma unroll
       for (int u = 0; u < 4; ++u)

@@ -14,15 +14,16 @@
 // same shared memory. Each token's codes are decoded twice per layer (two column blocks).
 //
 // The two tiles' groups are merged (both CTAs walk the same sorted union); a CTA whose tile lacks a
-// group decodes zeros for it. Roles per CTA (608 threads):
+// group decodes zeros for it. Roles per CTA (896 threads, seven warpgroups):
 //   warp 0     code producer: plane blocks of its own tile (cp.async.bulk, ring of code slots)
-//   warp 18    basis producer: its half of the basis rows of every MMA (TMA, ring of B stages)
 //   warp 1     even CTA: the pair MMA issuer; odd CTA: forwards its B-stage completions to the even
 //              CTA (a TMA completes on the issuing CTA's own barrier, so every CTA can drain its copies)
-//   warps 2-9  decode: bit planes -> bf16 A tile (128 tokens x 64 components, 128B swizzle); they
-//              follow the producer's slots (each slot carries its descriptor, the tile's token count
-//              and an end mark), so they hold no item state
-//   warps 10-17 epilogue: TMEM -> + mean -> RoPE -> bf16 keys -> q.k -> fp32 scores
+//   warp 2     basis producer: its half of the basis rows of every MMA (TMA, ring of B stages)
+//   warps 4-19 decode, two sets of 8 warps taking alternate groups: bit planes -> bf16 A tile (128
+//              tokens x 64 components, 128B swizzle); they follow the producer's slots (each slot carries
+//              its descriptor, the tile's token count and an end mark), so they hold no item state
+//   warps 20-27 epilogue: TMEM -> + mean -> RoPE -> q.k -> fp32 scores, two heads' accumulators
+//              loaded per TMEM wait
 // Cross-CTA signals: decode and epilogue warps arrive on the even CTA's a_full / accum_empty barriers
 // (one arrival per warp, after the operand writes are fenced to the async proxy); the MMA commits multicast to both CTAs' a_empty / b_empty /
 // accum_full barriers. Every wait is bounded; on any error both CTAs stop issuing, drain their own
@@ -35,7 +36,19 @@ namespace dkv {
 
 namespace {
 
-constexpr int kPairThreads = 608;
+constexpr int kPairThreads = 896;
+// Register split per warpgroup (setmaxnreg): the launch gives every thread kLaunchRegs; the control
+// warpgroup drops to 40, the four decode warpgroups to 48, the two epilogue warpgroups take 136:
+// 128*40 + 512*48 + 256*136 = 64512 <= 896*72 = 64512. The launch checks the compiled count first.
+constexpr int kLaunchRegs = 72;
+#ifndef DKV_REGS_CONTROL
+#define DKV_REGS_CONTROL 40
+#define DKV_REGS_DECODE 48
+#define DKV_REGS_EPILOGUE 136
+#endif
+constexpr int kRegsControl = DKV_REGS_CONTROL, kRegsDecode = DKV_REGS_DECODE, kRegsEpilogue = DKV_REGS_EPILOGUE;
+static_assert(128 * kRegsControl + 512 * kRegsDecode + 256 * kRegsEpilogue <= kPairThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr int kPairCols = 512;              // key columns per item
 constexpr int kMmaN = 256;                  // N of one pair MMA (two per K step)
 constexpr int kHalfCols = 128;              // basis columns of one pair MMA loaded by each CTA
@@ -188,6 +201,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const uint32_t b_peer_lead = mapa_shared(smem_u32(b_peer), 0);
   const uint32_t accum_empty_lead = mapa_shared(smem_u32(accum_empty), 0);
 
+  // Each role's register budget is set at the top of its warpgroup's branch (so that it governs the
+  // role's code) and the launch budget restored at the bottom, before the common exit path; the
+  // epilogue warpgroups release their extra registers there, which the others then take back.
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsControl>();
   if (warp == 0) {
     // ------------------------------------------------------------ code producer
     if (lane == 0) {
@@ -202,55 +220,53 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           *abort_flag = 1;
           break;
         }
+        if (cc.done()) {
+          c_ended = true;  // the end marks follow below
+          break;
+        }
         uint8_t* slot_end = c_slots + (cs + 1) * kCodeSlot;
         uint4* stash = reinterpret_cast<uint4*>(slot_end - 32);
-        if (cc.done()) {
-          // End mark: the decode warps stop here.
-          stash[0] = make_uint4(0u, 0u, 0u, kStashEnd << 24);
+        int desc;
+        const uint32_t g = cc.group(p, rank, desc);
+        const uint32_t n_tok = static_cast<uint32_t>(cc.tok[rank]);
+        if (desc >= 0) {
+          const GroupDesc* gd = &p.groups[desc];
+          const uint4* src = reinterpret_cast<const uint4*>(gd);
+          uint4 w0 = __ldg(src);
+          const uint4 w1 = __ldg(src + 1);
+          const GroupRegs gr = group_from_words(w0, w1);
+          if (gr.code_bytes > static_cast<uint32_t>(kCodeSlot - 32) ||
+              static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size ||
+              gr.group >= p.n_union_groups) {
+            record_error(p.status, kErrBadDescriptor);
+            *abort_flag = 1;
+            break;
+          }
+          w0.w = (w0.w & 0xFFFFu) | (n_tok << 16);  // pad0: the tile's token count
+          stash[0] = w0;
+          stash[1] = w1;
+          mbar_arrive_expect_tx(&code_full[cs], gr.code_bytes);
+          bulk_load(c_slots + cs * kCodeSlot, p.code + gr.code_offset, gr.code_bytes, &code_full[cs]);
+        } else {
+          // This CTA's tile has no block for the group: no token holds a plane (first[j] = 128).
+          stash[0] = make_uint4(g, 0u, 0u, n_tok << 16);
           stash[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
           mbar_arrive(&code_full[cs]);
-          c_ended = true;
-        } else {
-          int desc;
-          const uint32_t g = cc.group(p, rank, desc);
-          const uint32_t n_tok = static_cast<uint32_t>(cc.tok[rank]);
-          if (desc >= 0) {
-            const GroupDesc* gd = &p.groups[desc];
-            const uint4* src = reinterpret_cast<const uint4*>(gd);
-            uint4 w0 = __ldg(src);
-            const uint4 w1 = __ldg(src + 1);
-            const GroupRegs gr = group_from_words(w0, w1);
-            if (gr.code_bytes > static_cast<uint32_t>(kCodeSlot - 32) ||
-                static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size ||
-                gr.group >= p.n_union_groups) {
-              record_error(p.status, kErrBadDescriptor);
-              *abort_flag = 1;
-              break;
-            }
-            w0.w = (w0.w & 0xFFFFu) | (n_tok << 16);  // pad0: the tile's token count
-            stash[0] = w0;
-            stash[1] = w1;
-            mbar_arrive_expect_tx(&code_full[cs], gr.code_bytes);
-            bulk_load(c_slots + cs * kCodeSlot, p.code + gr.code_offset, gr.code_bytes, &code_full[cs]);
-          } else {
-            // This CTA's tile has no block for the group: no token holds a plane (first[j] = 128).
-            stash[0] = make_uint4(g, 0u, 0u, n_tok << 16);
-            stash[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-            mbar_arrive(&code_full[cs]);
-          }
-          cc.advance(p, nblocks);
         }
+        cc.advance(p, nblocks);
         ++c_iter;
       }
-      if (*abort_flag && !c_ended) {
-        // Release the decode warps waiting on the next slot: an end mark once the slot is free.
+      // End marks in the next two slots, one for each decode set (also after an error, to release them).
+      for (int e = 0; e < 2; ++e) {
         const int cs = c_iter % kStagesC;
-        if (c_iter < kStagesC || mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitDrain)) {
-          uint4* stash = reinterpret_cast<uint4*>(c_slots + (cs + 1) * kCodeSlot - 32);
-          stash[0] = make_uint4(0u, 0u, 0u, kStashEnd << 24);
-          mbar_arrive(&code_full[cs]);
-          ++c_iter;
-        }
+        if (c_iter >= kStagesC &&
+            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitDrain))
+          break;
+        uint4* stash = reinterpret_cast<uint4*>(c_slots + (cs + 1) * kCodeSlot - 32);
+        stash[0] = make_uint4(0u, 0u, 0u, kStashEnd << 24);
+        stash[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+        mbar_arrive(&code_full[cs]);
+        ++c_iter;
       }
       // Drain: every plane-block copy this CTA issued has landed before the CTA can leave.
       for (int s = 0; s < kStagesC && s < static_cast<int>(c_iter); ++s) {
@@ -258,7 +274,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kErrWaitDrain);
       }
     }
-  } else if (warp == 18) {
+  } else if (warp == 2) {
     // ------------------------------------------------------------ basis producer
     if (lane == 0) {
       prefetch_tensormap(&bmap);
@@ -365,23 +381,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
     }
-  } else if (warp >= 2 && warp < 10) {
+  }
+  setmaxnreg_inc<kLaunchRegs>();
+  } else if (warp < 20) {
+    setmaxnreg_dec<kRegsDecode>();
     // ------------------------------------------------------------ decode warps (follow the slots)
-    const int u = tid - 64;
+    // Set 0 (warps 4-11) takes the even positions of the group sequence, set 1 (warps 12-19) the odd.
+    const int set = (warp - 4) >> 3;
+    const int u = tid - 128 - set * 256;
     const int r = u & 127;
     const int h = u >> 7;
-    uint32_t c_iter = 0, a_iter = 0;
-    while (true) {
-      const int cs = c_iter % kStagesC;
-      if (!mbar_wait(&code_full[cs], (c_iter / kStagesC) & 1, p.status, kErrWaitCodes)) {
+    for (uint32_t i = set;; i += 2) {  // position in the sequence: code slot i % kStagesC, A stage i % kStagesA
+      const int cs = i % kStagesC;
+      if (!mbar_wait(&code_full[cs], (i / kStagesC) & 1, p.status, kErrWaitCodes)) {
         *abort_flag = 1;
         break;
       }
       const uint8_t* slot = c_slots + cs * kCodeSlot;
       const uint4 w0 = *reinterpret_cast<const uint4*>(slot + kCodeSlot - 32);
       if ((w0.w >> 24) & kStashEnd) break;
-      const int sa = a_iter % kStagesA;
-      if (a_iter >= kStagesA && !mbar_wait(&a_empty[sa], ((a_iter / kStagesA) - 1) & 1, p.status, kErrWaitEmpty)) {
+      const int sa = i % kStagesA;
+      if (i >= static_cast<uint32_t>(kStagesA) &&
+          !mbar_wait(&a_empty[sa], ((i / kStagesA) - 1) & 1, p.status, kErrWaitEmpty)) {
         *abort_flag = 1;
         break;
       }
@@ -398,16 +419,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_arrive(&code_empty[cs]);
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(a_full_lead + sa * 8);
-      ++c_iter;
-      ++a_iter;
     }
-  } else if (warp >= 10 && warp < 18) {
+    setmaxnreg_inc<kLaunchRegs>();
+  } else {
+    setmaxnreg_inc<kRegsEpilogue>();
     // ------------------------------------------------------------ epilogue warps
-    // A warp reads the TMEM lane quarter (warp % 4); warps 10..13 and 14..17 each cover quarters
-    // 2, 3, 0, 1, the first four taking the first half of the item's KV heads, the others the second.
+    // A warp reads the TMEM lane quarter (warp % 4); warps 20..23 and 24..27 each cover quarters
+    // 0..3, the first four taking the first half of the item's KV heads, the others the second.
     const int r = (warp & 3) * 32 + lane;  // TMEM lane == tile token row
-    const int et = tid - 320;              // 0..255 within the epilogue group
-    const int head_half = (warp - 10) >> 2;
+    const int et = tid - 640;              // 0..255 within the epilogue group
+    const int head_half = (warp - 20) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t item_iter = 0;
     for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
@@ -442,6 +463,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int64_t m_s = p.seq_m[s];
         float* out_base = p.scores + p.seq_score_off[s];
         const int kv0 = nblk * kHeads;
+        const int h0 = head_half * kHalfHeads;  // first head of this half
         for (int qi = 0; qi < p.q_len; ++qi) {
           named_sync_pair(1, 256);
           for (int i = et; i < kHeads * G * D; i += 256) {
@@ -455,68 +477,81 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int i = et; i < kPairCols; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
           }
           named_sync_pair(1, 256);
+          float acc[kHalfHeads][G];
+#pragma unroll
+          for (int e = 0; e < kHalfHeads; ++e)
+#pragma unroll
+            for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
 #pragma unroll 1
-          for (int hh = head_half * kHalfHeads; hh < (head_half + 1) * kHalfHeads; ++hh) {
-            float acc[G];
+          for (int c = 0; c < D / 2; c += 16) {
+            // The token's cos / sin for these 16 dims, shared by every head of the half.
+            const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
+            const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
+            const uint4 cv[2] = {__ldg(cp), __ldg(cp + 1)};
+            const uint4 sv[2] = {__ldg(sp), __ldg(sp + 1)};
+            const __nv_bfloat162* cbv = reinterpret_cast<const __nv_bfloat162*>(cv);
+            const __nv_bfloat162* sbv = reinterpret_cast<const __nv_bfloat162*>(sv);
 #pragma unroll
-            for (int j = 0; j < G; ++j) acc[j] = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < D / 2; c += 16) {
-              uint32_t x1[16], x2[16];
-              if (accumulated) {
-                tmem_ld16(tmem + lane_base + hh * D + c, x1);
-                tmem_ld16(tmem + lane_base + hh * D + D / 2 + c, x2);
-              } else {
+            for (int hp = 0; hp < kHalfHeads; hp += 2) {
+              uint32_t x1[2][16], x2[2][16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) x1[i] = x2[i] = 0u;
-              }
-              const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
-              const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
-              const uint4 cv[2] = {__ldg(cp), __ldg(cp + 1)};
-              const uint4 sv[2] = {__ldg(sp), __ldg(sp + 1)};
-              const __nv_bfloat162* cbv = reinterpret_cast<const __nv_bfloat162*>(cv);
-              const __nv_bfloat162* sbv = reinterpret_cast<const __nv_bfloat162*>(sv);
-              if (accumulated) tmem_ld_wait();
-              const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
-              const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
+              for (int e = 0; e < 2; ++e) {
+                const int hh = h0 + hp + e;
+                if (accumulated) {
+                  tmem_ld16(tmem + lane_base + hh * D + c, x1[e]);
+                  tmem_ld16(tmem + lane_base + hh * D + D / 2 + c, x2[e]);
+                } else {
 #pragma unroll
-              for (int i = 0; i < 16; i += 2) {
-                const float2 cf = __bfloat1622float2(cbv[i / 2]);
-                const float2 sf = __bfloat1622float2(sbv[i / 2]);
-                const float4 ma = m1[i / 4], mb = m2[i / 4];
-                const float k1a = __uint_as_float(x1[i]) + ((i & 2) ? ma.z : ma.x);
-                const float k1b = __uint_as_float(x1[i + 1]) + ((i & 2) ? ma.w : ma.y);
-                const float k2a = __uint_as_float(x2[i]) + ((i & 2) ? mb.z : mb.x);
-                const float k2b = __uint_as_float(x2[i + 1]) + ((i & 2) ? mb.w : mb.y);
-                x1[i] = __float_as_uint(k1a * cf.x - k2a * sf.x);
-                x1[i + 1] = __float_as_uint(k1b * cf.y - k2b * sf.y);
-                x2[i] = __float_as_uint(k2a * cf.x + k1a * sf.x);
-                x2[i + 1] = __float_as_uint(k2b * cf.y + k1b * sf.y);
-              }
-#pragma unroll
-              for (int j = 0; j < G; ++j) {
-                const float4* q1 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + c);
-                const float4* q2 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + D / 2 + c);
-                float a = 0.f;
-#pragma unroll
-                for (int i = 0; i < 16; i += 4) {
-                  const float4 qa = q1[i / 4], qb = q2[i / 4];
-                  a += qa.x * __uint_as_float(x1[i]) + qa.y * __uint_as_float(x1[i + 1]) +
-                       qa.z * __uint_as_float(x1[i + 2]) + qa.w * __uint_as_float(x1[i + 3]);
-                  a += qb.x * __uint_as_float(x2[i]) + qb.y * __uint_as_float(x2[i + 1]) +
-                       qb.z * __uint_as_float(x2[i + 2]) + qb.w * __uint_as_float(x2[i + 3]);
+                  for (int i = 0; i < 16; ++i) x1[e][i] = x2[e][i] = 0u;
                 }
-                acc[j] += a;
+              }
+              if (accumulated) tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int hh = h0 + hp + e;
+                const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
+                const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                  const float2 cf = __bfloat1622float2(cbv[i / 2]);
+                  const float2 sf = __bfloat1622float2(sbv[i / 2]);
+                  const float4 ma = m1[i / 4], mb = m2[i / 4];
+                  const float k1a = __uint_as_float(x1[e][i]) + ((i & 2) ? ma.z : ma.x);
+                  const float k1b = __uint_as_float(x1[e][i + 1]) + ((i & 2) ? ma.w : ma.y);
+                  const float k2a = __uint_as_float(x2[e][i]) + ((i & 2) ? mb.z : mb.x);
+                  const float k2b = __uint_as_float(x2[e][i + 1]) + ((i & 2) ? mb.w : mb.y);
+                  x1[e][i] = __float_as_uint(k1a * cf.x - k2a * sf.x);
+                  x1[e][i + 1] = __float_as_uint(k1b * cf.y - k2b * sf.y);
+                  x2[e][i] = __float_as_uint(k2a * cf.x + k1a * sf.x);
+                  x2[e][i + 1] = __float_as_uint(k2b * cf.y + k1b * sf.y);
+                }
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                  const float4* q1 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + c);
+                  const float4* q2 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + D / 2 + c);
+                  float a = 0.f;
+#pragma unroll
+                  for (int i = 0; i < 16; i += 4) {
+                    const float4 qa = q1[i / 4], qb = q2[i / 4];
+                    a += qa.x * __uint_as_float(x1[e][i]) + qa.y * __uint_as_float(x1[e][i + 1]) +
+                         qa.z * __uint_as_float(x1[e][i + 2]) + qa.w * __uint_as_float(x1[e][i + 3]);
+                    a += qb.x * __uint_as_float(x2[e][i]) + qb.y * __uint_as_float(x2[e][i + 1]) +
+                         qb.z * __uint_as_float(x2[e][i + 2]) + qb.w * __uint_as_float(x2[e][i + 3]);
+                  }
+                  acc[hp + e][j] += a;
+                }
               }
             }
-            if (valid) {
+          }
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < kHalfHeads; ++e)
 #pragma unroll
               for (int j = 0; j < G; ++j) {
-                const int hq = (kv0 + hh) * G + j;
+                const int hq = (kv0 + h0 + e) * G + j;
                 out_base[(static_cast<int64_t>(hq) * p.q_len + qi) * m_s + tile.score_base + r] =
-                    hidden ? -INFINITY : acc[j] * p.scaling;
+                    hidden ? -INFINITY : acc[e][j] * p.scaling;
               }
-            }
           }
         }
       }
@@ -527,6 +562,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         ++item_iter;
       }
     }
+    setmaxnreg_dec<kLaunchRegs>();
   }
   tc_fence_before();
   __syncthreads();
@@ -540,6 +576,11 @@ static int launch_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int gri
   using L = PairSmem<RAW>;
   const int smem = 1024 + L::kQ + (kPairCols / D) * G * D * 4 + kPairCols * 4 + 48 * 8 + 16;
   if (smem > 232448) return kDkvErrConfig;
+  // The warpgroup register split assumes exactly kLaunchRegs per thread at launch; with any other
+  // count setmaxnreg.inc could wait for registers that never come, so refuse to launch.
+  cudaFuncAttributes fattr{};
+  if (cudaFuncGetAttributes(&fattr, key_scores_pair_kernel<D, G, RAW>) != cudaSuccess) return kDkvErrCuda;
+  if (fattr.numRegs != kLaunchRegs) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_pair_kernel<D, G, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return kDkvErrCuda;
