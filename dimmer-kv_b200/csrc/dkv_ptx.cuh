@@ -102,6 +102,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Rendezvous of a fixed group of threads on one of two mbarriers used alternately (each initialised
+// with the group's size), bounded like every other wait, so a thread that gave up on an earlier wait
+// never leaves the rest of the group blocked. n counts this thread's rendezvous so far.
+__device__ __forceinline__ bool group_sync(uint64_t* bars2, uint32_t& n, int* status, int code) {
+  uint64_t* bar = bars2 + (n & 1);
+  const uint32_t parity = (n >> 1) & 1;
+  ++n;
+  mbar_arrive(bar);
+  return mbar_wait(bar, parity, status, code);
+}
+
 // ---------------------------------------------------------------- copies
 // 1-D bulk copy global -> shared, completion counted on an mbarrier in bytes.
 // Both addresses 16-byte aligned, size a multiple of 16.

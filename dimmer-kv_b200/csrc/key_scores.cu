@@ -31,10 +31,6 @@ constexpr int kThreads = 576;  // producer, MMA, 8 decode warps, 8 epilogue warp
 constexpr int kStagesB = 2;
 constexpr int kATile = 16384;  // 128 rows x 128 B
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 // RAW: the stream holds raw (16-plane) blocks, which need 17 KB code slots; otherwise blocks hold at
 // most 8 planes (<= 8.75 KB) and the saved shared memory buys a third A stage and a fourth code slot.
 template <int NB, bool RAW>
@@ -117,7 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_empty = b_full + kStagesB;          // [kStagesB]
   uint64_t* accum_full = b_empty + kStagesB;
   uint64_t* accum_empty = accum_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_empty + 1);
+  uint64_t* ep_sync = accum_empty + 1;  // [2] epilogue rendezvous (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_sync + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -141,6 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(accum_full, 1);
     mbar_init(accum_empty, 256);
+    mbar_init(&ep_sync[0], 256);
+    mbar_init(&ep_sync[1], 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -307,8 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = tid - 320;                      // 0..255 within the epilogue group
     const int head_half = (warp - 10) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t item_iter = 0;
-    for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+    uint32_t item_iter = 0, n_sync = 0;
+    bool failed = false;
+    for (int k = items.k; k < items.end && !failed && !*abort_flag; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
         record_error(p.status, kErrBadDescriptor);
@@ -337,7 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* out_base = p.scores + p.seq_score_off[s];
       const int kv0 = nblk * kHeads;
       for (int qi = 0; qi < p.q_len; ++qi) {
-        named_sync(1, 256);
+        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+          *abort_flag = 1;
+          failed = true;
+          break;
+        }
         // Stage this query row for the block's heads, and the block's mean slice.
         for (int i = et; i < kHeads * G * D; i += 256) {
           const int hq = kv0 * G + i / D;  // query head
@@ -349,7 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       static_cast<int64_t>(p.layer) * p.n_cols + nblk * NB;
           for (int i = et; i < NB; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
         }
-        named_sync(1, 256);
+        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+          *abort_flag = 1;
+          failed = true;
+          break;
+        }
 #pragma unroll 1
         for (int hh = head_half * kHalfHeads; hh < (head_half ? kHeads : kHalfHeads); ++hh) {
           float acc[G];
@@ -427,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D, int NB, int G, bool RAW>
 static int launch_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   using L = KeySmem<NB, RAW>;
-  const int smem = 1024 + L::kQ + (NB / D) * G * D * 4 + NB * 4 + 24 * 8 + 16;
+  const int smem = 1024 + L::kQ + (NB / D) * G * D * 4 + NB * 4 + 24 * 8 + 32;
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_kernel<D, NB, G, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

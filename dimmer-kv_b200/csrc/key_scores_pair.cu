@@ -56,10 +56,6 @@ constexpr int kATilePair = 16384;           // 128 rows x 128 B
 constexpr int kBHalf = kHalfCols * 128;     // 128 basis rows x 64 components x bf16
 constexpr int kBStagePair = 2 * kBHalf;     // both MMA halves
 
-__device__ __forceinline__ void named_sync_pair(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 template <bool RAW>
 struct PairSmem {
   static constexpr int kStagesA = RAW ? 2 : 3;
@@ -160,7 +156,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* accum_full = b_empty + kStagesB;     // pair-MMA commit
   uint64_t* accum_empty = accum_full + 1;        // even CTA: 16 warp arrivals
   uint64_t* mma_done = accum_empty + 1;          // even CTA: every issued pair MMA has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* ep_sync = mma_done + 1;              // [2] epilogue rendezvous (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_sync + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -188,6 +185,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     mbar_init(accum_full, 1);
     mbar_init(accum_empty, 16);
     mbar_init(mma_done, 1);
+    mbar_init(&ep_sync[0], 256);
+    mbar_init(&ep_sync[1], 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -430,8 +429,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int et = tid - 640;              // 0..255 within the epilogue group
     const int head_half = (warp - 20) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t item_iter = 0;
-    for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+    uint32_t item_iter = 0, n_sync = 0;
+    bool failed = false;
+    for (int k = items.k; k < items.end && !*abort_flag && !failed; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
         record_error(p.status, kErrBadDescriptor);
@@ -465,7 +465,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int kv0 = nblk * kHeads;
         const int h0 = head_half * kHalfHeads;  // first head of this half
         for (int qi = 0; qi < p.q_len; ++qi) {
-          named_sync_pair(1, 256);
+          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+            *abort_flag = 1;
+            failed = true;
+            break;
+          }
           for (int i = et; i < kHeads * G * D; i += 256) {
             const int hq = kv0 * G + i / D;
             const int d = i % D;
@@ -476,7 +480,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                                         static_cast<int64_t>(p.layer) * p.n_cols + nblk * kPairCols;
             for (int i = et; i < kPairCols; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
           }
-          named_sync_pair(1, 256);
+          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+            *abort_flag = 1;
+            failed = true;
+            break;
+          }
           float acc[kHalfHeads][G];
 #pragma unroll
           for (int e = 0; e < kHalfHeads; ++e)
@@ -574,7 +582,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 template <int D, int G, bool RAW>
 static int launch_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   using L = PairSmem<RAW>;
-  const int smem = 1024 + L::kQ + (kPairCols / D) * G * D * 4 + kPairCols * 4 + 48 * 8 + 16;
+  const int smem = 1024 + L::kQ + (kPairCols / D) * G * D * 4 + kPairCols * 4 + 48 * 8 + 32;
   if (smem > 232448) return kDkvErrConfig;
   // The warpgroup register split assumes exactly kLaunchRegs per thread at launch; with any other
   // count setmaxnreg.inc could wait for registers that never come, so refuse to launch.
