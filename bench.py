@@ -268,6 +268,46 @@ def roofline(flops_layer: int, key_ms: list) -> dict:
             "algorithmic_flop_per_launch": flops_layer, "traffic": traffic}
 
 
+def unpack_rate(batch, device, launches: int = 5) -> dict:
+    """dkv_unpack of the batch's whole key and value streams to dense bf16 [tokens, union width]
+    (every token at its own plane count, zeros for groups its tile does not hold). Algorithmic bytes
+    per launch = packed blocks + descriptors read + dense rows written; both are far larger than L2.
+    Timed with CUDA events on the launching stream after 3 warm-up launches."""
+    import torch
+
+    from dimmerkv import _lib
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    lib = batch.lib
+    stream = torch.cuda.current_stream(device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    out = {}
+    for kind, packed in (("key", batch.keys), ("value", batch.values)):
+        dense = torch.empty(packed.n_tokens, packed.width, dtype=torch.bfloat16, device=device)
+        a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
+                            packed.groups.data_ptr(), dense.data_ptr(), packed.width, 1, status.data_ptr())
+        for _ in range(3):
+            _lib.check(lib.dkv_unpack(a, stream.cuda_stream), "dkv_unpack")
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(launches + 1)]
+        torch.cuda.synchronize(device)
+        ev[0].record(stream)
+        for i in range(launches):
+            _lib.check(lib.dkv_unpack(a, stream.cuda_stream), "dkv_unpack")
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(device)
+        _lib.check_device_status(status)
+        ms = statistics.mean(ev[i].elapsed_time(ev[i + 1]) for i in range(launches))
+        nbytes = packed.code.numel() + packed.groups.numel() + packed.tiles.numel() * 4 + dense.numel() * 2
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[kind] = {"ms": round(ms, 4), "bytes": int(nbytes), "code_bytes": int(packed.code.numel()),
+                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        del dense
+    out["peak_gbs"] = peak
+    out["peak_source"] = "of measured (hbm_gbs)" if peaks else "of fallback"
+    return out
+
+
 def run_kernels(args, cfg, device) -> dict:
     """Profiling case: every layer's dkv_attend_layer over the packed codes, random queries, no model."""
     import torch
@@ -307,7 +347,7 @@ def run_kernels(args, cfg, device) -> dict:
             "attention_tok_s": round(seqs * args.steps / elapsed, 2),
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
-            "gpu_launches": len(timer.events) * 4}
+            "gpu_launches": len(timer.events) * 4, "unpack": unpack_rate(batch, device)}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
@@ -559,6 +599,7 @@ def run_ours(args, cfg, rank, world, device):
         e2e = {"value": world * seqs * args.steps / float(t.item()), "unit": "tok/s",
                "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"]}
     dimmer.STATE.compressed = None
+    unpack = unpack_rate(batch, device) if rank == 0 else None
 
     result = None
     if rank == 0:
@@ -578,6 +619,7 @@ def run_ours(args, cfg, rank, world, device):
             "clocks": clk,
             "stage_ms_per_step": stage_ms,
             "gpu_launches": len(key_ms) * 4,
+            "unpack": unpack,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }

@@ -26,17 +26,22 @@ constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many 
 constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a component chunk
 }  // namespace
 
-__global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block) {
+__global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block,
+                                                                  int row_block, int n_row_blocks) {
   extern __shared__ float smem_f[];
   const int D = p.head_dim;
   const int D2 = D / 2;
   const int G = p.q_per_kv;
   const int chunk = blockIdx.x, kvh = blockIdx.y;
-  const int s0 = blockIdx.z * seq_block;
+  const int s0 = (blockIdx.z / n_row_blocks) * seq_block;
   const int n_s = min(seq_block, p.n_seq - s0);
   const int r0 = chunk * kRChunk;
-  const int rlo = max(p.row_begin, kvh * G * p.q_len);
-  const int rhi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  // Rows of this KV head inside the call, then this CTA's block of them (many query rows per head,
+  // few conversations: the rows are spread over more CTAs).
+  const int head_lo = max(p.row_begin, kvh * G * p.q_len);
+  const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  const int rlo = head_lo + static_cast<int>(blockIdx.z % n_row_blocks) * row_block;
+  const int rhi = min(head_hi, rlo + row_block);
   const int nr = rhi - rlo;
   if (nr <= 0 || n_s <= 0) return;
   __nv_bfloat162* bs = reinterpret_cast<__nv_bfloat162*>(smem_f);  // [kRChunk][D/2]
@@ -183,17 +188,23 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   if (p.n_seq == 0 || p.n_rows == 0) return kDkvOk;
   // Rows of one KV head inside this call: at most q_per_kv * q_len and at most n_rows.
   const int nr_max = min(p.n_rows, p.q_per_kv * p.q_len);
+  const int n_chunks = finalize_chunks(p.r_v);
+  const int n_kv = p.n_q_heads / p.q_per_kv;
+  // Many rows per KV head and few conversations (question-length queries): cut each head's rows into
+  // blocks of 16 so that the grid covers the SMs (a call's rows then span one or two KV heads).
+  int row_block = nr_max;
+  if (p.n_seq < kSeqBlock && nr_max > 16) row_block = 16;
+  const int n_row_blocks = (nr_max + row_block - 1) / row_block;
   const int basis_bytes = kRChunk * p.head_dim / 2 * 4;
-  const int per_seq = nr_max * kRChunk * 4;
+  const int per_seq = row_block * kRChunk * 4;
   const int seq_block = min(kSeqBlock, (200 * 1024 - basis_bytes) / per_seq);
   if (seq_block < 1) return kDkvErrConfig;
   const int smem = basis_bytes + seq_block * per_seq;
   if (cudaFuncSetAttribute(vbasis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kDkvErrCuda;
-  const int n_chunks = finalize_chunks(p.r_v);
-  const int n_kv = p.n_q_heads / p.q_per_kv;
-  vbasis_kernel<<<dim3(n_chunks, n_kv, (p.n_seq + seq_block - 1) / seq_block), kFinalizeThreads, smem, stream>>>(
-      p, seq_block);
+  const int seq_blocks = (p.n_seq + seq_block - 1) / seq_block;
+  vbasis_kernel<<<dim3(n_chunks, n_kv, seq_blocks * n_row_blocks), kFinalizeThreads, smem, stream>>>(
+      p, seq_block, row_block, n_row_blocks);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
   const int rows_per_head = min(p.n_rows, p.q_per_kv * p.q_len);
   const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + kCombineRows - 1) / kCombineRows);

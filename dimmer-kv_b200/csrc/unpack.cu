@@ -2,55 +2,214 @@
 //
 // Replaces progressive.dequantize (scripts/progressive.py:47-55) for a packed stream, and the
 // ladder decode of kvtc.quantize_groups (scripts/kvtc.py:78): every token of every tile is
-// decoded at its own plane count, one CTA per tile, two threads per token (32 components each).
-// Plane words are read straight from global memory with 128-bit loads per 4 words where
-// aligned; output rows are written in stream order, columns = union group * 64 + component.
+// decoded at its own plane count and written as a dense row of out_cols coefficients (stream
+// order; column = union group * 64 + component; zeros for groups the tile does not hold).
+//
+// One CTA per tile. A producer warp stages the tile's plane blocks into a ring of shared-memory
+// slots with cp.async.bulk (completion on mbarriers); eight decode warps take two threads per
+// token (32 components each), decode from shared memory, and write through a per-warp staging
+// buffer so that every store instruction covers whole 32-byte sectors: the kernel is bound by
+// the HBM write of the dense output (2 or 4 bytes per component) plus the code read.
 #include "dkv_format.cuh"
 #include "dkv_kernels.h"
 #include "dkv_ptx.cuh"
 
 namespace dkv {
 
-__global__ void __launch_bounds__(256) unpack_kernel(const UnpackParams p) {
-  const int ti = blockIdx.x;
-  const TileDesc tile = p.tiles[ti];
-  const int r = threadIdx.x & 127;
-  const int h = threadIdx.x >> 7;
-  if (tile.n_tokens < 1 || tile.n_tokens > kTileTokens) {
-    record_error(p.status, kErrBadDescriptor);
+namespace {
+
+constexpr int kUnpackSlots = 4;
+constexpr int kUnpackSlotBytes = 16896;  // largest block: 128 headers + 16 planes x 128 words
+constexpr int kUnpackDecodeThreads = 256;
+constexpr int kUnpackThreads = kUnpackDecodeThreads + 32;
+
+template <bool BF16>
+struct UnpackSmem {
+  static constexpr int kHalfBytes = BF16 ? 64 : 128;           // 32 components of one row
+  static constexpr int kStageWarp = 32 * kHalfBytes;           // one warp's 32 rows
+  static constexpr int kStage = kUnpackSlots * kUnpackSlotBytes;
+  static constexpr int kBars = kStage + 8 * kStageWarp;
+  static constexpr int kBytes = kBars + 2 * kUnpackSlots * 8 + 16;
+};
+
+// Store 32 rows x (32 components) held one row per lane (in regs, 16 B chunks) to global memory:
+// through the warp's staging buffer (chunk index XOR-swizzled against bank conflicts) so that each
+// store instruction writes whole sectors (4 lanes per 64-byte row half for bf16, 8 per 128 bytes
+// for fp32). Rows at or past n_valid are not written.
+template <bool BF16>
+__device__ __forceinline__ void store_rows(uint8_t* stage, const uint4 (&chunks)[UnpackSmem<BF16>::kHalfBytes / 16],
+                                           uint8_t* out_row0, int64_t row_stride_bytes, int lane, int n_valid) {
+  constexpr int kC = UnpackSmem<BF16>::kHalfBytes / 16;  // 4 (bf16) or 8 (fp32) chunks per row half
+  const int sw = BF16 ? ((lane >> 1) & 3) : (lane & 7);
+#pragma unroll
+  for (int c = 0; c < kC; ++c)
+    *reinterpret_cast<uint4*>(stage + lane * (kC * 16) + ((c ^ sw) * 16)) = chunks[c];
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < kC; ++j) {
+    const int k = lane + 32 * j;
+    const int row = k / kC;
+    const int c = k % kC;
+    const int swr = BF16 ? ((row >> 1) & 3) : (row & 7);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + row * (kC * 16) + ((c ^ swr) * 16));
+    if (row < n_valid) *reinterpret_cast<uint4*>(out_row0 + row * row_stride_bytes + c * 16) = v;
+  }
+  __syncwarp();
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store_zero_rows(uint8_t* out_row0, int64_t row_stride_bytes, int lane, int n_valid) {
+  constexpr int kC = UnpackSmem<BF16>::kHalfBytes / 16;
+#pragma unroll
+  for (int j = 0; j < kC; ++j) {
+    const int k = lane + 32 * j;
+    const int row = k / kC;
+    if (row < n_valid)
+      *reinterpret_cast<uint4*>(out_row0 + row * row_stride_bytes + (k % kC) * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+}  // namespace
+
+template <bool BF16>
+__global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackParams p) {
+  using S = UnpackSmem<BF16>;
+  constexpr int kC = S::kHalfBytes / 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  uint64_t* empty = full + kUnpackSlots;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kUnpackSlots);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const TileDesc tile = p.tiles[blockIdx.x];
+  const int n_union = static_cast<int>(p.out_cols / kGroup);
+  if (tile.n_tokens < 1 || tile.n_tokens > kTileTokens || tile.n_groups < 0 || tile.n_groups > n_union) {
+    if (tid == 0) record_error(p.status, kErrBadDescriptor);
+    return;  // uniform over the CTA: nothing initialised yet
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kUnpackSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kUnpackDecodeThreads);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer: blocks in tile order
+    if (lane == 0) {
+      int issued = 0;
+      for (int gi = 0; gi < tile.n_groups && !*abort_flag; ++gi) {
+        const GroupRegs gr = load_group(&p.groups[tile.group_base + gi]);
+        if (gr.code_bytes == 0 || gr.code_bytes > static_cast<uint32_t>(kUnpackSlotBytes) || (gr.code_bytes & 15u) ||
+            (gr.code_offset & 15u) || static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size) {
+          record_error(p.status, kErrBadDescriptor);
+          *abort_flag = 1;
+          break;
+        }
+        const int s = issued % kUnpackSlots;
+        if (issued >= kUnpackSlots &&
+            !mbar_wait(&empty[s], ((issued / kUnpackSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], gr.code_bytes);
+        bulk_load(smem + s * kUnpackSlotBytes, p.code + gr.code_offset, gr.code_bytes, &full[s]);
+        ++issued;
+      }
+      // Drain: the CTA must not exit with a copy into its shared memory in flight.
+      const int first = issued > kUnpackSlots ? issued - kUnpackSlots : 0;
+      for (int i = first; i < issued; ++i)
+        mbar_wait(&full[i % kUnpackSlots], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes);
+    }
     return;
   }
-  if (r >= tile.n_tokens) return;
-  const int64_t row = static_cast<int64_t>(tile.token_base + r);
-  for (int gi = 0; gi < tile.n_groups; ++gi) {
-    const GroupRegs gr = load_group(&p.groups[tile.group_base + gi]);
-    if (static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size ||
-        static_cast<int64_t>(gr.group + 1) * kGroup > p.out_cols) {
-      record_error(p.status, kErrBadDescriptor);
+
+  // -------------------------------------------------------------- decode warps
+  // Thread (r, h): token row r of the tile, components 32h..32h+31 of each group. Warp w holds rows
+  // 32 (w % 4) .. +31 of half h = w / 4 and stores them itself.
+  const int r = tid & 127;
+  const int h = tid >> 7;
+  const int row0 = (warp & 3) * 32;
+  const int n_valid = tile.n_tokens - row0;  // rows of this warp inside the tile (may be <= 0)
+  uint8_t* stage = smem + S::kStage + warp * S::kStageWarp;
+  const int64_t stride = p.out_cols * (BF16 ? 2 : 4);
+  uint8_t* out_base = reinterpret_cast<uint8_t*>(p.out) + (static_cast<int64_t>(tile.token_base) + row0) * stride +
+                      static_cast<int64_t>(h) * S::kHalfBytes;
+  int cursor = 0, consumed = 0;
+  int next_group = -1;
+  GroupRegs gr{};
+  if (tile.n_groups > 0) {
+    gr = load_group(&p.groups[tile.group_base]);
+    next_group = static_cast<int>(gr.group);
+  }
+  for (int g = 0; g < n_union; ++g) {
+    uint8_t* out_g = out_base + static_cast<int64_t>(g) * kGroup * (BF16 ? 2 : 4);
+    if (g != next_group) {
+      if (n_valid > 0) store_zero_rows<BF16>(out_g, stride, lane, n_valid);
+      continue;
+    }
+    const int s = consumed % kUnpackSlots;
+    // The warp leaves together (its stores end in __syncwarp): one lane giving up ends the warp.
+    const bool landed = mbar_wait(&full[s], (consumed / kUnpackSlots) & 1, p.status, kErrWaitCodes);
+    if (!__all_sync(0xffffffffu, landed)) {
+      *abort_flag = 1;
       return;
     }
-    const uint8_t* blk = p.code + gr.code_offset;
-    const int64_t col = static_cast<int64_t>(gr.group) * kGroup + 32 * h;
-    if (p.out_bf16) {
+    const uint8_t* blk = smem + s * kUnpackSlotBytes;
+    uint4 chunks[kC];
+    if (BF16) {
       uint32_t out[16];
       decode_half(blk, gr, tile.n_tokens, r, h, out);
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + row * p.out_cols + col);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) dst[k] = make_uint4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
+      for (int k = 0; k < 4; ++k) chunks[k] = make_uint4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
     } else {
       float out[32];
       decode_half_f32(blk, gr, tile.n_tokens, r, h, out);
-      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.out_cols + col);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) dst[k] = make_float4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
+      for (int k = 0; k < kC; ++k)
+        chunks[k] = make_uint4(__float_as_uint(out[4 * k]), __float_as_uint(out[4 * k + 1]),
+                               __float_as_uint(out[4 * k + 2]), __float_as_uint(out[4 * k + 3]));
+    }
+    mbar_arrive(&empty[s]);
+    ++consumed;
+    if (n_valid > 0) store_rows<BF16>(stage, chunks, out_g, stride, lane, n_valid);
+    // Next block of the tile: its group must come after this one (descriptors in union order).
+    ++cursor;
+    next_group = -1;
+    if (cursor < tile.n_groups) {
+      gr = load_group(&p.groups[tile.group_base + cursor]);
+      next_group = static_cast<int>(gr.group);
+      if (next_group <= g) {
+        record_error(p.status, kErrBadDescriptor);
+        *abort_flag = 1;
+        return;
+      }
     }
   }
+  if (cursor != tile.n_groups) record_error(p.status, kErrBadDescriptor);  // a group at or past out_cols / 64
 }
 
 int run_unpack(const UnpackParams& p, cudaStream_t stream) {
   if (p.n_tiles == 0) return kDkvOk;
-  if (p.out_cols % 64 != 0) return kDkvErrArgs;
-  unpack_kernel<<<p.n_tiles, 256, 0, stream>>>(p);
+  if (p.out_cols % 64 != 0 || p.out_cols <= 0) return kDkvErrArgs;
+  if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
+  if (p.out_bf16) {
+    const int smem = UnpackSmem<true>::kBytes + 128;
+    if (cudaFuncSetAttribute(unpack_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kDkvErrCuda;
+    unpack_kernel<true><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
+  } else {
+    const int smem = UnpackSmem<false>::kBytes + 128;
+    if (cudaFuncSetAttribute(unpack_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kDkvErrCuda;
+    unpack_kernel<false><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

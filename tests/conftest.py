@@ -2,8 +2,15 @@
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
+
+# The host math library picks its thread count per call under load unless told not to, and a float32
+# matmul's rounding then varies from run to run; the drop-in tests compare against fixtures made with
+# a fixed thread count.
+os.environ.setdefault("MKL_DYNAMIC", "FALSE")
+os.environ.setdefault("OMP_DYNAMIC", "FALSE")
 
 import numpy as np
 import pytest

@@ -37,9 +37,16 @@ def test_prog_encode_refine_match_reference(golden, tmp_path, tiny_model):
         assert compressed.used_bytes == int(fix["hot_bytes"])
         assert stored.cold_bytes == int(fix["cold_bytes"]) and stored.budget_bytes == int(fix["budget_bytes"])
         assert (stored.start, stored.end) == tuple(int(v) for v in fix["span"])
+        flipped = np.zeros(stored.end - stored.start, dtype=bool)
         for kind in ("key", "value"):
             s = stored.stores[kind]
-            assert np.array_equal(s.codes.numpy(), fix[f"codes_{kind}"])
+            # The codes quantise the float32 product (keys - mean) @ basis, whose last bit depends on the
+            # host BLAS's blocking; a coefficient on a bin edge may then land one bin over (quantize8 itself
+            # is pinned bit-exact on fixed coefficients in test_oracle_golden). Allow a few such codes.
+            diff = s.codes.numpy().astype(np.int32) - fix[f"codes_{kind}"].astype(np.int32)
+            assert np.abs(diff).max() <= 1 and (diff != 0).sum() <= max(4, diff.size // 10000), \
+                (kind, int((diff != 0).sum()))
+            flipped |= (diff != 0).any(axis=(1, 2))
             assert np.array_equal(s.low.numpy(), f16_from_bits(fix[f"low_{kind}"]))
             assert np.array_equal(s.span.numpy(), f16_from_bits(fix[f"lowspan_{kind}"]))
             assert np.array_equal(s.hot_pieces.numpy(), fix[f"hot_pieces_{kind}"])
@@ -52,7 +59,9 @@ def test_prog_encode_refine_match_reference(golden, tmp_path, tiny_model):
     assert fetched == int(fix["fetched"])
     rows = np.sort(fix["top"])
     got = np.stack([k[0][:, rows].contiguous().view(torch.int16).numpy().view(np.uint16) for k in new_keys])
-    assert np.array_equal(got, fix["refined_keys"])
+    same = ~flipped[rows - stored.start]  # rows whose codes all match the reference's
+    assert same.sum() >= len(rows) - 1
+    assert np.array_equal(got[:, :, same], fix["refined_keys"][:, :, same])
     assert stored.fetched_bytes(torch.from_numpy(rows)) == int(fix["fetched"])
 
 

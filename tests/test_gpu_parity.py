@@ -114,6 +114,7 @@ def test_unpack_all_plane_counts_random():
     m = np.sort(rng.choice([0, 1, 2, 3, 4, 5, 6, 7, 8], size=n))
     planes = np.repeat(m[:, None], g, axis=1).astype(np.uint8)
     planes[:, -1] = 0
+    planes[m < 5, 3] = 0  # group 3 held only by the later tiles: the earlier ones get zeros there
     codes = rng.integers(0, 256, size=(n, g, 64), dtype=np.uint8)
     low = (rng.standard_normal((n, g)) * 3).astype(np.float16)
     span = np.abs(rng.standard_normal((n, g)) * 2).astype(np.float16)
@@ -121,14 +122,19 @@ def test_unpack_all_plane_counts_random():
                            torch.from_numpy(planes), torch.from_numpy(m.astype(np.int64)))
     s = StreamCodes(tok.planes.to(DEV), tok.index.to(DEV), tok.header.to(DEV), torch.zeros(n, dtype=torch.int32, device=DEV))
     packed = pack_streams([s])
-    out = torch.zeros(n, packed.width, dtype=torch.float32, device=DEV)
-    status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
-                        packed.groups.data_ptr(), out.data_ptr(), packed.width, 0, status.data_ptr())
-    _lib.check(lib.dkv_unpack(a, torch.cuda.current_stream().cuda_stream), "dkv_unpack")
-    torch.cuda.synchronize()
+    assert not bool(packed.present[0, 3]) and bool(packed.present[-1, 3])
     want = oc.dequantize(codes, low, span, planes)[:, : packed.width]
-    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    for bf16 in (0, 1):
+        # Every element of every row is written (zeros where the tile holds no block of the group).
+        out = torch.full((n, packed.width), float("nan"), dtype=torch.bfloat16 if bf16 else torch.float32, device=DEV)
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
+                            packed.groups.data_ptr(), out.data_ptr(), packed.width, bf16, status.data_ptr())
+        _lib.check(lib.dkv_unpack(a, torch.cuda.current_stream().cuda_stream), "dkv_unpack")
+        torch.cuda.synchronize()
+        _lib.check_device_status(status)
+        ref = oc.round_bf16(want) if bf16 else want
+        assert np.array_equal(out.float().cpu().numpy().view(np.uint32), ref.view(np.uint32)), bf16
 
 
 def _random_conv(rng, n_mid, groups, start, pos_dtype=np.int64):
