@@ -286,7 +286,8 @@ def unpack_rate(batch, device, launches: int = 5) -> dict:
     for kind, packed in (("key", batch.keys), ("value", batch.values)):
         dense = torch.empty(packed.n_tokens, packed.width, dtype=torch.bfloat16, device=device)
         a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
-                            packed.groups.data_ptr(), dense.data_ptr(), packed.width, 1, status.data_ptr())
+                            packed.groups.data_ptr(), dense.data_ptr(), packed.width, 1, status.data_ptr(),
+                            packed.max_planes)
         for _ in range(3):
             _lib.check(lib.dkv_unpack(a, stream.cuda_stream), "dkv_unpack")
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(launches + 1)]
@@ -306,6 +307,53 @@ def unpack_rate(batch, device, launches: int = 5) -> dict:
     out["peak_gbs"] = peak
     out["peak_source"] = "of measured (hbm_gbs)" if peaks else "of fallback"
     return out
+
+
+def encode_rate(device, tokens: int = 16348, features: int = 28672, launches: int = 5) -> dict:
+    """dkv_encode_groups (quantize8 + per-rung errors of ProgressiveCodec.encode) on the largest cfg3
+    conversation's shape: 16348 middle tokens x 28672 features (3B: 28 layers x 8 KV heads x 128) of
+    seeded float32 coefficients, 12 rungs. Algorithmic bytes = coefficients read + codes, low, span,
+    rung sums and energies written; timed with CUDA events after 3 warm-up launches (inputs > L2)."""
+    import torch
+
+    from dimmerkv import _lib
+    from dimmerkv.encode import encode_groups
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    g = torch.Generator(device=device).manual_seed(77)
+    groups, rungs = features // 64, 12
+    scale = torch.logspace(1.5, -3, features, device=device)
+    coeff = torch.randn(tokens, features, generator=g, device=device) * scale
+    # Monotone plane counts per rung (each rung holds at least the previous one's planes).
+    steps = torch.randint(0, 2, (rungs, groups), generator=g, device=device)
+    rung_planes = steps.cumsum(0).clamp_max(8).to(torch.uint8)
+    rung_planes[-1] = 8
+    stream = torch.cuda.current_stream(device)
+    codes, low, span, rung_sum, energy = encode_groups(coeff, 64, rung_planes)  # checked once through the API
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    args = _lib.EncodeArgs(coeff.data_ptr(), coeff.stride(0), tokens, features, rung_planes.data_ptr(), rungs,
+                           codes.data_ptr(), low.data_ptr(), span.data_ptr(), rung_sum.data_ptr(), energy.data_ptr(),
+                           status.data_ptr())
+    lib = _lib.lib()
+    for _ in range(3):
+        _lib.check(lib.dkv_encode_groups(args, stream.cuda_stream), "dkv_encode_groups")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(launches + 1)]
+    torch.cuda.synchronize(device)
+    ev[0].record(stream)
+    for i in range(launches):
+        _lib.check(lib.dkv_encode_groups(args, stream.cuda_stream), "dkv_encode_groups")
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize(device)
+    _lib.check_device_status(status)
+    ms = statistics.mean(ev[i].elapsed_time(ev[i + 1]) for i in range(launches))
+    nbytes = tokens * features * 4 + tokens * features + 2 * tokens * groups * 2 + tokens * (rungs + 1) * 4
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del coeff
+    return {"kernel": "encode_groups (quantize8 + rung errors)", "tokens": tokens, "features": features,
+            "rungs": rungs, "ms": round(ms, 4), "bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "peak_gbs": peak,
+            "peak_source": "of measured (hbm_gbs)" if peaks else "of fallback"}
 
 
 def run_kernels(args, cfg, device) -> dict:
@@ -347,7 +395,8 @@ def run_kernels(args, cfg, device) -> dict:
             "attention_tok_s": round(seqs * args.steps / elapsed, 2),
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
-            "gpu_launches": len(timer.events) * 4, "unpack": unpack_rate(batch, device)}
+            "gpu_launches": len(timer.events) * 4, "unpack": unpack_rate(batch, device),
+            "encode": encode_rate(device)}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
@@ -600,6 +649,7 @@ def run_ours(args, cfg, rank, world, device):
                "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"]}
     dimmer.STATE.compressed = None
     unpack = unpack_rate(batch, device) if rank == 0 else None
+    encode = encode_rate(device) if rank == 0 else None
 
     result = None
     if rank == 0:
@@ -620,6 +670,7 @@ def run_ours(args, cfg, rank, world, device):
             "stage_ms_per_step": stage_ms,
             "gpu_launches": len(key_ms) * 4,
             "unpack": unpack,
+            "encode": encode,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }

@@ -364,8 +364,29 @@ int dkv_unpack(const dkv_unpack_args* a, void* stream) {
   p.out = a->out;
   p.out_cols = a->out_cols;
   p.out_bf16 = a->out_bf16;
+  p.max_planes = a->max_planes;
   p.status = a->status;
   return dkv::run_unpack(p, static_cast<cudaStream_t>(stream));
+}
+
+int dkv_encode_groups(const dkv_encode_args* a, void* stream) {
+  if (a == nullptr || a->coeff == nullptr || a->rung_planes == nullptr || a->codes == nullptr ||
+      a->low == nullptr || a->span == nullptr || a->rung_error == nullptr || a->status == nullptr)
+    return DKV_ERR_ARGS;
+  dkv::EncodeParams p{};
+  p.coeff = a->coeff;
+  p.coeff_stride = a->coeff_stride;
+  p.tokens = a->tokens;
+  p.features = a->features;
+  p.rung_planes = a->rung_planes;
+  p.n_rungs = a->n_rungs;
+  p.codes = a->codes;
+  p.low = a->low;
+  p.span = a->span;
+  p.rung_error = a->rung_error;
+  p.energy = a->energy;
+  p.status = a->status;
+  return dkv::run_encode(p, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

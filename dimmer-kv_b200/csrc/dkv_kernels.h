@@ -118,6 +118,22 @@ struct FinalizeParams {
 int finalize_chunks(int r_v);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);
 
+// Encode side of the progressive codec: quantize8 + per-rung errors (encode.cu).
+struct EncodeParams {
+  const float* coeff;
+  int64_t coeff_stride;
+  int tokens, features;
+  const uint8_t* rung_planes;   // [n_rungs][features / 64]
+  int n_rungs;
+  uint8_t* codes;               // [tokens][features]
+  uint16_t* low;                // [tokens][features / 64] f16 bits
+  uint16_t* span;
+  float* rung_error;            // [tokens][n_rungs]
+  float* energy;                // [tokens] or nullptr
+  int* status;
+};
+int run_encode(const EncodeParams& p, cudaStream_t stream);
+
 // Standalone ragged bit-plane unpack (unpack.cu).
 struct UnpackParams {
   const uint8_t* code;
@@ -128,6 +144,7 @@ struct UnpackParams {
   void* out;                      // [tokens][out_cols] fp32 or bf16, stream order
   int64_t out_cols;
   int out_bf16;
+  int max_planes;                 // 0: unknown (slots sized for raw blocks)
   int* status;
 };
 int run_unpack(const UnpackParams& p, cudaStream_t stream);

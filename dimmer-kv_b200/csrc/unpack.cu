@@ -19,15 +19,18 @@ namespace dkv {
 namespace {
 
 constexpr int kUnpackSlots = 4;
-constexpr int kUnpackSlotBytes = 16896;  // largest block: 128 headers + 16 planes x 128 words
 constexpr int kUnpackDecodeThreads = 256;
 constexpr int kUnpackThreads = kUnpackDecodeThreads + 32;
 
-template <bool BF16>
+// RAW: the stream holds raw (16-plane) blocks of up to 16896 bytes (128 headers + 16 planes x 128
+// words); otherwise blocks hold at most 8 planes (<= 8704 bytes) and the smaller slots let more CTAs
+// share an SM.
+template <bool BF16, bool RAW>
 struct UnpackSmem {
+  static constexpr int kSlotBytes = RAW ? 16896 : 8704;
   static constexpr int kHalfBytes = BF16 ? 64 : 128;           // 32 components of one row
   static constexpr int kStageWarp = 32 * kHalfBytes;           // one warp's 32 rows
-  static constexpr int kStage = kUnpackSlots * kUnpackSlotBytes;
+  static constexpr int kStage = kUnpackSlots * kSlotBytes;
   static constexpr int kBars = kStage + 8 * kStageWarp;
   static constexpr int kBytes = kBars + 2 * kUnpackSlots * 8 + 16;
 };
@@ -37,9 +40,9 @@ struct UnpackSmem {
 // store instruction writes whole sectors (4 lanes per 64-byte row half for bf16, 8 per 128 bytes
 // for fp32). Rows at or past n_valid are not written.
 template <bool BF16>
-__device__ __forceinline__ void store_rows(uint8_t* stage, const uint4 (&chunks)[UnpackSmem<BF16>::kHalfBytes / 16],
+__device__ __forceinline__ void store_rows(uint8_t* stage, const uint4 (&chunks)[BF16 ? 4 : 8],
                                            uint8_t* out_row0, int64_t row_stride_bytes, int lane, int n_valid) {
-  constexpr int kC = UnpackSmem<BF16>::kHalfBytes / 16;  // 4 (bf16) or 8 (fp32) chunks per row half
+  constexpr int kC = BF16 ? 4 : 8;  // 16-byte chunks per row half
   const int sw = BF16 ? ((lane >> 1) & 3) : (lane & 7);
 #pragma unroll
   for (int c = 0; c < kC; ++c)
@@ -59,7 +62,7 @@ __device__ __forceinline__ void store_rows(uint8_t* stage, const uint4 (&chunks)
 
 template <bool BF16>
 __device__ __forceinline__ void store_zero_rows(uint8_t* out_row0, int64_t row_stride_bytes, int lane, int n_valid) {
-  constexpr int kC = UnpackSmem<BF16>::kHalfBytes / 16;
+  constexpr int kC = BF16 ? 4 : 8;
 #pragma unroll
   for (int j = 0; j < kC; ++j) {
     const int k = lane + 32 * j;
@@ -71,9 +74,10 @@ __device__ __forceinline__ void store_zero_rows(uint8_t* out_row0, int64_t row_s
 
 }  // namespace
 
-template <bool BF16>
-__global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackParams p) {
-  using S = UnpackSmem<BF16>;
+template <bool BF16, bool RAW>
+__global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(const UnpackParams p) {
+  using S = UnpackSmem<BF16, RAW>;
+  constexpr int kUnpackSlotBytes = S::kSlotBytes;
   constexpr int kC = S::kHalfBytes / 16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -162,6 +166,10 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackPara
       return;
     }
     const uint8_t* blk = smem + s * kUnpackSlotBytes;
+    // The next block's descriptor, fetched now so that its latency hides behind this block's decode.
+    ++cursor;
+    GroupRegs gn{};
+    if (cursor < tile.n_groups) gn = load_group(&p.groups[tile.group_base + cursor]);
     uint4 chunks[kC];
     if (BF16) {
       uint32_t out[16];
@@ -180,10 +188,9 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackPara
     ++consumed;
     if (n_valid > 0) store_rows<BF16>(stage, chunks, out_g, stride, lane, n_valid);
     // Next block of the tile: its group must come after this one (descriptors in union order).
-    ++cursor;
     next_group = -1;
     if (cursor < tile.n_groups) {
-      gr = load_group(&p.groups[tile.group_base + cursor]);
+      gr = gn;
       next_group = static_cast<int>(gr.group);
       if (next_group <= g) {
         record_error(p.status, kErrBadDescriptor);
@@ -195,22 +202,24 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackPara
   if (cursor != tile.n_groups) record_error(p.status, kErrBadDescriptor);  // a group at or past out_cols / 64
 }
 
+template <bool BF16, bool RAW>
+static int launch_unpack(const UnpackParams& p, cudaStream_t stream) {
+  const int smem = UnpackSmem<BF16, RAW>::kBytes + 128;
+  if (cudaFuncSetAttribute(unpack_kernel<BF16, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return kDkvErrCuda;
+  unpack_kernel<BF16, RAW><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
 int run_unpack(const UnpackParams& p, cudaStream_t stream) {
   if (p.n_tiles == 0) return kDkvOk;
   if (p.out_cols % 64 != 0 || p.out_cols <= 0) return kDkvErrArgs;
   if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
-  if (p.out_bf16) {
-    const int smem = UnpackSmem<true>::kBytes + 128;
-    if (cudaFuncSetAttribute(unpack_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return kDkvErrCuda;
-    unpack_kernel<true><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
-  } else {
-    const int smem = UnpackSmem<false>::kBytes + 128;
-    if (cudaFuncSetAttribute(unpack_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return kDkvErrCuda;
-    unpack_kernel<false><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
-  }
-  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+  const bool raw = p.max_planes <= 0 || p.max_planes > 8;
+  if (p.out_bf16)
+    return raw ? launch_unpack<true, true>(p, stream) : launch_unpack<true, false>(p, stream);
+  return raw ? launch_unpack<false, true>(p, stream) : launch_unpack<false, false>(p, stream);
 }
 
 }  // namespace dkv

@@ -23,7 +23,7 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
            "dkv_attend_tail",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
-           "dkv_vpart_floats", "dkv_version", "dkv_status_string")
+           "dkv_vpart_floats", "dkv_encode_groups", "dkv_version", "dkv_status_string")
 
 
 class AttendArgs(ctypes.Structure):
@@ -59,6 +59,17 @@ class UnpackArgs(ctypes.Structure):
     _fields_ = [
         ("code", c_void_p), ("code_size", c_uint64), ("tiles", c_void_p), ("n_tiles", c_int32),
         ("groups", c_void_p), ("out", c_void_p), ("out_cols", c_int64), ("out_bf16", c_int32), ("status", c_void_p),
+        ("max_planes", c_int32),
+    ]
+
+
+class EncodeArgs(ctypes.Structure):
+    """Mirror of ``dkv_encode_args``."""
+
+    _fields_ = [
+        ("coeff", c_void_p), ("coeff_stride", c_int64), ("tokens", c_int32), ("features", c_int32),
+        ("rung_planes", c_void_p), ("n_rungs", c_int32), ("codes", c_void_p), ("low", c_void_p), ("span", c_void_p),
+        ("rung_error", c_void_p), ("energy", c_void_p), ("status", c_void_p),
     ]
 
 
@@ -115,7 +126,8 @@ def lib():
             fn.restype = c_int32
         handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
         handle.dkv_unpack.restype = c_int32
-        for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs)):
+        for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs),
+                         ("dkv_encode_groups", EncodeArgs)):
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(st), c_void_p]
             fn.restype = c_int32

@@ -22,6 +22,7 @@ import torch
 from . import dimmer
 from .codes import from_progressive
 from .common import build_cache
+from .encode import encode_groups
 from .kvtc import KVTCCodec, allocate_rungs, inverse_transform, rerotate, rope_tables
 
 PLANES = 8
@@ -149,7 +150,9 @@ class ProgressiveCodec:
     def encode(self, keys, values, budget: float, exact_recent: int, weights=None) -> "ProgressiveCache":
         """Quantise every middle token once and choose its hot prefix under the budget
         (progressive.py:135-172): the budget covers the exact tokens too; per-rung errors come from a
-        [tokens, groups, 9] table of errors at 0..8 planes; allocate_rungs picks the rungs."""
+        [tokens, groups, 9] table of errors at 0..8 planes; allocate_rungs picks the rungs. On a CUDA
+        device quantize8 and the per-rung errors are one kernel (dkv_encode_groups); the allocator stays
+        on the host side, as in the reference."""
         base, tokens = self.base, keys[0].shape[2]
         start = min(base.sinks, tokens)
         end = max(start, tokens - exact_recent)
@@ -162,18 +165,24 @@ class ProgressiveCodec:
             stream, order = base.streams[kind], self.orders[kind]
             matrix = base.to_matrix(tensors, kind, cos, sin)
             coefficients = (matrix[start:end] - stream.mean) @ stream.basis
-            codes, low, span = quantize8(coefficients, base.group)
-            energy = coefficients.square().sum(dim=1).mean().clamp_min(1e-12)
-            grouped = coefficients.view(middle, -1, base.group)
-            groups = grouped.shape[1]
-            table = torch.stack([
-                (grouped - dequantize(codes, low, span, torch.full((1, groups), m, device=self.device))
-                 .view_as(grouped)).square().sum(dim=-1)
-                for m in range(PLANES + 1)
-            ], dim=-1)
-            rung_planes = order.planes[order.rungs].long().T
-            rung_error = table.gather(2, rung_planes[None].expand(middle, -1, -1)).sum(dim=1) / energy
-            del table, grouped
+            if coefficients.is_cuda:
+                # One kernel: codes, low, span and the per-rung error sums (dkv_encode_groups).
+                codes, low, span, rung_sum, token_energy = encode_groups(
+                    coefficients, base.group, order.planes[order.rungs])
+                rung_error = rung_sum / token_energy.mean().clamp_min(1e-12)
+            else:
+                codes, low, span = quantize8(coefficients, base.group)
+                energy = coefficients.square().sum(dim=1).mean().clamp_min(1e-12)
+                grouped = coefficients.view(middle, -1, base.group)
+                groups = grouped.shape[1]
+                table = torch.stack([
+                    (grouped - dequantize(codes, low, span, torch.full((1, groups), m, device=self.device))
+                     .view_as(grouped)).square().sum(dim=-1)
+                    for m in range(PLANES + 1)
+                ], dim=-1)
+                rung_planes = order.planes[order.rungs].long().T
+                rung_error = table.gather(2, rung_planes[None].expand(middle, -1, -1)).sum(dim=1) / energy
+                del table, grouped
             if weights is not None:
                 importance = weights[start:end].float()
                 rung_error = rung_error * (importance / importance.mean().clamp_min(1e-12))[:, None]

@@ -167,7 +167,9 @@ int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_scores, void*
 
 /* Ragged bit-plane unpack of a packed stream to dense coefficients (stream order).
  * Replaces progressive.dequantize (scripts/progressive.py:47-55) and the ladder decode of
- * kvtc.quantize_groups (scripts/kvtc.py:78). */
+ * kvtc.quantize_groups (scripts/kvtc.py:78). Every element of the out rows is written: a token's
+ * groups at its own plane count, zeros for union groups its tile holds no block of. `out` must be
+ * 16-byte aligned. */
 typedef struct dkv_unpack_args {
   const uint8_t* code;
   uint64_t code_size;
@@ -178,6 +180,7 @@ typedef struct dkv_unpack_args {
   int64_t out_cols;
   int32_t out_bf16;              /* 1: bf16 (the reference's .to(dtype)), 0: fp32 */
   int* status;
+  int32_t max_planes;            /* largest plane count of any block (16: raw bf16 blocks); 0: unknown */
 } dkv_unpack_args;
 int dkv_unpack(const dkv_unpack_args* args, void* stream);
 
@@ -230,6 +233,30 @@ typedef struct dkv_refine_args {
   int* status;
 } dkv_refine_args;
 int dkv_refine_merge(const dkv_refine_args* args, void* stream);
+
+/* Encode side of the progressive codec, on the GPU: quantize8 of every (token, group of 64) and the
+ * squared error of each token at each rung of the progressive order. Replaces quantize8
+ * (scripts/progressive.py:37-44) and the error table of ProgressiveCodec.encode
+ * (scripts/progressive.py:152-163): the reference's [tokens, groups, 9] table of errors at 0..8 planes,
+ * gathered at the rungs' plane counts and summed over groups, is produced without the table.
+ * codes / low / span are bit-exact with quantize8 on the same float32 coefficients; rung_error and
+ * energy are float32 sums (fixed order) of the same squared differences. The caller divides rung_error
+ * by the mean energy and runs the (host) allocator, as the reference does. */
+typedef struct dkv_encode_args {
+  const float* coeff;            /* [tokens][coeff_stride] float32, 16-byte aligned rows */
+  int64_t coeff_stride;          /* elements between rows, multiple of 4 */
+  int32_t tokens;
+  int32_t features;              /* multiple of 64; groups = features / 64 */
+  const uint8_t* rung_planes;    /* [n_rungs][groups]: planes (0..8) of each group at each rung */
+  int32_t n_rungs;               /* 1..32 */
+  uint8_t* codes;                /* [tokens][features]: the 8-bit codes (4-byte aligned) */
+  uint16_t* low;                 /* [tokens][groups]: f16 bits of the group minimum */
+  uint16_t* span;                /* [tokens][groups]: f16 bits of max(max - low, 1e-8) */
+  float* rung_error;             /* [tokens][n_rungs]: sum over groups of the squared error at the rung */
+  float* energy;                 /* [tokens]: sum of squared coefficients (NULL: not written) */
+  int* status;
+} dkv_encode_args;
+int dkv_encode_groups(const dkv_encode_args* args, void* stream);
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int dkv_version(void);

@@ -149,3 +149,28 @@ def prog_piece_bytes(planes: np.ndarray) -> np.ndarray:
     """Hot bytes of a per-(token, group) plane count: 8 B per plane + 4 B header (progressive.py:11-12)."""
     p = np.asarray(planes, dtype=np.int64)
     return 8 * p + HEADER_BYTES * (p > 0)
+
+
+def encode_tables(coefficients: np.ndarray, group: int, rung_planes: np.ndarray):
+    """The error side of ProgressiveCodec.encode (scripts/progressive.py:152-163) for one stream.
+
+    ``rung_planes`` [n_rungs, groups]: planes of each group at each rung (order.planes[order.rungs]).
+    Returns (codes, low, span, table, rung_error, energy) with table [tokens, groups, 9] the squared
+    error of each (token, group) decoded at 0..8 planes (lines 155-159), rung_error [tokens, n_rungs]
+    its gather at the rungs' plane counts summed over groups (line 161) before the division by the
+    energy, and energy [tokens] the sum of squared coefficients (line 153 before its mean). float32
+    throughout, sums in numpy's order.
+    """
+    x = np.asarray(coefficients, dtype=np.float32)
+    codes, low, span = quantize8(x, group)
+    tokens, groups, _ = codes.shape
+    grouped = x.reshape(tokens, groups, group)
+    table = np.stack([
+        np.square(grouped - dequantize(codes, low, span, np.full((1, groups), m)).reshape(grouped.shape)).sum(axis=-1)
+        for m in range(PLANES + 1)
+    ], axis=-1).astype(np.float32)
+    rp = np.asarray(rung_planes, dtype=np.int64)                      # [n_rungs, groups]
+    gathered = np.take_along_axis(table, rp.T[None].repeat(tokens, axis=0), axis=2)  # [tokens, groups, rungs]
+    rung_error = gathered.sum(axis=1, dtype=np.float32)
+    energy = np.square(x).sum(axis=1, dtype=np.float32)
+    return codes, low, span, table, rung_error, energy

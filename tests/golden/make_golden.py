@@ -1,7 +1,8 @@
 """Write the golden fixtures of this directory by running the REFERENCE code on seeded inputs.
 
 Usage (only where the reference checkout exists; the GPU box does not have it):
-    DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py
+    DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py [fixture ...]
+(no names: every fixture; names such as ``encode`` or ``codes``: only those).
 
 Every array saved here is produced by the reference's own functions (scripts/progressive.py,
 scripts/kvtc.py, scripts/compressed_attention.py, scripts/dimmer.py, scripts/methods.py,
@@ -69,11 +70,50 @@ def allocator_fixture(out: Path) -> None:
                         middle=middle, budget=8000, chosen=chosen.numpy())
 
 
+def encode_fixture(out: Path) -> None:
+    """The error side of ProgressiveCodec.encode (progressive.py:150-163) on seeded coefficients: the
+    reference's quantize8 / dequantize / build_order, and encode's table, gather and sums written out
+    line by line (they are inline in encode, not a function of their own)."""
+    g = torch.Generator().manual_seed(21)
+    scales = torch.logspace(1.5, -3, 1024)[None]
+    calib = torch.randn(200, 1024, generator=g) * scales
+    coeff = torch.randn(300, 1024, generator=g) * scales
+    coeff[7, :64] = 0.0             # constant group: span rounds to 0
+    coeff[8, 64:128] = -1.5         # constant non-zero group
+    coeff[9, 128:192] *= 1e-6       # tiny span
+    coeff[10, 192:256] *= 1e3       # wide span (still inside the f16 range)
+    order = progressive.build_order(calib, 64, TARGETS, 2 * 1024)
+    codes, low, span = progressive.quantize8(coeff, 64)
+    middle, groups = coeff.shape[0], 16
+    grouped = coeff.view(middle, -1, 64)
+    table = torch.stack([
+        (grouped - progressive.dequantize(codes, low, span, torch.full((1, groups), m)).view_as(grouped))
+        .square().sum(dim=-1)
+        for m in range(progressive.PLANES + 1)
+    ], dim=-1)
+    rung_planes = order.planes[order.rungs].long().T
+    rung_sum = table.gather(2, rung_planes[None].expand(middle, -1, -1)).sum(dim=1)
+    token_energy = coeff.square().sum(dim=1)
+    energy = token_energy.mean().clamp_min(1e-12)
+    np.savez_compressed(
+        out / "encode.npz", coeff=coeff.numpy(), rung_planes=order.planes[order.rungs].numpy(),
+        rungs=np.array(order.rungs), codes=codes.numpy(), low=bits16(low), span=bits16(span),
+        table=table.numpy(), rung_sum=rung_sum.numpy(), token_energy=token_energy.numpy(),
+        rung_error=(rung_sum / energy).numpy(),
+    )
+
+
 def main() -> None:
     out = HERE
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    only = sys.argv[1:]
+    if only:  # e.g. `make_golden.py encode`: write just the named fixtures
+        for name in only:
+            globals()[f"{name}_fixture"](out)
+        return
     codes_fixture(out)
     allocator_fixture(out)
+    encode_fixture(out)
 
     model = tm.build_model(torch.bfloat16)
     dimmer.install(model)

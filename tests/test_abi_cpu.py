@@ -1,0 +1,46 @@
+"""The C ABI without a GPU: the built library loads on the host and exports every entry point that
+include/dimmer_kv.h declares, and the ctypes binding covers exactly those (no kernel is called)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from dimmerkv import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "dimmer_kv.h"
+
+
+def declared() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(dkv_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_entry_points():
+    names = declared()
+    assert {"dkv_attend_layer", "dkv_unpack", "dkv_encode_groups", "dkv_topk"} <= names
+    assert names == set(_lib.EXPORTS)
+
+
+@pytest.mark.skipif(not _lib.LIB_PATH.exists(), reason="library not built (dimmer-kv_b200/build_lib.py)")
+def test_library_exports_every_declared_symbol():
+    handle = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [name for name in sorted(declared()) if not hasattr(handle, name)]
+    assert not missing, missing
+    lib = _lib.lib()
+    assert lib.dkv_version() >= 100
+    assert lib.dkv_status_string(1) == b"invalid argument"
+
+
+def test_struct_mirrors_match_the_header_field_counts():
+    """Each ctypes mirror lists as many fields as the C struct declares (catches a field added on one side)."""
+    text = HEADER.read_text()
+    for struct, mirror in (("dkv_attend_args", _lib.AttendArgs), ("dkv_unpack_args", _lib.UnpackArgs),
+                           ("dkv_encode_args", _lib.EncodeArgs)):
+        body = re.search(r"typedef struct " + struct + r" \{(.*?)\} " + struct + ";", text, flags=re.S).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        fields = [f for stmt in body.split(";") if stmt.strip() for f in stmt.split(",")]
+        assert len(fields) == len(mirror._fields_), (struct, len(fields), len(mirror._fields_))

@@ -95,7 +95,8 @@ def test_unpack_bit_exact(golden):
             out = torch.zeros(packed.n_tokens, packed.width, dtype=torch.bfloat16 if bf16 else torch.float32, device=DEV)
             status = torch.zeros(1, dtype=torch.int32, device=DEV)
             a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
-                                packed.groups.data_ptr(), out.data_ptr(), packed.width, bf16, status.data_ptr())
+                                packed.groups.data_ptr(), out.data_ptr(), packed.width, bf16, status.data_ptr(),
+                                packed.max_planes)
             _lib.check(lib.dkv_unpack(a, torch.cuda.current_stream().cuda_stream), "dkv_unpack")
             torch.cuda.synchronize()
             _lib.check_device_status(status)
@@ -124,17 +125,19 @@ def test_unpack_all_plane_counts_random():
     packed = pack_streams([s])
     assert not bool(packed.present[0, 3]) and bool(packed.present[-1, 3])
     want = oc.dequantize(codes, low, span, planes)[:, : packed.width]
-    for bf16 in (0, 1):
+    for bf16, max_planes in ((0, 0), (1, 0), (0, packed.max_planes), (1, packed.max_planes)):
         # Every element of every row is written (zeros where the tile holds no block of the group).
+        # max_planes 0: slots sized for raw blocks; the stream's own maximum (<= 8): the smaller slots.
         out = torch.full((n, packed.width), float("nan"), dtype=torch.bfloat16 if bf16 else torch.float32, device=DEV)
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
         a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
-                            packed.groups.data_ptr(), out.data_ptr(), packed.width, bf16, status.data_ptr())
+                            packed.groups.data_ptr(), out.data_ptr(), packed.width, bf16, status.data_ptr(),
+                            max_planes)
         _lib.check(lib.dkv_unpack(a, torch.cuda.current_stream().cuda_stream), "dkv_unpack")
         torch.cuda.synchronize()
         _lib.check_device_status(status)
         ref = oc.round_bf16(want) if bf16 else want
-        assert np.array_equal(out.float().cpu().numpy().view(np.uint32), ref.view(np.uint32)), bf16
+        assert np.array_equal(out.float().cpu().numpy().view(np.uint32), ref.view(np.uint32)), (bf16, max_planes)
 
 
 def _random_conv(rng, n_mid, groups, start, pos_dtype=np.int64):

@@ -35,6 +35,20 @@ def test_ladder_bit_exact(golden):
     assert np.array_equal(again[finite].view(np.uint32), want[finite].view(np.uint32))
 
 
+def test_encode_tables_match_reference(golden):
+    """quantize8 + the error table / rung sums of ProgressiveCodec.encode (progressive.py:150-163)."""
+    g = golden("encode")
+    codes, low, span, table, rung_sum, energy = oc.encode_tables(g["coeff"], 64, g["rung_planes"])
+    assert np.array_equal(codes, g["codes"])
+    assert np.array_equal(low.view(np.uint16), g["low"])
+    assert np.array_equal(span.view(np.uint16), g["span"])
+    # float32 sums in another order: relative to the row's largest entry.
+    assert np.all(np.abs(table - g["table"]) <= 1e-5 * np.abs(g["table"]).max(axis=-1, keepdims=True) + 1e-30)
+    assert np.all(np.abs(rung_sum - g["rung_sum"]) <= 1e-5 * np.abs(g["rung_sum"]).max(axis=-1, keepdims=True))
+    assert np.allclose(energy, g["token_energy"], rtol=1e-5)
+    assert np.allclose(rung_sum / energy.mean(), g["rung_error"], rtol=1e-4)
+
+
 def test_bf16_rounding_matches_torch():
     import torch
     x = torch.randn(10000) * torch.logspace(-30, 30, 10000)
