@@ -204,6 +204,8 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
   p.status = a->status;
   p.cta_begin = a->v_cta_begin;
   p.item_order = a->v_item_order;
+  p.p_img = a->p_img;
+  p.n_tiles = a->n_v_tiles;
   if ((a->v_item_order != nullptr && a->v_cta_begin == nullptr) || (a->v_cta_begin != nullptr && a->grid_v <= 0))
     return DKV_ERR_ARGS;
   const int grid = a->grid_v > 0 ? a->grid_v : (a->n_v_items < sm_count() ? a->n_v_items : sm_count());

@@ -93,6 +93,8 @@ struct ValueWeightParams {
   int* status;
   const int32_t* cta_begin;       // optional static schedule: CTA b takes item_order[cta_begin[b] .. cta_begin[b+1])
   const int32_t* item_order;
+  uint8_t* p_img;                 // optional [n_tiles][2][n_rows_pad][128 B]: P^T images (vprobs_kernel)
+  int n_tiles;                    // value tiles (with p_img)
 };
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream);
 

@@ -74,5 +74,6 @@ extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_sc
   a.p_exact = reinterpret_cast<float*>(p + scores_bytes + stats_bytes);
   a.partial = reinterpret_cast<float*>(p + scores_bytes + stats_bytes + exact_bytes);
   a.vpart = reinterpret_cast<float*>(p + scores_bytes + stats_bytes + exact_bytes + partial_bytes);
+  a.p_img = nullptr;  // the value kernel builds its probability tiles itself
   return dkv_attend_layer(&a, stream);
 }

@@ -5,19 +5,23 @@
 //   p_c = softmax(...)[..., :middle].to(dtype)
 //   weighted += einsum("bhgqn,nr->bhgqr", p_c[..., block.index], block.coefficients)
 // for a batch of conversations. One work item = (conversation, run of value tiles, range of
-// union groups). Two sets of 8 worker warps share every tile:
-//   - both build P^T (rows = query head x query row, K = the tile's 128 tokens; each set half of
-//     the rows) in bf16 from the fp32 scores and the softmax statistics (exactly the reference's
-//     rounding of p to the cache dtype), 128B-swizzled K-major;
-//   - they decode alternate pairs of coefficient groups (pair ordinal k of a tile goes to set
-//     k % 2, into that set's own ring of A tiles) into 128-component x 128-token bf16 tiles
-//     (MN-major operand: token rows of 64 components, 128B swizzle), so two decodes are in flight.
+// union groups). Two sets of 8 worker warps share every tile: they decode alternate pairs of
+// coefficient groups (pair ordinal k of a tile goes to set k % 2, into that set's own ring of A
+// tiles) into 128-component x 128-token bf16 tiles (MN-major operand: token rows of 64 components,
+// 128B swizzle), so two decodes are in flight. The B operand is P^T (rows = query head x query row,
+// K = the tile's 128 tokens) in bf16, exactly the reference's rounding of p to the cache dtype,
+// 128B-swizzled K-major: with p_img (PIMG) vprobs_kernel builds it once per value tile and call (it is
+// the same for every group range of a tile) and a producer fetches it with one bulk copy; without, both
+// worker sets build it in shared memory from the fp32 scores and the softmax statistics.
 // The MMA warp accumulates D[128 components, rows] += C^T P^T with tcgen05 (M=128, N=rows,
-// K=16 tokens per instruction) into one TMEM column range per group pair. At the end of the
-// item the accumulators are written to `partial` (fp32), which finalize.cu reduces.
-// The producer copies each tile's descriptors (the host lists, per item and tile, the range of
-// descriptors inside the item's groups) into shared memory with one bulk copy; every role walks
-// the group pairs there, and the producer streams the code blocks into a ring of slots.
+// K=16 tokens per instruction) into one TMEM column range per group pair, inside one of two
+// 256-column accumulators that consecutive items alternate between. At the end of an item warps 4, 5,
+// 14 and 15 (one per TMEM lane quarter, two from each set) write its accumulator to `partial` (fp32,
+// reduced by finalize.cu) while the next item accumulates into the other.
+// Producers: warp 19 copies each tile's P image and its descriptors (the host lists, per item and
+// tile, the range of descriptors inside the item's groups) into shared memory with bulk copies; every
+// role walks the group pairs there; warps 0 and 18 stream the code blocks of set 0's and set 1's pairs
+// into one ring of slots each, so a set never waits on a slot the other set still holds.
 #include "dkv_ptx.cuh"
 #include "dkv_format.cuh"
 #include "dkv_kernels.h"
@@ -26,13 +30,16 @@ namespace dkv {
 
 namespace {
 
-constexpr int kVThreads = 576;    // producer, MMA, worker set 0 (warps 2-9; 4-7 also epilogue), set 1 (10-17)
+// Warps: 0 and 18 code producers (one ring per worker set), 1 MMA, 2-9 worker set 0, 10-17 worker set
+// 1 (4, 5, 14, 15 also drain the accumulators), 19 P-image / descriptor producer.
+constexpr int kVThreads = 640;
 constexpr int kPairTile = 32768;  // two groups x 128 tokens x 128 B
 constexpr int kMaxRangeGroups = 64;
+constexpr int kAccumCols = 256;   // TMEM columns of one item's accumulator (two alternate in the 512)
 
 template <bool RAW>
 struct ValueSmem {
-  static constexpr int kCodeSlots = RAW ? 3 : 6;
+  static constexpr int kCodeSlots = RAW ? 2 : 3;  // per worker set
   static constexpr int kCodeSlot = RAW ? 17408 : 8960;
 };
 
@@ -53,7 +60,40 @@ __device__ __forceinline__ int next_pair(const GroupDesc* d, int n, int g0, int&
 
 }  // namespace
 
-template <bool RAW>
+// One CTA per value tile: the tile's P^T image for the call's rows (bf16 probabilities, rounded as the
+// reference rounds p to the cache dtype, compressed_attention.py:127), laid out exactly as the MMA's
+// B operand sits in shared memory (two atoms of 64 tokens, n_rows_pad rows x 128 B, 128B swizzle),
+// built in shared memory and written out whole.
+__global__ void __launch_bounds__(256) vprobs_kernel(const ValueWeightParams p) {
+  extern __shared__ __align__(16) uint8_t img[];  // [2][NR][128]
+  const int NR = p.n_rows_pad;
+  const int t = blockIdx.x;
+  const TileDesc tile = p.tiles[t];
+  const bool tile_ok = tile.n_tokens >= 1 && tile.n_tokens <= kTileTokens;
+  if (!tile_ok && threadIdx.x == 0) record_error(p.status, kErrBadDescriptor);
+  const int s = tile.seq;
+  const int r = threadIdx.x & 127;
+  const bool tok_ok = tile_ok && r < tile.n_tokens;
+  const int64_t m_s = tile_ok ? p.seq_m[s] : 0;
+  const float* sc = p.scores + (tile_ok ? p.seq_score_off[s] : 0);
+  const int sidx = tok_ok ? p.tok_sidx[tile.token_base + r] : 0;
+  const int atom = r >> 6, chunk = (r & 63) >> 3, within = (r & 7) * 2;
+  for (int n = threadIdx.x >> 7; n < NR; n += 2) {
+    float prob = 0.f;
+    if (tok_ok && n < p.n_rows) {
+      const float x = sc[static_cast<int64_t>(p.row_begin + n) * m_s + sidx];
+      const float* st = p.row_stats + (static_cast<int64_t>(s) * p.n_q_heads * p.q_len + p.row_begin + n) * 4;
+      prob = (x == -INFINITY) ? 0.f : expf(x - st[0]) * st[1];
+    }
+    *reinterpret_cast<__nv_bfloat16*>(img + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
+        __float2bfloat16_rn(prob);
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(p.p_img + static_cast<int64_t>(t) * NR * 256);
+  for (int i = threadIdx.x; i < NR * 16; i += blockDim.x) dst[i] = reinterpret_cast<const uint4*>(img)[i];
+}
+
+template <bool RAW, bool PIMG>
 __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const ValueWeightParams p, int a_slots) {
   using L = ValueSmem<RAW>;
   constexpr int kCodeSlots = L::kCodeSlots;
@@ -66,20 +106,20 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   uint8_t* p_tiles = a_tiles + 2 * a_slots * kPairTile;                 // [2][p_tile]
   GroupDesc* descs = reinterpret_cast<GroupDesc*>(p_tiles + 2 * p_tile);  // [2][kMaxRangeGroups]
   float* stats_s = reinterpret_cast<float*>(descs + 2 * kMaxRangeGroups);  // [3][128][2] max, 1/sum
-  uint8_t* c_slots = reinterpret_cast<uint8_t*>(stats_s + 3 * 256);        // [kCodeSlots][kCodeSlot]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(c_slots + kCodeSlots * kCodeSlot);
-  uint64_t* code_full = bars;
-  uint64_t* code_empty = code_full + kCodeSlots;
-  uint64_t* a_full = code_empty + kCodeSlots;  // [2 sets][2]
+  uint8_t* c_slots = reinterpret_cast<uint8_t*>(stats_s + 3 * 256);        // [2 sets][kCodeSlots][kCodeSlot]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(c_slots + 2 * kCodeSlots * kCodeSlot);
+  uint64_t* code_full = bars;                       // [2 sets][kCodeSlots]
+  uint64_t* code_empty = code_full + 2 * kCodeSlots;  // [2 sets][kCodeSlots]
+  uint64_t* a_full = code_empty + 2 * kCodeSlots;  // [2 sets][2]
   uint64_t* a_empty = a_full + 4;              // [2 sets][2]
   uint64_t* p_full = a_empty + 4;              // [2]
   uint64_t* p_empty = p_full + 2;              // [2]
   uint64_t* d_full = p_empty + 2;              // [2]
   uint64_t* d_empty = d_full + 2;              // [2]
   uint64_t* stats_ready = d_empty + 2;         // [3]
-  uint64_t* accum_full = stats_ready + 3;
-  uint64_t* accum_empty = accum_full + 1;
-  uint64_t* mma_done = accum_empty + 1;        // MMA issuer: its MMAs completed (early exit)
+  uint64_t* accum_full = stats_ready + 3;      // [2] TMEM accumulator halves (items alternate)
+  uint64_t* accum_empty = accum_full + 2;      // [2]
+  uint64_t* mma_done = accum_empty + 2;        // MMA issuer: its MMAs completed (early exit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -90,7 +130,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   const ItemRange items(p.cta_begin, p.item_order, p.n_items);
 
   if (tid == 0) {
-    for (int i = 0; i < kCodeSlots; ++i) {
+    for (int i = 0; i < 2 * kCodeSlots; ++i) {
       mbar_init(&code_full[i], 1);
       mbar_init(&code_empty[i], 256);  // the 256 threads of the set that decodes the block
     }
@@ -99,14 +139,16 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 512);
+      mbar_init(&p_full[i], PIMG ? 1 : 512);  // the producer's bulk copy, or the 512 workers
       mbar_init(&p_empty[i], 1);
       mbar_init(&d_full[i], 1);
-      mbar_init(&d_empty[i], 513);
+      mbar_init(&d_empty[i], 515);  // the 512 workers, the MMA issuer and the two code producers
     }
     for (int i = 0; i < 3; ++i) mbar_init(&stats_ready[i], 512);
-    mbar_init(accum_full, 1);
-    mbar_init(accum_empty, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accum_full[i], 1);
+      mbar_init(&accum_empty[i], 128);
+    }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -116,10 +158,11 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer: descriptors, code blocks
+  if (warp == 19) {
+    // ------------------------------------------------------------ producer: P images and descriptors
     if (lane == 0) {
-      uint32_t c_iter = 0, d_iter = 0;
+      uint32_t d_iter = 0, p_iter = 0;
+      const int p_tile = p.n_rows_pad * 256;
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
@@ -138,6 +181,21 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             *abort_flag = 1;
             break;
           }
+          if (PIMG) {
+            if (t < 0 || t >= p.n_tiles) {
+              record_error(p.status, kErrBadDescriptor);
+              *abort_flag = 1;
+              break;
+            }
+            const int pb = p_iter & 1;
+            if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&p_full[pb], p_tile);
+            bulk_load(p_tiles + pb * p_tile, p.p_img + static_cast<int64_t>(t) * p_tile, p_tile, &p_full[pb]);
+            ++p_iter;
+          }
           if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
             *abort_flag = 1;
             break;
@@ -148,39 +206,82 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           } else {
             mbar_arrive(&d_full[db]);
           }
+          ++d_iter;
+        }
+      }
+      // Drain: every copy this producer issued has landed before the CTA can leave.
+      for (int s = 0; s < 2 && s < static_cast<int>(d_iter); ++s) {
+        const uint32_t last = d_iter - 1 - ((d_iter - 1 - s) % 2);
+        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+      }
+      for (int s = 0; PIMG && s < 2 && s < static_cast<int>(p_iter); ++s) {
+        const uint32_t last = p_iter - 1 - ((p_iter - 1 - s) % 2);
+        mbar_wait(&p_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+      }
+    }
+  } else if (warp == 0 || warp == 18) {
+    // ------------------------------------------------------------ producers: code blocks of one worker set
+    // Warp 0 streams the blocks of the pairs set 0 decodes (even ordinals of a tile) into ring 0, warp 18
+    // those of set 1 into ring 1, so neither set waits on a slot the other still holds.
+    if (lane == 0) {
+      const int ring = warp == 18 ? 1 : 0;
+      uint8_t* slots = c_slots + ring * kCodeSlots * kCodeSlot;
+      uint64_t* r_full = code_full + ring * kCodeSlots;
+      uint64_t* r_empty = code_empty + ring * kCodeSlots;
+      uint32_t c_iter = 0, d_iter = 0;
+      for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
+        const int it = items.at(k);
+        if (it < 0) {
+          record_error(p.status, kErrBadDescriptor);
+          *abort_flag = 1;
+          break;
+        }
+        const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
+        for (int t = tb; t < te && !*abort_flag; ++t) {
+          const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
+                        p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
+          const int db = d_iter & 1;
           if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
             *abort_flag = 1;
             break;
           }
           const GroupDesc* d = descs + db * kMaxRangeGroups;
-          for (int i = 0; i < n; ++i) {
-            const uint32_t off = d[i].code_offset, bytes = d[i].code_bytes;
-            if (bytes > static_cast<uint32_t>(kCodeSlot) || static_cast<uint64_t>(off) + bytes > p.code_size) {
-              record_error(p.status, kErrBadDescriptor);
-              *abort_flag = 1;
-              break;
+          int i = 0, lo, hi, pair, ord = 0;
+          bool ok = n >= 0 && n <= kMaxRangeGroups;
+          while (ok && (pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
+            if ((ord++ & 1) != ring) continue;
+            for (int half = 0; half < 2 && ok; ++half) {
+              const int gi = half ? hi : lo;
+              if (gi < 0) continue;
+              const uint32_t off = d[gi].code_offset, bytes = d[gi].code_bytes;
+              if (bytes > static_cast<uint32_t>(kCodeSlot) || static_cast<uint64_t>(off) + bytes > p.code_size) {
+                record_error(p.status, kErrBadDescriptor);
+                ok = false;
+                break;
+              }
+              const int cs = c_iter % kCodeSlots;
+              if (c_iter >= kCodeSlots &&
+                  !mbar_wait(&r_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&r_full[cs], bytes);
+              bulk_load(slots + cs * kCodeSlot, p.code + off, bytes, &r_full[cs]);
+              ++c_iter;
             }
-            const int cs = c_iter % kCodeSlots;
-            if (c_iter >= kCodeSlots &&
-                !mbar_wait(&code_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
-              *abort_flag = 1;
-              break;
-            }
-            mbar_arrive_expect_tx(&code_full[cs], bytes);
-            bulk_load(c_slots + cs * kCodeSlot, p.code + off, bytes, &code_full[cs]);
-            ++c_iter;
           }
+          mbar_arrive(&d_empty[db]);  // done reading this tile's descriptors
           ++d_iter;
+          if (!ok) {
+            *abort_flag = 1;
+            break;
+          }
         }
       }
-      // Drain: every copy this CTA issued has landed before the CTA can leave.
+      // Drain: every copy this producer issued has landed before the CTA can leave.
       for (int s = 0; s < kCodeSlots && s < static_cast<int>(c_iter); ++s) {
         const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kCodeSlots);
-        mbar_wait(&code_full[s], (last / kCodeSlots) & 1, p.status, kErrWaitDrain);
-      }
-      for (int s = 0; s < 2 && s < static_cast<int>(d_iter); ++s) {
-        const uint32_t last = d_iter - 1 - ((d_iter - 1 - s) % 2);
-        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&r_full[s], (last / kCodeSlots) & 1, p.status, kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -197,7 +298,11 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           break;
         }
         const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
-        if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
+        // Two accumulators of kAccumCols columns: item i uses half i % 2, so the epilogue of an item
+        // drains one half while the next item accumulates into the other.
+        const uint32_t acc_base = tmem + (item_iter & 1) * kAccumCols;
+        if (item_iter >= 2 &&
+            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kErrWaitAccumFree)) {
           *abort_flag = 1;
           break;
         }
@@ -230,7 +335,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               const uint64_t adesc = smem_desc_sw128(a_base + kk * 2048, 16384, 1024);
               const uint64_t bdesc = smem_desc_sw128(p_base + (kk >> 2) * (NR * 128) + (kk & 3) * 32, 16, 1024);
               const uint32_t acc = ((started >> pair) & 1u) || kk > 0 ? 1u : 0u;
-              mma_f16(tmem + pair * NR, adesc, bdesc, idesc, acc);
+              mma_f16(acc_base + pair * NR, adesc, bdesc, idesc, acc);
             }
             issued = true;
             started |= 1u << pair;
@@ -248,7 +353,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           *abort_flag = 1;
           break;
         }
-        mma_commit(accum_full);
+        mma_commit(&accum_full[item_iter & 1]);
         ++item_iter;
       }
       if (issued && *abort_flag) {
@@ -279,6 +384,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       // can be at most two items ahead of the slowest one (each P tile waits for the MMA of the tile
       // two before it, which waits for every worker), so three buffers never collide.
       float* st_s = stats_s + (item_iter % 3) * 256;
+      if (!PIMG) {
       if (w < NR) {
         float mx = 0.f, inv = 0.f;
         if (w < p.n_rows) {
@@ -294,16 +400,17 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         *abort_flag = 1;
         break;
       }
+      }
       for (int t = tb; t < te && !*abort_flag; ++t) {
         const TileDesc tile = p.tiles[t];
         // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype); set s builds
         //      rows [s*NR/2, (s+1)*NR/2), thread half h a quarter of them.
         const int pb = p_iter & 1;
-        if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+        if (!PIMG && p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
           *abort_flag = 1;
           break;
         }
-        {
+        if (!PIMG) {
           uint8_t* pt = p_tiles + pb * p_tile;
           const bool tok_ok = r < tile.n_tokens;
           const int sidx = tok_ok ? p.tok_sidx[tile.token_base + r] : 0;
@@ -340,9 +447,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         const GroupDesc* d = descs + db * kMaxRangeGroups;
         int i = 0, lo, hi, pair, ord = 0;
         while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
-          const int blocks = (lo >= 0) + (hi >= 0);
-          if ((ord & 1) != set) {  // the other set's pair: skip its code slots
-            c_iter += blocks;
+          if ((ord & 1) != set) {  // the other set's pair (its blocks are in the other ring)
             ++ord;
             continue;
           }
@@ -358,7 +463,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             uint8_t* dst = a + half * 16384;
             uint32_t out[16];
             if (gi >= 0) {
-              const int cs = c_iter % kCodeSlots;
+              const int cs = set * kCodeSlots + c_iter % kCodeSlots;  // this set's ring
               if (!mbar_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kErrWaitCodes)) {
                 *abort_flag = 1;
                 break;
@@ -388,14 +493,14 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       }
       if (*abort_flag) break;
       // ---- epilogue (warps 4..7, one per TMEM lane quarter): TMEM -> partial sums
-      if (warp >= 4 && warp < 8) {
-        if (!mbar_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum)) {
+      if (warp == 4 || warp == 5 || warp == 14 || warp == 15) {
+        if (!mbar_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kErrWaitAccum)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const int c = (warp - 4) * 32 + lane;  // component within the pair == TMEM lane
-        const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
+        const int c = (warp & 3) * 32 + lane;  // component within the pair == TMEM lane (quarter warp % 4)
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         float* dst = p.partial + static_cast<int64_t>(it) * NR * item_cols;
         // Pairs started by either set: the MMA started every pair that has a block in the item.
         uint32_t live_mask = 0;
@@ -409,7 +514,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           for (int n0 = 0; n0 < NR; n0 += 16) {
             uint32_t v[16];
             if (live) {
-              tmem_ld16(tmem + lane_base + pair2 * NR + n0, v);
+              tmem_ld16(tmem + (item_iter & 1) * kAccumCols + lane_base + pair2 * NR + n0, v);
               tmem_ld_wait();
             } else {
 #pragma unroll
@@ -421,7 +526,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           }
         }
         tc_fence_before();
-        mbar_arrive(accum_empty);
+        mbar_arrive(&accum_empty[item_iter & 1]);
       }
       ++item_iter;
     }
@@ -431,27 +536,36 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+template <bool RAW, bool PIMG>
+static int launch_vw(const ValueWeightParams& p, int grid, int smem, int a_slots, cudaStream_t stream) {
+  if (cudaFuncSetAttribute(value_weights_kernel<RAW, PIMG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return kDkvErrCuda;
+  value_weights_kernel<RAW, PIMG><<<grid, kVThreads, smem, stream>>>(p, a_slots);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream) {
   if (p.n_rows_pad % 16 != 0 || p.n_rows_pad < 16 || p.n_rows_pad > 128 || p.n_rows > p.n_rows_pad)
     return kDkvErrConfig;
-  if ((p.item_groups / 2) * p.n_rows_pad > 512 || p.item_groups % 2 != 0 || p.item_groups > kMaxRangeGroups)
+  if ((p.item_groups / 2) * p.n_rows_pad > kAccumCols || p.item_groups % 2 != 0 || p.item_groups > kMaxRangeGroups)
     return kDkvErrConfig;
   if (p.n_items == 0) return kDkvOk;
   const bool raw = p.max_planes > 8;
-  const int slots = raw ? ValueSmem<true>::kCodeSlots * ValueSmem<true>::kCodeSlot
-                        : ValueSmem<false>::kCodeSlots * ValueSmem<false>::kCodeSlot;
+  const int slots = 2 * (raw ? ValueSmem<true>::kCodeSlots * ValueSmem<true>::kCodeSlot
+                             : ValueSmem<false>::kCodeSlots * ValueSmem<false>::kCodeSlot);
   const int a_slots = p.n_rows_pad > 64 ? 1 : 2;  // two A tiles per set where the P tiles leave room
   const int smem = 1024 + 2 * a_slots * kPairTile + 2 * p.n_rows_pad * 256 + 2 * kMaxRangeGroups * 32 + 3 * 256 * 4 +
                    slots + 48 * 8;
   if (smem > 232448) return kDkvErrConfig;
-  cudaError_t e = raw ? cudaFuncSetAttribute(value_weights_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                      : cudaFuncSetAttribute(value_weights_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return kDkvErrCuda;
-  if (raw)
-    value_weights_kernel<true><<<grid, kVThreads, smem, stream>>>(p, a_slots);
-  else
-    value_weights_kernel<false><<<grid, kVThreads, smem, stream>>>(p, a_slots);
-  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+  if (p.p_img != nullptr) {
+    // P^T images of every value tile for this call's rows, then the weighting that fetches them.
+    if (p.n_tiles <= 0 || (reinterpret_cast<uintptr_t>(p.p_img) & 15u)) return kDkvErrArgs;
+    vprobs_kernel<<<p.n_tiles, 256, p.n_rows_pad * 256, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
+    return raw ? launch_vw<true, true>(p, grid, smem, a_slots, stream) : launch_vw<false, true>(p, grid, smem, a_slots, stream);
+  }
+  return raw ? launch_vw<true, false>(p, grid, smem, a_slots, stream) : launch_vw<false, false>(p, grid, smem, a_slots, stream);
 }
 
 }  // namespace dkv

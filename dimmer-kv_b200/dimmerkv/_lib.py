@@ -50,6 +50,7 @@ class AttendArgs(ctypes.Structure):
         ("vpart", c_void_p),
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
         ("k_pairs", c_void_p), ("k_pair_groups", c_void_p), ("softmax_mode", c_int32),
+        ("p_img", c_void_p), ("n_v_tiles", c_int32),
     ]
 
 

@@ -260,21 +260,36 @@ class CompressedBatch:
         least loaded one, so that the persistent CTAs finish together."""
         if rows_pad in self._v_items_cache:
             return self._v_items_cache[rows_pad]
-        item_groups = min(64, 2 * (512 // rows_pad))
+        item_groups = min(64, 2 * (256 // rows_pad))  # one of the kernel's two 256-column accumulators
         present = self.values.present
         gu = int(present.shape[1]) if present is not None and present.dim() == 2 else 0
         prefix = torch.zeros(present.shape[0], gu + 1, dtype=torch.int64)
         if gu:
             prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
         group_base = self.values.tiles[:, 4].to(torch.int64).cpu()
+        # Estimated cost of a (tile, group) block: a fixed part (its MMAs) plus its decode, which grows
+        # with the block's plane count; prefix sums of it per tile give each range's cost.
+        tiles_c = self.values.tiles.cpu().to(torch.int64)
+        desc = self.values.groups.cpu().view(torch.int32).view(-1, 8).to(torch.int64)
+        weight = torch.zeros(present.shape[0], gu, dtype=torch.float64)
+        n_blk = tiles_c[:, 3]
+        if gu and int(n_blk.sum()):
+            t_of = torch.repeat_interleave(torch.arange(tiles_c.shape[0]), n_blk)
+            first = torch.cumsum(n_blk, 0) - n_blk
+            blk = tiles_c[t_of, 4] + torch.arange(int(n_blk.sum())) - first[t_of]
+            weight[t_of, desc[blk, 0]] = 1.0 + 0.2 * ((desc[blk, 3] >> 8) & 0xFF).to(torch.float64).clamp_max(16)
+        wprefix = torch.zeros(present.shape[0], gu + 1, dtype=torch.float64)
+        if gu:
+            wprefix[:, 1:] = weight.cumsum(dim=1)
         tile_ranges = [[(t0, t1)] for t0, t1 in self.values.seq_tiles]
         for s, t0, t1 in self.extra_value_tiles:
             tile_ranges[s].append((t0, t1))
         ranges_g = [(g0, min(g0 + item_groups, gu)) for g0 in range(0, gu, item_groups)]
-        # Estimated cost of (tile, group range): decoded groups + ~0.75 group of probability build.
-        counts = [(prefix[:, g1] - prefix[:, g0]).tolist() for g0, g1 in ranges_g]
-        total = sum(sum(c) for c in counts) + 0.75 * present.shape[0] * max(1, len(ranges_g))
-        target = max(4.0, total / (4 * self.sm_count))
+        # Estimated cost of (tile, group range): its blocks + ~0.5 block of per-tile work; items are cut to
+        # about an eighth of a CTA's share so that the longest-first deal ends level.
+        counts = [(wprefix[:, g1] - wprefix[:, g0]).tolist() for g0, g1 in ranges_g]
+        total = sum(sum(c) for c in counts) + 0.5 * present.shape[0] * max(1, len(ranges_g))
+        target = max(4.0, total / (8 * self.sm_count))
         rows, ranges, spans, costs = [], [], [], []
         for s, seq_ranges in enumerate(tile_ranges):
             first = len(rows)
@@ -283,7 +298,7 @@ class CompressedBatch:
                     cnt = counts[ri]
                     c0, acc, used = t0, 0.0, False
                     for t in range(t0, t1):
-                        acc += cnt[t] + 0.75
+                        acc += cnt[t] + 0.5
                         used |= cnt[t] > 0
                         if t + 1 == t1 or t + 1 - c0 == self.tile_chunk or acc >= target:
                             if used:
@@ -306,7 +321,7 @@ class CompressedBatch:
         return out
 
     def _workspace(self, q_len: int, n_exact: int, rows_pad: int, n_v_items: int, item_groups: int):
-        key = (q_len, n_exact, rows_pad)
+        key = (q_len, n_exact, rows_pad, self.values.n_tiles)
         w = self._work.get(key)
         if w is None:
             counts = (self.seq_m.to(torch.int64) * self.q_heads * q_len).cpu()
@@ -322,6 +337,9 @@ class CompressedBatch:
                 "vpart": torch.empty(max(1, int(self.lib.dkv_vpart_floats(self.v_width, self.n_seq, rows_pad,
                                                                           self.head_dim))),
                                      dtype=torch.float32, device=self.device),
+                # bf16 probability tiles of every value tile, built once per layer and row chunk
+                "p_img": torch.empty(max(1, self.values.n_tiles * rows_pad * 256), dtype=torch.uint8,
+                                     device=self.device),
             }
             self._work = {key: w}
         return w
@@ -360,6 +378,7 @@ class CompressedBatch:
         a.k_max_planes, a.v_max_planes = ks.max_planes, vs.max_planes
         a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
         a.vpart = w["vpart"].data_ptr()
+        a.p_img, a.n_v_tiles = w["p_img"].data_ptr(), vs.n_tiles
         a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
         a.k_pairs = self.k_pairs.data_ptr() if self.k_pairs is not None else None
         a.k_pair_groups = self.k_pair_groups.data_ptr() if self.k_pairs is not None else None

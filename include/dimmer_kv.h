@@ -123,6 +123,11 @@ typedef struct dkv_attend_args {
    * row_stats[0..1] = the merged (max, 1 / sum) and fills the compressed mass and p_exact.
    * dkv_attend_layer requires 0. */
   int32_t softmax_mode;
+  /* Optional scratch for the value stage: [n_v_tiles][rows_pad * 256] bytes, 16-byte aligned. Given,
+   * each value tile's bf16 probabilities are built once per call (and row chunk) and fetched by the
+   * weighting kernel for every group range of the tile; NULL builds them inside the weighting kernel. */
+  uint8_t* p_img;
+  int32_t n_v_tiles;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
@@ -157,7 +162,7 @@ int dkv_finalize(const dkv_attend_args* args, void* stream);
 /* dkv_attend_layer for callers that cannot allocate device memory. No counterpart in the reference.
  * Callers inside another framework's memory manager (which owns every device allocation and forbids
  * cudaMalloc / cudaFree) or in latency-critical loops pass the same arguments as to
- * dkv_attend_layer except the five scratch pointers (scores, row_stats, p_exact, partial, vpart), which are
+ * dkv_attend_layer except the scratch pointers (scores, row_stats, p_exact, partial, vpart, p_img), which are
  * ignored; the scratch comes from a fixed 32 MiB array declared by the library in device memory.
  * n_scores = sum over conversations of n_q_heads * q_len * seq_m[s]. Returns DKV_ERR_SCRATCH, having
  * launched nothing, when the scratch would not fit. The first call on a device looks up the array's
