@@ -8,16 +8,21 @@
 //
 // Arithmetic, as the reference's float32 torch ops:
 //   low  = f16(min), span = f16(max(max - low, 1e-8))
-//   code = clamp(floor((x - low) / span * 256), 0, 255)    (IEEE divide; NaN -> 0 like the cast)
-//   v_m  = low + (code >> (8 - m) + 0.5) * span / 2^m       (m >= 1; the product is exact, so one
-//          fused multiply-add rounds once, like the reference's multiply, divide, add)
-//   err_m = sum over the group of (x - v_m)^2, v_0 = 0
-// The codes, low and span are bit-exact; the error sums are float32 in a fixed order of their own.
+//   code = clamp(floor((x - low) / span * 256), 0, 255)    (IEEE quotient; NaN -> 0 like the cast)
+//   err_m = sum over the group of (x - v_m)^2,  v_m = low + (code >> (8 - m) + 0.5) * span / 2^m,  v_0 = 0
+// The codes, low and span are bit-exact. The quotient is first taken as (x - low) * (256 / span);
+// that product is within 3 * 2^-24 relative of 256 * fl((x - low) / span), i.e. within 7e-5 for
+// every value up to 384 (the largest a group reaches: span is its f16-rounded range, at worst half a
+// subnormal step short), so when its fraction is farther than 1e-4 from an integer both floor alike,
+// and only the rest (values on a bin edge, NaN, infinities) takes the correctly rounded division.
+// The error sums are float32 in a fixed order of their own (d = (x - low) - (idx + 0.5) * span / 2^m,
+// fused into the square-add).
 //
 // Layout: one CTA of 8 warps per 4 tokens, two warps per token; a warp takes two adjacent groups at a
 // time (one per half-warp, four coefficients per lane, one 512-byte load per warp), with the next pair
-// loaded before the current one is processed. Each lane r < n_rungs of a warp keeps rung r's sum; the
-// two warps of a token add theirs at the end.
+// loaded before the current one is processed. Each lane keeps its own running sum for every rung (the
+// rung's plane count of the lane's group picks one of the lane's nine errors), and the lanes' sums are
+// added once per token at the end.
 #include <cuda_fp16.h>
 
 #include "dkv_kernels.h"
@@ -29,13 +34,24 @@ namespace {
 constexpr int kEncodeWarps = 8;
 constexpr int kEncodeTokensPerCta = 4;
 constexpr int kEncodeMaxRungs = 32;
-constexpr int kEncodeMaxGroups = 1024;  // rung table staged in shared memory: n_rungs x groups bytes
+constexpr int kEncodeMaxGroups = 1024;  // rung table staged in shared memory: groups x n_rungs bytes
+
+// floor((x - low) / span * 256) clamped to [0, 255], bit-exact with the IEEE quotient.
+__device__ __forceinline__ uint32_t code_of(float y, float scale256, float span) {
+  const float q = __fmul_rn(y, scale256);
+  float k = floorf(q);
+  const float frac = q - k;
+  if (!(frac > 1e-4f && frac < 0.9999f)) k = floorf(__fmul_rn(__fdiv_rn(y, span), 256.f));
+  k = fminf(fmaxf(k, 0.f), 255.f);  // NaN (0 / 0 of a constant group) -> 0, like the uint8 cast
+  return static_cast<uint32_t>(k);
+}
 }  // namespace
 
+template <int R>
 __global__ void __launch_bounds__(kEncodeWarps * 32) encode_kernel(const EncodeParams p) {
-  extern __shared__ uint8_t rung_planes_s[];  // [n_rungs][groups]
-  __shared__ float scratch[kEncodeWarps][2][9];
-  __shared__ float red[kEncodeTokensPerCta][kEncodeMaxRungs + 1];
+  extern __shared__ uint8_t rung_planes_s[];  // [groups][n_rungs] (transposed: a group's rungs are adjacent)
+  __shared__ float err_s[kEncodeWarps][32][9];  // a lane's nine errors (odd row stride: no bank conflicts)
+  __shared__ float red[kEncodeTokensPerCta][R + 1];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -43,13 +59,15 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) encode_kernel(const EncodeP
   const int half = lane >> 4;
   const int l16 = lane & 15;
   const int groups = p.features / 64;
-  for (int i = tid; i < p.n_rungs * groups; i += blockDim.x) {
+  const int nr = p.n_rungs;
+  for (int i = tid; i < nr * groups; i += blockDim.x) {
+    const int r = i / groups, g = i % groups;  // read coalesced, store transposed
     uint8_t m = p.rung_planes[i];
     if (m > 8) {  // a plane count the codes cannot hold: report it, never index past the nine errors
       record_error(p.status, kErrBadDescriptor);
       m = 8;
     }
-    rung_planes_s[i] = m;
+    rung_planes_s[g * nr + r] = m;
   }
   __syncthreads();
 
@@ -57,8 +75,11 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) encode_kernel(const EncodeP
   const int wt = warp & 1;                            // warp of the token
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kEncodeTokensPerCta + tl;
   const bool active = t < p.tokens;
-  float acc_rung = 0.f;    // lane r: rung r's sum over this warp's groups
-  float acc_energy = 0.f;  // lane 0
+  float acc[R];     // this lane's sum for every rung
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+  float energy = 0.f;
+  float* my_err = err_s[warp][lane];
   if (active) {
     const float* row = p.coeff + t * p.coeff_stride;
     // Warp wt takes the group pairs (2 (wt + 2k), 2 (wt + 2k) + 1), k = 0, 1, ...
@@ -83,34 +104,30 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) encode_kernel(const EncodeP
       const float low = __half2float(low_h);
       const __half span_h = __float2half_rn(fmaxf(__fsub_rn(mx, low), 1e-8f));
       const float span = __half2float(span_h);
+      const float scale256 = __fdiv_rn(256.f, span);
+      float y[4];
       uint32_t code[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        float q = floorf(__fmul_rn(__fdiv_rn(__fsub_rn(xv[k], low), span), 256.f));
-        q = fminf(fmaxf(q, 0.f), 255.f);  // NaN (0 / 0 of a constant group) -> 0, like the uint8 cast
-        code[k] = static_cast<uint32_t>(q);
+        y[k] = __fsub_rn(xv[k], low);
+        code[k] = code_of(y[k], scale256, span);
       }
-      // Squared error at 0..8 planes.
+      // This lane's squared error at 0..8 planes (its four values).
       float e[9];
       e[0] = 0.f;
 #pragma unroll
       for (int k = 0; k < 4; ++k) e[0] = fmaf(xv[k], xv[k], e[0]);
 #pragma unroll
       for (int m = 1; m <= 8; ++m) {
-        const float scale = __fmul_rn(span, __int_as_float((127 - m) << 23));  // span / 2^m, exact
-        float s = 0.f;
+        const float s = __fmul_rn(span, __int_as_float((127 - m) << 23));  // span / 2^m, exact
+        float a = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float idx = __fsub_rn(__uint_as_float(0x4B000000u | (code[k] >> (8 - m))), 8388607.5f);  // + 0.5
-          const float d = __fsub_rn(xv[k], __fmaf_rn(idx, scale, low));
-          s = fmaf(d, d, s);
+          const float d = fmaf(-idx, s, y[k]);
+          a = fmaf(d, d, a);
         }
-        e[m] = s;
-      }
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) {
-#pragma unroll
-        for (int m = 0; m <= 8; ++m) e[m] += __shfl_xor_sync(0xffffffffu, e[m], o);
+        e[m] = a;
       }
       if (valid) {
         const int64_t col = static_cast<int64_t>(g) * 64 + 4 * l16;
@@ -120,32 +137,38 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) encode_kernel(const EncodeP
           p.low[t * groups + g] = __half_as_ushort(low_h);
           p.span[t * groups + g] = __half_as_ushort(span_h);
         }
-      }
+        energy += e[0];
+        // Each rung's plane count for this group picks one of the nine errors.
 #pragma unroll
-      for (int m = 0; m <= 8; ++m)
-        if (l16 == m) scratch[warp][half][m] = valid ? e[m] : 0.f;
-      __syncwarp();
-      if (lane < p.n_rungs) {
-        const int g0 = pair;  // the half-warps hold groups pair and pair + 1
-        float a = scratch[warp][0][rung_planes_s[lane * groups + g0]];
-        if (g0 + 1 < groups) a += scratch[warp][1][rung_planes_s[lane * groups + g0 + 1]];
-        acc_rung += a;
+        for (int m = 0; m <= 8; ++m) my_err[m] = e[m];
+        const uint8_t* planes = rung_planes_s + g * nr;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          if (r < nr) acc[r] += my_err[planes[r]];
       }
-      if (lane == 0) acc_energy += scratch[warp][0][0] + scratch[warp][1][0];
-      __syncwarp();
       x = xn;
       g = gnext;
     }
   }
-  // The token's two warps: warp 1 hands its sums to warp 0, which writes them.
-  if (wt == 1) {
-    if (lane < p.n_rungs) red[tl][lane] = acc_rung;
-    if (lane == 0) red[tl][kEncodeMaxRungs] = acc_energy;
+  // Sum the lanes, then the token's two warps: warp 1 hands its sums to warp 0, which writes them.
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) energy += __shfl_xor_sync(0xffffffffu, energy, o);
+  if (wt == 1 && lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[tl][r] = acc[r];
+    red[tl][R] = energy;
   }
   __syncthreads();
-  if (wt == 0 && active) {
-    if (lane < p.n_rungs) p.rung_error[t * p.n_rungs + lane] = acc_rung + red[tl][lane];
-    if (lane == 0 && p.energy != nullptr) p.energy[t] = acc_energy + red[tl][kEncodeMaxRungs];
+  if (wt == 0 && active && lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < nr) p.rung_error[t * nr + r] = acc[r] + red[tl][r];
+    if (p.energy != nullptr) p.energy[t] = energy + red[tl][R];
   }
 }
 
@@ -161,7 +184,10 @@ int run_encode(const EncodeParams& p, cudaStream_t stream) {
   if (p.tokens == 0) return kDkvOk;
   const int smem = p.n_rungs * groups;  // <= 32 KB
   const int grid = (p.tokens + kEncodeTokensPerCta - 1) / kEncodeTokensPerCta;
-  encode_kernel<<<grid, kEncodeWarps * 32, smem, stream>>>(p);
+  if (p.n_rungs <= 16)
+    encode_kernel<16><<<grid, kEncodeWarps * 32, smem, stream>>>(p);
+  else
+    encode_kernel<32><<<grid, kEncodeWarps * 32, smem, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
