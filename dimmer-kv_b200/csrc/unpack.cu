@@ -28,9 +28,10 @@ constexpr int kUnpackThreads = kUnpackDecodeThreads + 32;
 template <bool BF16, bool RAW>
 struct UnpackSmem {
   static constexpr int kSlotBytes = RAW ? 16896 : 8704;
+  static constexpr int kSlotStride = kSlotBytes + 32;          // the block, then its descriptor
   static constexpr int kHalfBytes = BF16 ? 64 : 128;           // 32 components of one row
   static constexpr int kStageWarp = 32 * kHalfBytes;           // one warp's 32 rows
-  static constexpr int kStage = kUnpackSlots * kSlotBytes;
+  static constexpr int kStage = kUnpackSlots * kSlotStride;
   static constexpr int kBars = kStage + 8 * kStageWarp;
   static constexpr int kBytes = kBars + 2 * kUnpackSlots * 8 + 16;
 };
@@ -122,8 +123,14 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
           *abort_flag = 1;
           break;
         }
+        // The block's descriptor goes into the slot's tail before the copy is issued; the decoders read
+        // it after the slot's barrier completes (arrive releases, the wait acquires).
+        uint4* stash = reinterpret_cast<uint4*>(smem + s * S::kSlotStride + kUnpackSlotBytes);
+        const uint4* src = reinterpret_cast<const uint4*>(&p.groups[tile.group_base + gi]);
+        stash[0] = __ldg(src);
+        stash[1] = __ldg(src + 1);
         mbar_arrive_expect_tx(&full[s], gr.code_bytes);
-        bulk_load(smem + s * kUnpackSlotBytes, p.code + gr.code_offset, gr.code_bytes, &full[s]);
+        bulk_load(smem + s * S::kSlotStride, p.code + gr.code_offset, gr.code_bytes, &full[s]);
         ++issued;
       }
       // Drain: the CTA must not exit with a copy into its shared memory in flight.
@@ -145,31 +152,29 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   const int64_t stride = p.out_cols * (BF16 ? 2 : 4);
   uint8_t* out_base = reinterpret_cast<uint8_t*>(p.out) + (static_cast<int64_t>(tile.token_base) + row0) * stride +
                       static_cast<int64_t>(h) * S::kHalfBytes;
-  int cursor = 0, consumed = 0;
-  int next_group = -1;
-  GroupRegs gr{};
-  if (tile.n_groups > 0) {
-    gr = load_group(&p.groups[tile.group_base]);
-    next_group = static_cast<int>(gr.group);
-  }
-  for (int g = 0; g < n_union; ++g) {
-    uint8_t* out_g = out_base + static_cast<int64_t>(g) * kGroup * (BF16 ? 2 : 4);
-    if (g != next_group) {
-      if (n_valid > 0) store_zero_rows<BF16>(out_g, stride, lane, n_valid);
-      continue;
-    }
-    const int s = consumed % kUnpackSlots;
+  // Blocks arrive in the tile's order (ascending union group); the groups before each block and after
+  // the last one are written as zeros.
+  int g_done = 0;  // groups [0, g_done) of the rows are written
+  for (int i = 0; i < tile.n_groups; ++i) {
+    const int s = i % kUnpackSlots;
     // The warp leaves together (its stores end in __syncwarp): one lane giving up ends the warp.
-    const bool landed = mbar_wait(&full[s], (consumed / kUnpackSlots) & 1, p.status, kErrWaitCodes);
+    const bool landed = mbar_wait(&full[s], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes);
     if (!__all_sync(0xffffffffu, landed)) {
       *abort_flag = 1;
       return;
     }
-    const uint8_t* blk = smem + s * kUnpackSlotBytes;
-    // The next block's descriptor, fetched now so that its latency hides behind this block's decode.
-    ++cursor;
-    GroupRegs gn{};
-    if (cursor < tile.n_groups) gn = load_group(&p.groups[tile.group_base + cursor]);
+    const uint8_t* blk = smem + s * S::kSlotStride;
+    const uint4* stash = reinterpret_cast<const uint4*>(blk + kUnpackSlotBytes);
+    const GroupRegs gr = group_from_words(stash[0], stash[1]);
+    const int g = static_cast<int>(gr.group);
+    if (g < g_done || g >= n_union) {  // descriptors out of union order, or a group past out_cols / 64
+      record_error(p.status, kErrBadDescriptor);
+      *abort_flag = 1;
+      return;
+    }
+    for (; g_done < g; ++g_done)
+      if (n_valid > 0) store_zero_rows<BF16>(out_base + static_cast<int64_t>(g_done) * kGroup * (BF16 ? 2 : 4), stride,
+                                             lane, n_valid);
     uint4 chunks[kC];
     if (BF16) {
       uint32_t out[16];
@@ -185,21 +190,14 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
                                __float_as_uint(out[4 * k + 2]), __float_as_uint(out[4 * k + 3]));
     }
     mbar_arrive(&empty[s]);
-    ++consumed;
-    if (n_valid > 0) store_rows<BF16>(stage, chunks, out_g, stride, lane, n_valid);
-    // Next block of the tile: its group must come after this one (descriptors in union order).
-    next_group = -1;
-    if (cursor < tile.n_groups) {
-      gr = gn;
-      next_group = static_cast<int>(gr.group);
-      if (next_group <= g) {
-        record_error(p.status, kErrBadDescriptor);
-        *abort_flag = 1;
-        return;
-      }
-    }
+    if (n_valid > 0)
+      store_rows<BF16>(stage, chunks, out_base + static_cast<int64_t>(g) * kGroup * (BF16 ? 2 : 4), stride, lane,
+                       n_valid);
+    g_done = g + 1;
   }
-  if (cursor != tile.n_groups) record_error(p.status, kErrBadDescriptor);  // a group at or past out_cols / 64
+  for (; g_done < n_union; ++g_done)
+    if (n_valid > 0)
+      store_zero_rows<BF16>(out_base + static_cast<int64_t>(g_done) * kGroup * (BF16 ? 2 : 4), stride, lane, n_valid);
 }
 
 template <bool BF16, bool RAW>

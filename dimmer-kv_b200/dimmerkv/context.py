@@ -71,6 +71,22 @@ class ColdTier:
     words: torch.Tensor    # int64 [M, Gu, 8], pinned
     headers: torch.Tensor  # int32 [M, Gu], pinned
     hot_planes: torch.Tensor | None = None  # uint8 [M, Gu]: planes already in the hot tier (for byte counts)
+    w_stage: torch.Tensor | None = None     # pinned staging rows for a refine (grown on demand)
+    h_stage: torch.Tensor | None = None
+
+    def stage(self, rows: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The cold planes and headers of ``rows`` (host int64 indices) gathered into pinned staging
+        buffers that are kept between refines (pinned allocation is slow; the copies out of them are
+        complete when refine returns)."""
+        n = int(rows.numel())
+        if self.w_stage is None or self.w_stage.shape[0] < n:
+            cap = max(n, 256, int(self.words.shape[0]) // 50)
+            self.w_stage = torch.empty(cap, *self.words.shape[1:], dtype=self.words.dtype).pin_memory()
+            self.h_stage = torch.empty(cap, *self.headers.shape[1:], dtype=self.headers.dtype).pin_memory()
+        w, h = self.w_stage[:n], self.h_stage[:n]
+        torch.index_select(self.words, 0, rows, out=w)
+        torch.index_select(self.headers, 0, rows, out=h)
+        return w, h
 
 
 def plane_words(codes: torch.Tensor) -> torch.Tensor:
@@ -535,10 +551,7 @@ class CompressedBatch:
                 hot_tile.append(t0 + local // 128)
                 hot_row.append(local % 128)
                 ct = cold[s][kind]
-                staging = torch.empty(mid.numel(), gu, 8, dtype=torch.int64).pin_memory()
-                torch.index_select(ct.words, 0, mid, out=staging)
-                hstage = torch.empty(mid.numel(), gu, dtype=torch.int32).pin_memory()
-                torch.index_select(ct.headers, 0, mid, out=hstage)
+                staging, hstage = ct.stage(mid)
                 words.append(staging)
                 headers.append(hstage)
                 if ct.hot_planes is not None:
@@ -555,8 +568,11 @@ class CompressedBatch:
                 continue
             # Cold planes to the device on a side stream (pinned -> device copies).
             with torch.cuda.stream(stream):
-                words_d = torch.cat(words).to(self.device, non_blocking=True)
-                headers_d = torch.cat(headers).to(self.device, non_blocking=True)
+                # One conversation: straight from its pinned staging rows; several: one pinned concatenation.
+                w_host = words[0] if len(words) == 1 else torch.cat(words).pin_memory()
+                h_host = headers[0] if len(headers) == 1 else torch.cat(headers).pin_memory()
+                words_d = w_host.to(self.device, non_blocking=True)
+                headers_d = h_host.to(self.device, non_blocking=True)
             main.wait_stream(stream)
             # Layout of the refined tiles: per conversation, tiles of up to 128 selected tokens, every union
             # group holding 8 planes.

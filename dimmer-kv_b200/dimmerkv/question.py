@@ -33,7 +33,9 @@ def cold_tier(codes: torch.Tensor, low: torch.Tensor, span: torch.Tensor, union:
     words = plane_words(codes[:, u].contiguous())
     headers = header_bits(low[:, u], span[:, u])
     hp = hot_planes.cpu()[:, union.cpu()] if hot_planes is not None else None
-    return ColdTier(words=words.cpu().pin_memory(), headers=headers.cpu().pin_memory(), hot_planes=hp)
+    tier = ColdTier(words=words.cpu().pin_memory(), headers=headers.cpu().pin_memory(), hot_planes=hp)
+    tier.stage(torch.zeros(0, dtype=torch.int64))  # allocate the pinned staging rows now, not at refine time
+    return tier
 
 
 def clone_cache(cache, model) -> DynamicCache:
