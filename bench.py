@@ -359,6 +359,83 @@ def encode_rate(device, tokens: int = 16348, features: int = 28672, launches: in
             "peak_source": "of measured (hbm_gbs)" if peaks else "of fallback"}
 
 
+def storage_rate(device, middle: int = 16348, features: int = 28672, launches: int = 5) -> dict:
+    """dkv_storage_unpack (restore of the kvtc byte format) on one stream of the largest cfg3 conversation's
+    shape: 16348 tokens x 448 groups of 64, a 10-rung ladder (rung r: 8 bits on the first 8r groups, 4 on
+    the next 8r, 2 on the next 16r), tokens on rungs 0-9 with seeded weights, seeded code bytes.
+    Algorithmic bytes = packed codes + f16 low / scale read + restored float32 values written; timed with
+    CUDA events after 3 warm-up launches."""
+    import numpy as np
+    import torch
+
+    from dimmerkv import _lib
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    groups = features // 64
+    rng = np.random.default_rng(5)
+    rungs = rng.choice(10, size=middle, p=np.array([8, 10, 12, 12, 12, 12, 10, 10, 8, 6]) / 100.0)
+    seg = []
+    rows_all, groups_all = [], []
+    offset = 12 + middle
+    read_bytes = written = 0
+    for r in range(10):
+        rows = np.nonzero(rungs == r)[0].astype(np.int32)
+        bits = np.zeros(groups, dtype=np.int64)
+        n8, n4, n2 = 8 * (r + 1), 8 * (r + 1), 16 * (r + 1)
+        bits[:n8] = 8
+        bits[n8:n8 + n4] = 4
+        bits[n8 + n4:n8 + n4 + n2] = 2
+        for width in (2, 4, 8):
+            chosen = np.nonzero(bits == width)[0].astype(np.int32)
+            if chosen.size == 0 or rows.size == 0:
+                continue
+            n_codes = rows.size * chosen.size * 64
+            codes_at = offset
+            offset += (n_codes * width + 7) // 8
+            low_at = offset
+            offset += rows.size * chosen.size * 2
+            scale_at = offset
+            offset += rows.size * chosen.size * 2
+            seg.append((codes_at, low_at, scale_at, rows.size, chosen.size, width,
+                        sum(x.size for x in rows_all), sum(x.size for x in groups_all), 0))
+            rows_all.append(rows)
+            groups_all.append(chosen)
+            read_bytes += (n_codes * width + 7) // 8 + rows.size * chosen.size * 4
+            written += n_codes * 4
+    data = torch.randint(0, 256, (offset,), dtype=torch.uint8, device=device,
+                         generator=torch.Generator(device=device).manual_seed(6))
+    seg_np = np.array(seg, dtype=_lib.STORAGE_SEGMENT)
+    seg_d = torch.from_numpy(seg_np.view(np.uint8).copy()).to(device)
+    rows_d = torch.from_numpy(np.concatenate(rows_all)).to(device)
+    groups_d = torch.from_numpy(np.concatenate(groups_all)).to(device)
+    out = torch.zeros(middle, features, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    max_quads = max(s[3] * s[4] * 16 for s in seg)
+    a = _lib.StorageArgs(data.data_ptr(), offset, seg_d.data_ptr(), len(seg), max_quads, rows_d.data_ptr(),
+                         groups_d.data_ptr(), out.data_ptr(), middle, features, status.data_ptr())
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        _lib.check(lib.dkv_storage_unpack(a, stream.cuda_stream), "dkv_storage_unpack")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(launches + 1)]
+    torch.cuda.synchronize(device)
+    ev[0].record(stream)
+    for i in range(launches):
+        _lib.check(lib.dkv_storage_unpack(a, stream.cuda_stream), "dkv_storage_unpack")
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize(device)
+    _lib.check_device_status(status)
+    ms = statistics.mean(ev[i].elapsed_time(ev[i + 1]) for i in range(launches))
+    nbytes = read_bytes + written
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del out, data
+    return {"kernel": "storage_unpack (kvtc byte format -> coefficients)", "tokens": middle, "features": features,
+            "segments": len(seg), "stored_bytes": int(offset), "ms": round(ms, 4), "bytes": int(nbytes),
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_gbs": peak,
+            "peak_source": "of measured (hbm_gbs)" if peaks else "of fallback"}
+
+
 def run_kernels(args, cfg, device) -> dict:
     """Profiling case: every layer's dkv_attend_layer over the packed codes, random queries, no model."""
     import torch
@@ -399,7 +476,7 @@ def run_kernels(args, cfg, device) -> dict:
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
             "gpu_launches": len(timer.events) * KERNELS_PER_LAYER, "unpack": unpack_rate(batch, device),
-            "encode": encode_rate(device)}
+            "encode": encode_rate(device), "storage": storage_rate(device)}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
@@ -653,6 +730,7 @@ def run_ours(args, cfg, rank, world, device):
     dimmer.STATE.compressed = None
     unpack = unpack_rate(batch, device) if rank == 0 else None
     encode = encode_rate(device) if rank == 0 else None
+    storage = storage_rate(device) if rank == 0 else None
 
     result = None
     if rank == 0:
@@ -674,6 +752,7 @@ def run_ours(args, cfg, rank, world, device):
             "gpu_launches": len(key_ms) * KERNELS_PER_LAYER,
             "unpack": unpack,
             "encode": encode,
+            "storage": storage,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }

@@ -391,4 +391,24 @@ int dkv_encode_groups(const dkv_encode_args* a, void* stream) {
   return dkv::run_encode(p, static_cast<cudaStream_t>(stream));
 }
 
+int dkv_storage_unpack(const dkv_storage_args* a, void* stream) {
+  if (a == nullptr || a->data == nullptr || a->segments == nullptr || a->rows == nullptr || a->groups == nullptr ||
+      a->out == nullptr || a->status == nullptr || a->out_rows < 0 || a->out_cols < 0)
+    return DKV_ERR_ARGS;
+  static_assert(sizeof(dkv_storage_segment) == sizeof(dkv::StorageSegment), "segment layout");
+  dkv::StorageParams p{};
+  p.data = a->data;
+  p.data_size = a->data_size;
+  p.segments = reinterpret_cast<const dkv::StorageSegment*>(a->segments);
+  p.n_segments = a->n_segments;
+  p.max_quads = a->max_quads;
+  p.rows = a->rows;
+  p.groups = a->groups;
+  p.out = a->out;
+  p.out_rows = a->out_rows;
+  p.out_cols = a->out_cols;
+  p.status = a->status;
+  return dkv::run_storage_unpack(p, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

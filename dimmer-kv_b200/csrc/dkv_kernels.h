@@ -136,6 +136,26 @@ struct EncodeParams {
 };
 int run_encode(const EncodeParams& p, cudaStream_t stream);
 
+// Restore of the kvtc byte format (storage.cu).
+struct StorageSegment {
+  uint64_t codes_offset, low_offset, scale_offset;  // byte offsets into the stored bytes
+  int32_t count, n_groups, width;                    // tokens, groups of this bit width, bits per code
+  int32_t rows_offset, groups_offset, pad;           // into rows[] / groups[]
+};
+struct StorageParams {
+  const uint8_t* data;
+  uint64_t data_size;
+  const StorageSegment* segments;
+  int n_segments;
+  int64_t max_quads;              // largest count * n_groups * 16 of any segment
+  const int32_t* rows;            // token row of each segment's tokens
+  const int32_t* groups;          // group index of each segment's groups
+  float* out;                     // [out_rows][out_cols], zero where no segment writes
+  int64_t out_rows, out_cols;
+  int* status;
+};
+int run_storage_unpack(const StorageParams& p, cudaStream_t stream);
+
 // Standalone ragged bit-plane unpack (unpack.cu).
 struct UnpackParams {
   const uint8_t* code;

@@ -1,0 +1,85 @@
+// storage.cu — restore of the kvtc byte format: bit-packed ladder codes -> dense coefficients.
+//
+// Replaces the per-rung, per-width loop of kvtc_storage.decode_bytes (scripts/kvtc_storage.py:103-114):
+// for every (rung, bit width) segment of a stream, the packed w-bit codes of count tokens x n_groups
+// groups x 64 components (8 / w codes per byte, the first in the low bits) and their f16 low and scale
+// become codes * scale + low (float32 multiply, then add, as the reference's torch ops) in the rows of
+// the segment's tokens and the columns of its groups. The host walks the format (the rung of every
+// token is in the clear, so every segment's offsets follow) and lists the segments; one launch
+// restores a whole stream.
+//
+// One thread per four consecutive components: their codes are one byte (w = 2), two (w = 4) or four
+// (w = 8), read byte by byte because the format packs its arrays without alignment; the four values
+// go out as one 16-byte store.
+#include <cuda_fp16.h>
+
+#include "dkv_kernels.h"
+#include "dkv_ptx.cuh"
+
+namespace dkv {
+
+namespace {
+constexpr int kStorageThreads = 256;
+
+__device__ __forceinline__ float f16_at(const uint8_t* data, uint64_t at) {
+  const unsigned short bits = static_cast<unsigned short>(data[at] | (data[at + 1] << 8));
+  return __half2float(__ushort_as_half(bits));
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kStorageThreads) storage_unpack_kernel(const StorageParams p) {
+  const StorageSegment sg = p.segments[blockIdx.y];
+  const int64_t quads = static_cast<int64_t>(sg.count) * sg.n_groups * 16;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kStorageThreads + threadIdx.x;
+  if (q >= quads) return;
+  const int w = sg.width;
+  if (w != 2 && w != 4 && w != 8) {
+    record_error(p.status, kErrBadDescriptor);
+    return;
+  }
+  const int64_t e = q * 4;                      // first code of the quad, in (token, group, component) order
+  const int64_t tg = e / 64;                    // (token, group) index
+  const int i = static_cast<int>(tg / sg.n_groups);
+  const int j = static_cast<int>(tg % sg.n_groups);
+  const int c = static_cast<int>(e % 64);
+  const uint64_t byte0 = sg.codes_offset + static_cast<uint64_t>(e) * w / 8;
+  const int nbytes = w / 2;                      // 4 codes x w bits
+  const uint64_t hdr = static_cast<uint64_t>(tg) * 2;
+  if (byte0 + nbytes > p.data_size || sg.low_offset + hdr + 2 > p.data_size ||
+      sg.scale_offset + hdr + 2 > p.data_size) {
+    record_error(p.status, kErrBadDescriptor);
+    return;
+  }
+  const int row = p.rows[sg.rows_offset + i];
+  const int group = p.groups[sg.groups_offset + j];
+  if (row < 0 || row >= p.out_rows || group < 0 || (static_cast<int64_t>(group) + 1) * 64 > p.out_cols) {
+    record_error(p.status, kErrBadDescriptor);
+    return;
+  }
+  uint32_t bits = 0;
+  for (int b = 0; b < nbytes; ++b) bits |= static_cast<uint32_t>(p.data[byte0 + b]) << (8 * b);
+  const uint32_t mask = (1u << w) - 1u;
+  const float low = f16_at(p.data, sg.low_offset + hdr);
+  const float scale = f16_at(p.data, sg.scale_offset + hdr);
+  float v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float code = static_cast<float>((bits >> (k * w)) & mask);
+    v[k] = __fadd_rn(__fmul_rn(code, scale), low);
+  }
+  float4* dst = reinterpret_cast<float4*>(p.out + static_cast<int64_t>(row) * p.out_cols + group * 64 + c);
+  *dst = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+int run_storage_unpack(const StorageParams& p, cudaStream_t stream) {
+  if (p.n_segments < 0 || p.out_cols % 64 != 0 || p.max_quads < 0) return kDkvErrArgs;
+  if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
+  if (p.n_segments == 0 || p.max_quads == 0) return kDkvOk;
+  if (p.n_segments > 65535) return kDkvErrConfig;
+  const int64_t blocks = (p.max_quads + kStorageThreads - 1) / kStorageThreads;
+  if (blocks > 0x7FFFFFFF) return kDkvErrConfig;
+  storage_unpack_kernel<<<dim3(static_cast<unsigned>(blocks), p.n_segments), kStorageThreads, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
+}  // namespace dkv

@@ -23,7 +23,7 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
            "dkv_attend_tail",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
-           "dkv_vpart_floats", "dkv_encode_groups", "dkv_version", "dkv_status_string")
+           "dkv_vpart_floats", "dkv_encode_groups", "dkv_storage_unpack", "dkv_version", "dkv_status_string")
 
 
 class AttendArgs(ctypes.Structure):
@@ -72,6 +72,22 @@ class EncodeArgs(ctypes.Structure):
         ("rung_planes", c_void_p), ("n_rungs", c_int32), ("codes", c_void_p), ("low", c_void_p), ("span", c_void_p),
         ("rung_error", c_void_p), ("energy", c_void_p), ("status", c_void_p),
     ]
+
+
+class StorageArgs(ctypes.Structure):
+    """Mirror of ``dkv_storage_args`` (the segments are a uint8 tensor of STORAGE_SEGMENT records)."""
+
+    _fields_ = [
+        ("data", c_void_p), ("data_size", c_uint64), ("segments", c_void_p), ("n_segments", c_int32),
+        ("max_quads", c_int64), ("rows", c_void_p), ("groups", c_void_p), ("out", c_void_p), ("out_rows", c_int64),
+        ("out_cols", c_int64), ("status", c_void_p),
+    ]
+
+
+# numpy record of one dkv_storage_segment.
+STORAGE_SEGMENT = [("codes_offset", "<u8"), ("low_offset", "<u8"), ("scale_offset", "<u8"), ("count", "<i4"),
+                   ("n_groups", "<i4"), ("width", "<i4"), ("rows_offset", "<i4"), ("groups_offset", "<i4"),
+                   ("pad", "<i4")]
 
 
 class ImportanceArgs(ctypes.Structure):
@@ -128,7 +144,7 @@ def lib():
         handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
         handle.dkv_unpack.restype = c_int32
         for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs),
-                         ("dkv_encode_groups", EncodeArgs)):
+                         ("dkv_encode_groups", EncodeArgs), ("dkv_storage_unpack", StorageArgs)):
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(st), c_void_p]
             fn.restype = c_int32

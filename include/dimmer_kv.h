@@ -263,6 +263,39 @@ typedef struct dkv_encode_args {
 } dkv_encode_args;
 int dkv_encode_groups(const dkv_encode_args* args, void* stream);
 
+/* Restore side of the kvtc byte format (scripts/kvtc_storage.py:42-135): the bit-packed ladder codes of
+ * every (rung, bit width) segment of a stream, decoded to float32 coefficients code * scale + low (a
+ * multiply, then an add, as the reference's float32 torch ops; kvtc_storage.py:103-114) in the rows of
+ * the segment's tokens and the 64 columns of each of its groups. Replaces that loop of decode_bytes; the
+ * host reads the format's layout (the rung of every token is stored in the clear) and fills one
+ * dkv_storage_segment per (rung, width). Rows and groups no segment covers are left as they are (the
+ * reference starts from zeros). `data` may hold its arrays at any byte offset; `out` 16-byte aligned. */
+typedef struct dkv_storage_segment {
+  uint64_t codes_offset;         /* packed codes: 8 / width per byte, the first in the low bits */
+  uint64_t low_offset;           /* f16 [count][n_groups] */
+  uint64_t scale_offset;         /* f16 [count][n_groups] */
+  int32_t count;                 /* tokens of the rung */
+  int32_t n_groups;              /* groups stored at this width */
+  int32_t width;                 /* 2, 4 or 8 */
+  int32_t rows_offset;           /* first of the segment's count token rows in `rows` */
+  int32_t groups_offset;         /* first of its n_groups group indices in `groups` */
+  int32_t pad;
+} dkv_storage_segment;
+
+typedef struct dkv_storage_args {
+  const uint8_t* data;           /* the stored bytes (device) */
+  uint64_t data_size;
+  const dkv_storage_segment* segments;
+  int32_t n_segments;
+  int64_t max_quads;             /* largest count * n_groups * 16 over the segments */
+  const int32_t* rows;
+  const int32_t* groups;
+  float* out;                    /* [out_rows][out_cols] */
+  int64_t out_rows, out_cols;
+  int* status;
+} dkv_storage_args;
+int dkv_storage_unpack(const dkv_storage_args* args, void* stream);
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int dkv_version(void);
 

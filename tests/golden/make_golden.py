@@ -2,7 +2,7 @@
 
 Usage (only where the reference checkout exists; the GPU box does not have it):
     DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py [fixture ...]
-(no names: every fixture; names such as ``encode`` or ``codes``: only those).
+(no names: every fixture; names such as ``encode``, ``codes``, ``storage`` or ``tiny``: only those).
 
 Every array saved here is produced by the reference's own functions (scripts/progressive.py,
 scripts/kvtc.py, scripts/compressed_attention.py, scripts/dimmer.py, scripts/methods.py,
@@ -103,17 +103,43 @@ def encode_fixture(out: Path) -> None:
     )
 
 
+def storage_fixture(out: Path, methods, keys, values, scores) -> None:
+    """kvtc_storage.encode_bytes / decode_bytes of the tiny model's dkvtc caches at two budgets, the
+    second one high enough that some tokens take the ladder's exact rung (the reference's byte format,
+    kvtc_storage.py:42-135)."""
+    import kvtc_storage  # reference
+
+    fixture = {}
+    for tag, name in (("lo", "dkvtc@0.1:snap:floor1"), ("hi", "dkvtc@0.6:snap:floor1")):
+        with torch.inference_mode():
+            methods.apply(name, keys, values, scores)
+            codec = methods.codec("kvtc")
+            data = kvtc_storage.encode_bytes(codec, keys, values, codec.last_choice, tm.RECENT)
+            dec_keys, dec_values = kvtc_storage.decode_bytes(codec, data, dtype=torch.float32)
+        fixture.update({
+            f"{tag}_name": name, f"{tag}_data": np.frombuffer(data, dtype=np.uint8),
+            f"{tag}_choice_key": codec.last_choice["key"].numpy(), f"{tag}_choice_value": codec.last_choice["value"].numpy(),
+            # Layer 0, KV heads 0-1 of the restored caches (float32), to keep the file small.
+            f"{tag}_keys": dec_keys[0][0, :2].numpy(), f"{tag}_values": dec_values[0][0, :2].numpy(),
+        })
+    fixture["exact_rung"] = len(methods.codec("kvtc").streams["key"].rung_bytes)
+    np.savez_compressed(out / "storage.npz", **fixture)
+
+
 def main() -> None:
     out = HERE
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     only = sys.argv[1:]
-    if only:  # e.g. `make_golden.py encode`: write just the named fixtures
-        for name in only:
+    standalone = {"codes", "allocator", "encode"}  # fixtures that need no model
+    for name in only:
+        if name in standalone:  # e.g. `make_golden.py encode`: write just the named fixtures
             globals()[f"{name}_fixture"](out)
+    if only and not (set(only) - standalone):
         return
-    codes_fixture(out)
-    allocator_fixture(out)
-    encode_fixture(out)
+    if not only:
+        codes_fixture(out)
+        allocator_fixture(out)
+        encode_fixture(out)
 
     model = tm.build_model(torch.bfloat16)
     dimmer.install(model)
@@ -148,6 +174,10 @@ def main() -> None:
     torch.save(orders, tmp / "progressive.pt")
     methods = Methods("tiny", tmp / "none", tmp / "none", torch.device("cpu"), tm.RECENT, model=model,
                       kvtc=tmp / "kvtc.pt", progressive=tmp / "progressive.pt")
+    if not only or "storage" in only:
+        storage_fixture(out, methods, keys, values, scores)
+    if only and "tiny" not in only:
+        return
 
     inputs = dict(ids=ids.numpy(), keys=np.stack([bits16(k[0]) for k in keys]),
                   values=np.stack([bits16(v[0]) for v in values]),
