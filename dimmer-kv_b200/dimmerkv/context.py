@@ -535,6 +535,7 @@ class CompressedBatch:
             orders = self.key_orders if kind == "key" else self.value_orders
             gu = int(packed.union.numel())
             hot_tile, hot_row, words, headers, aux, per_seq = [], [], [], [], [], []
+            staged = set()
             for s, sel in enumerate(selected):
                 if sel.numel() == 0:
                     per_seq.append(0)
@@ -551,7 +552,14 @@ class CompressedBatch:
                 hot_tile.append(t0 + local // 128)
                 hot_row.append(local % 128)
                 ct = cold[s][kind]
-                staging, hstage = ct.stage(mid)
+                if id(ct) in staged:  # the same tier twice in one call: its staging rows are taken
+                    staging = torch.empty(mid.numel(), *ct.words.shape[1:], dtype=ct.words.dtype).pin_memory()
+                    hstage = torch.empty(mid.numel(), *ct.headers.shape[1:], dtype=ct.headers.dtype).pin_memory()
+                    torch.index_select(ct.words, 0, mid, out=staging)
+                    torch.index_select(ct.headers, 0, mid, out=hstage)
+                else:
+                    staging, hstage = ct.stage(mid)
+                    staged.add(id(ct))
                 words.append(staging)
                 headers.append(hstage)
                 if ct.hot_planes is not None:
