@@ -404,6 +404,8 @@ int dkv_storage_unpack(const dkv_storage_args* a, void* stream) {
   p.max_quads = a->max_quads;
   p.rows = a->rows;
   p.groups = a->groups;
+  p.n_rows_idx = a->n_rows_idx;
+  p.n_groups_idx = a->n_groups_idx;
   p.out = a->out;
   p.out_rows = a->out_rows;
   p.out_cols = a->out_cols;

@@ -150,6 +150,7 @@ struct StorageParams {
   int64_t max_quads;              // largest count * n_groups * 16 of any segment
   const int32_t* rows;            // token row of each segment's tokens
   const int32_t* groups;          // group index of each segment's groups
+  int64_t n_rows_idx, n_groups_idx;  // entries of rows[] and groups[]
   float* out;                     // [out_rows][out_cols], zero where no segment writes
   int64_t out_rows, out_cols;
   int* status;

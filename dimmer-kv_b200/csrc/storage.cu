@@ -29,24 +29,33 @@ __device__ __forceinline__ float f16_at(const uint8_t* data, uint64_t at) {
 
 __global__ void __launch_bounds__(kStorageThreads) storage_unpack_kernel(const StorageParams p) {
   const StorageSegment sg = p.segments[blockIdx.y];
-  const int64_t quads = static_cast<int64_t>(sg.count) * sg.n_groups * 16;
-  const int64_t q = static_cast<int64_t>(blockIdx.x) * kStorageThreads + threadIdx.x;
+  // Quads of a segment: at most max_quads < 2^31 (checked here and on the host), so 32-bit index math.
+  if (sg.count < 0 || sg.n_groups <= 0 || static_cast<int64_t>(sg.count) * sg.n_groups * 16 > p.max_quads) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.status, kErrBadDescriptor);
+    return;
+  }
+  const uint32_t quads = static_cast<uint32_t>(sg.count) * static_cast<uint32_t>(sg.n_groups) * 16u;
+  const uint32_t q = blockIdx.x * kStorageThreads + threadIdx.x;
   if (q >= quads) return;
   const int w = sg.width;
   if (w != 2 && w != 4 && w != 8) {
     record_error(p.status, kErrBadDescriptor);
     return;
   }
-  const int64_t e = q * 4;                      // first code of the quad, in (token, group, component) order
-  const int64_t tg = e / 64;                    // (token, group) index
-  const int i = static_cast<int>(tg / sg.n_groups);
-  const int j = static_cast<int>(tg % sg.n_groups);
-  const int c = static_cast<int>(e % 64);
-  const uint64_t byte0 = sg.codes_offset + static_cast<uint64_t>(e) * w / 8;
+  const uint32_t tg = q >> 4;                   // (token, group) index
+  const int i = static_cast<int>(tg / static_cast<uint32_t>(sg.n_groups));
+  const int j = static_cast<int>(tg - static_cast<uint32_t>(i) * static_cast<uint32_t>(sg.n_groups));
+  const int c = static_cast<int>(q & 15u) * 4;  // first component of the quad
+  const uint64_t byte0 = sg.codes_offset + (static_cast<uint64_t>(q) * 4u * static_cast<uint32_t>(w)) / 8u;
   const int nbytes = w / 2;                      // 4 codes x w bits
   const uint64_t hdr = static_cast<uint64_t>(tg) * 2;
   if (byte0 + nbytes > p.data_size || sg.low_offset + hdr + 2 > p.data_size ||
       sg.scale_offset + hdr + 2 > p.data_size) {
+    record_error(p.status, kErrBadDescriptor);
+    return;
+  }
+  if (sg.rows_offset < 0 || sg.groups_offset < 0 || static_cast<int64_t>(sg.rows_offset) + i >= p.n_rows_idx ||
+      static_cast<int64_t>(sg.groups_offset) + j >= p.n_groups_idx) {
     record_error(p.status, kErrBadDescriptor);
     return;
   }
@@ -75,9 +84,8 @@ int run_storage_unpack(const StorageParams& p, cudaStream_t stream) {
   if (p.n_segments < 0 || p.out_cols % 64 != 0 || p.max_quads < 0) return kDkvErrArgs;
   if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
   if (p.n_segments == 0 || p.max_quads == 0) return kDkvOk;
-  if (p.n_segments > 65535) return kDkvErrConfig;
+  if (p.n_segments > 65535 || p.max_quads >= (int64_t{1} << 31)) return kDkvErrConfig;
   const int64_t blocks = (p.max_quads + kStorageThreads - 1) / kStorageThreads;
-  if (blocks > 0x7FFFFFFF) return kDkvErrConfig;
   storage_unpack_kernel<<<dim3(static_cast<unsigned>(blocks), p.n_segments), kStorageThreads, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }

@@ -162,8 +162,8 @@ def _restore_coefficients_device(data_d: torch.Tensor, layout: _Layout, middle: 
     groups_d = torch.from_numpy(np.concatenate(groups_all)).to(device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     args = _lib.StorageArgs(data_d.data_ptr(), data_d.numel(), seg_d.data_ptr(), len(layout.segments), max_quads,
-                            rows_d.data_ptr(), groups_d.data_ptr(), decoded.data_ptr(), middle, features,
-                            status.data_ptr())
+                            rows_d.data_ptr(), groups_d.data_ptr(), rows_d.numel(), groups_d.numel(),
+                            decoded.data_ptr(), middle, features, status.data_ptr())
     lib = _lib.lib()
     _lib.check(lib.dkv_storage_unpack(args, torch.cuda.current_stream(device).cuda_stream), "dkv_storage_unpack")
     _lib.check_device_status(status)  # also keeps seg_d / rows_d / groups_d alive until the kernel is done

@@ -290,6 +290,8 @@ typedef struct dkv_storage_args {
   int64_t max_quads;             /* largest count * n_groups * 16 over the segments */
   const int32_t* rows;
   const int32_t* groups;
+  int64_t n_rows_idx;            /* entries of `rows` */
+  int64_t n_groups_idx;          /* entries of `groups` */
   float* out;                    /* [out_rows][out_cols] */
   int64_t out_rows, out_cols;
   int* status;
