@@ -20,7 +20,7 @@ namespace dkv {
 namespace {
 constexpr int kFinalizeThreads = 256;
 constexpr int kCombineThreads = 128;
-constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA
+constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA (one when a head has many rows)
 constexpr int kRChunk = 128;   // basis components per vbasis CTA
 constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
 constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a component chunk
@@ -126,15 +126,16 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
 }
 
 // One CTA per (conversation, KV head, block of 8 rows of the head); a thread per output dim.
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const FinalizeParams p, int n_chunks) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const FinalizeParams p, int n_chunks,
+                                                                   int rows_per_cta) {
   const int G = p.q_per_kv;
   const int n_kv = p.n_q_heads / G;
   const int s = blockIdx.x / n_kv, kvh = blockIdx.x % n_kv;
   const int D = p.head_dim;
   const int head_lo = max(p.row_begin, kvh * G * p.q_len);
   const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
-  const int rlo = head_lo + blockIdx.y * kCombineRows;
-  const int rhi = min(head_hi, rlo + kCombineRows);
+  const int rlo = head_lo + blockIdx.y * rows_per_cta;
+  const int rhi = min(head_hi, rlo + rows_per_cta);
   for (int i = threadIdx.x; i < (rhi - rlo) * D; i += blockDim.x) {
     const int row = rlo + i / D, d = i % D;
     const int lr = row - p.row_begin;
@@ -207,8 +208,10 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
       p, seq_block, row_block, n_row_blocks);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
   const int rows_per_head = min(p.n_rows, p.q_per_kv * p.q_len);
-  const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + kCombineRows - 1) / kCombineRows);
-  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks);
+  // Question-length queries put many rows on a head: one row per CTA then keeps the SMs busy.
+  const int rows_per_cta = rows_per_head >= 32 ? 1 : kCombineRows;
+  const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + rows_per_cta - 1) / rows_per_cta);
+  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks, rows_per_cta);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
