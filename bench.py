@@ -577,6 +577,7 @@ def run_question(args, cfg, device) -> dict:
             "warmup": args.warmup, "dtype": "bf16", "data": "synthetic (seeded random-init weights, random ids)",
             "config": {"workload": cfg["workload"], "context": tokens, "groups": conv.groups, "refined": count},
             "phases_ms": {k: round(v, 3) for k, v in phases.items()}, "fetched_bytes": fetched,
+            "refine_host_ms": {k: round(v * 1e3, 3) for k, v in getattr(batch, "last_refine_seconds", {}).items()},
             "topk_matches_lowest_index_rule": exact,
             "answer_after_refine": {"question_tokens": cfg["question"], "decode_steps": cfg["decode"],
                                     "seconds": round(answer_s, 3), "decode_tok_s": round(cfg["decode"] / answer_s, 2),

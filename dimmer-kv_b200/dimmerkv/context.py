@@ -13,6 +13,8 @@ scripts/compressed_attention.py:31-137) to a ragged batch packed into one launch
 
 from __future__ import annotations
 
+import time
+
 from dataclasses import dataclass
 
 import torch
@@ -530,6 +532,9 @@ class CompressedBatch:
         fetched = 0
         stream = side_stream or torch.cuda.Stream(self.device)
         main = torch.cuda.current_stream(self.device)
+        clock = time.perf_counter
+        phases = {"stage": 0.0, "layout": 0.0, "merge": 0.0, "append": 0.0, "work_lists": 0.0}
+        t_mark = clock()
         for kind in ("key", "value"):
             packed = self.keys if kind == "key" else self.values
             orders = self.key_orders if kind == "key" else self.value_orders
@@ -582,6 +587,8 @@ class CompressedBatch:
                 words_d = w_host.to(self.device, non_blocking=True)
                 headers_d = h_host.to(self.device, non_blocking=True)
             main.wait_stream(stream)
+            phases["stage"] += clock() - t_mark
+            t_mark = clock()
             # Layout of the refined tiles: per conversation, tiles of up to 128 selected tokens, every union
             # group holding 8 planes.
             old_code = packed.code.numel()
@@ -607,6 +614,8 @@ class CompressedBatch:
                 d32[i, 3] = 0 | (8 << 8)  # progressive codes, 8 planes
                 desc[i, 16:32] = torch.tensor(first, dtype=torch.uint8)
             desc_d = desc.to(self.device)
+            phases["layout"] += clock() - t_mark
+            t_mark = clock()
             code = torch.zeros(offs + 16, dtype=torch.uint8, device=self.device)
             code[:old_code] = packed.code
             # Selected tokens in refined-tile order (the loop above walks conversations in order).
@@ -628,6 +637,8 @@ class CompressedBatch:
                 g_done += n_tiles_s * gu
             torch.cuda.synchronize(self.device)
             self.check_status()
+            phases["merge"] += clock() - t_mark
+            t_mark = clock()
             # Append the refined tiles to the stream.
             first_new_tile = packed.n_tiles
             packed.code = code
@@ -669,9 +680,13 @@ class CompressedBatch:
                 tok += n
                 self.refined_tokens[s] += n
         self.seq_m = self.seq_m + torch.tensor(k_counts, dtype=torch.int32, device=self.device)
+        phases["append"] += clock() - t_mark
+        t_mark = clock()
         self._rebuild_key_items()
         self._v_items_cache.clear()
         self._work = {}
+        phases["work_lists"] += clock() - t_mark
+        self.last_refine_seconds = phases  # host wall time of the refine's phases
         self._score_cache = None
         for s, sel in enumerate(selected):
             self._refined_pos[s] = torch.cat([self._refined_pos[s], sel.to(torch.int64).cpu()])
