@@ -536,10 +536,15 @@ def run_question(args, cfg, device) -> dict:
     count = refine_count(cfg["fraction"], conv.middle)
     stream = torch.cuda.current_stream(device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    import gc
+
     with torch.inference_mode():
         for _ in range(max(1, args.warmup)):
             question_importance_direct(model, batch, cache, tail, [tokens])
         torch.cuda.synchronize(device)
+        # The timed path, not the interpreter's collector: collect now, none inside the timed phases.
+        gc.collect()
+        gc.disable()
         ev[0].record(stream)
         imp = question_importance_direct(model, batch, cache, tail, [tokens])[0]
         ev[1].record(stream)
@@ -548,6 +553,7 @@ def run_question(args, cfg, device) -> dict:
         fetched = batch.refine(selected, [cold], torch.cuda.Stream(device))
         ev[3].record(stream)
         torch.cuda.synchronize(device)
+        gc.enable()
         batch.check_status()
         # The selection against the lowest-index rule on the same importance vector (host check).
         start, end = batch.spans[0]
