@@ -28,7 +28,10 @@ extern "C" {
 #define DKV_ERR_TENSORMAP 4  /* cuTensorMapEncodeTiled rejected the basis layout */
 #define DKV_ERR_SCRATCH 5    /* the call needs more scratch than dkv_attend_layer_static's fixed array */
 
-/* Packed plane-stream descriptors (layout documented in DESIGN.md, "Plane stream"). */
+/* Packed plane-stream descriptors. A stream is cut into tiles of up to 128 tokens; per (tile, union group)
+ * one 16-byte-aligned block holds the f16 (low, scale) headers of the tokens with at least one plane, then
+ * for every plane j one 64-bit word per token holding it (tokens sorted by plane count, so the holders of
+ * plane j start at first[j]). dimmerkv/planes.py writes this layout. */
 typedef struct dkv_tile {
   int32_t seq, token_base, n_tokens, n_groups, group_base, score_base, reserved0, reserved1;
 } dkv_tile;

@@ -23,7 +23,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-REF = Path(os.environ.get("DIMMERKV_REFERENCE", "/root/reference")) / "scripts"
+if "DIMMERKV_REFERENCE" not in os.environ:
+    raise SystemExit("set DIMMERKV_REFERENCE to the reference checkout (the directory holding scripts/)")
+REF = Path(os.environ["DIMMERKV_REFERENCE"]) / "scripts"
 sys.path.insert(0, str(REF))
 
 import compressed_attention  # noqa: E402  (reference)
