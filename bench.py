@@ -411,8 +411,8 @@ def storage_rate(device, middle: int = 16348, features: int = 28672, launches: i
     groups_d = torch.from_numpy(np.concatenate(groups_all)).to(device)
     out = torch.zeros(middle, features, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
-    max_quads = max(s[3] * s[4] * 16 for s in seg)
-    a = _lib.StorageArgs(data.data_ptr(), offset, seg_d.data_ptr(), len(seg), max_quads, rows_d.data_ptr(),
+    max_units = max(s[3] * s[4] * 4 for s in seg)
+    a = _lib.StorageArgs(data.data_ptr(), offset, seg_d.data_ptr(), len(seg), max_units, rows_d.data_ptr(),
                          groups_d.data_ptr(), rows_d.numel(), groups_d.numel(), out.data_ptr(), middle, features,
                          status.data_ptr())
     lib = _lib.lib()

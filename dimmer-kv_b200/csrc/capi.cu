@@ -401,7 +401,7 @@ int dkv_storage_unpack(const dkv_storage_args* a, void* stream) {
   p.data_size = a->data_size;
   p.segments = reinterpret_cast<const dkv::StorageSegment*>(a->segments);
   p.n_segments = a->n_segments;
-  p.max_quads = a->max_quads;
+  p.max_units = a->max_units;
   p.rows = a->rows;
   p.groups = a->groups;
   p.n_rows_idx = a->n_rows_idx;

@@ -147,7 +147,7 @@ struct StorageParams {
   uint64_t data_size;
   const StorageSegment* segments;
   int n_segments;
-  int64_t max_quads;              // largest count * n_groups * 16 of any segment
+  int64_t max_units;              // largest count * n_groups * 4 (16-component units) of any segment
   const int32_t* rows;            // token row of each segment's tokens
   const int32_t* groups;          // group index of each segment's groups
   int64_t n_rows_idx, n_groups_idx;  // entries of rows[] and groups[]

@@ -8,9 +8,9 @@
 // token is in the clear, so every segment's offsets follow) and lists the segments; one launch
 // restores a whole stream.
 //
-// One thread per four consecutive components: their codes are one byte (w = 2), two (w = 4) or four
-// (w = 8), read byte by byte because the format packs its arrays without alignment; the four values
-// go out as one 16-byte store.
+// One thread per 16 consecutive components of a (token, group): their codes are 4 (w = 2), 8 (w = 4) or
+// 16 (w = 8) bytes, read byte by byte because the format packs its arrays without alignment; the values
+// go out as four 16-byte stores. The segment record is read once per CTA.
 #include <cuda_fp16.h>
 
 #include "dkv_kernels.h"
@@ -28,26 +28,29 @@ __device__ __forceinline__ float f16_at(const uint8_t* data, uint64_t at) {
 }  // namespace
 
 __global__ void __launch_bounds__(kStorageThreads) storage_unpack_kernel(const StorageParams p) {
-  const StorageSegment sg = p.segments[blockIdx.y];
-  // Quads of a segment: at most max_quads < 2^31 (checked here and on the host), so 32-bit index math.
-  if (sg.count < 0 || sg.n_groups <= 0 || static_cast<int64_t>(sg.count) * sg.n_groups * 16 > p.max_quads) {
+  __shared__ StorageSegment sg_s;
+  if (threadIdx.x == 0) sg_s = p.segments[blockIdx.y];
+  __syncthreads();
+  const StorageSegment sg = sg_s;
+  if (sg.count < 0 || sg.n_groups <= 0 || static_cast<int64_t>(sg.count) * sg.n_groups * 4 > p.max_units) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.status, kErrBadDescriptor);
     return;
   }
-  const uint32_t quads = static_cast<uint32_t>(sg.count) * static_cast<uint32_t>(sg.n_groups) * 16u;
+  // Units of a segment: at most max_units < 2^31 (checked here and on the host), so 32-bit index math.
+  const uint32_t units = static_cast<uint32_t>(sg.count) * static_cast<uint32_t>(sg.n_groups) * 4u;
   const uint32_t q = blockIdx.x * kStorageThreads + threadIdx.x;
-  if (q >= quads) return;
+  if (q >= units) return;
   const int w = sg.width;
   if (w != 2 && w != 4 && w != 8) {
     record_error(p.status, kErrBadDescriptor);
     return;
   }
-  const uint32_t tg = q >> 4;                   // (token, group) index
+  const uint32_t tg = q >> 2;                   // (token, group) index
   const int i = static_cast<int>(tg / static_cast<uint32_t>(sg.n_groups));
   const int j = static_cast<int>(tg - static_cast<uint32_t>(i) * static_cast<uint32_t>(sg.n_groups));
-  const int c = static_cast<int>(q & 15u) * 4;  // first component of the quad
-  const uint64_t byte0 = sg.codes_offset + (static_cast<uint64_t>(q) * 4u * static_cast<uint32_t>(w)) / 8u;
-  const int nbytes = w / 2;                      // 4 codes x w bits
+  const int c = static_cast<int>(q & 3u) * 16;  // first of the thread's 16 components
+  const uint64_t byte0 = sg.codes_offset + (static_cast<uint64_t>(q) * 16u * static_cast<uint32_t>(w)) / 8u;
+  const int nbytes = 2 * w;                      // 16 codes x w bits
   const uint64_t hdr = static_cast<uint64_t>(tg) * 2;
   if (byte0 + nbytes > p.data_size || sg.low_offset + hdr + 2 > p.data_size ||
       sg.scale_offset + hdr + 2 > p.data_size) {
@@ -65,27 +68,34 @@ __global__ void __launch_bounds__(kStorageThreads) storage_unpack_kernel(const S
     record_error(p.status, kErrBadDescriptor);
     return;
   }
-  uint32_t bits = 0;
-  for (int b = 0; b < nbytes; ++b) bits |= static_cast<uint32_t>(p.data[byte0 + b]) << (8 * b);
+  // The thread's 2w bytes of codes, read byte by byte (the format aligns nothing), as little-endian words.
+  uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int b = 0; b < 16; ++b)
+    if (b < nbytes) words[b >> 2] |= static_cast<uint32_t>(p.data[byte0 + b]) << (8 * (b & 3));
   const uint32_t mask = (1u << w) - 1u;
   const float low = f16_at(p.data, sg.low_offset + hdr);
   const float scale = f16_at(p.data, sg.scale_offset + hdr);
-  float v[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float code = static_cast<float>((bits >> (k * w)) & mask);
-    v[k] = __fadd_rn(__fmul_rn(code, scale), low);
-  }
   float4* dst = reinterpret_cast<float4*>(p.out + static_cast<int64_t>(row) * p.out_cols + group * 64 + c);
-  *dst = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+  for (int k4 = 0; k4 < 4; ++k4) {
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int bit = (4 * k4 + k) * w;  // bit of code 4 k4 + k in the thread's little-endian run
+      const float code = static_cast<float>((words[bit >> 5] >> (bit & 31)) & mask);
+      v[k] = __fadd_rn(__fmul_rn(code, scale), low);
+    }
+    dst[k4] = make_float4(v[0], v[1], v[2], v[3]);
+  }
 }
 
 int run_storage_unpack(const StorageParams& p, cudaStream_t stream) {
-  if (p.n_segments < 0 || p.out_cols % 64 != 0 || p.max_quads < 0) return kDkvErrArgs;
+  if (p.n_segments < 0 || p.out_cols % 64 != 0 || p.max_units < 0) return kDkvErrArgs;
   if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
-  if (p.n_segments == 0 || p.max_quads == 0) return kDkvOk;
-  if (p.n_segments > 65535 || p.max_quads >= (int64_t{1} << 31)) return kDkvErrConfig;
-  const int64_t blocks = (p.max_quads + kStorageThreads - 1) / kStorageThreads;
+  if (p.n_segments == 0 || p.max_units == 0) return kDkvOk;
+  if (p.n_segments > 65535 || p.max_units >= (int64_t{1} << 31)) return kDkvErrConfig;
+  const int64_t blocks = (p.max_units + kStorageThreads - 1) / kStorageThreads;
   storage_unpack_kernel<<<dim3(static_cast<unsigned>(blocks), p.n_segments), kStorageThreads, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }

@@ -79,7 +79,7 @@ class StorageArgs(ctypes.Structure):
 
     _fields_ = [
         ("data", c_void_p), ("data_size", c_uint64), ("segments", c_void_p), ("n_segments", c_int32),
-        ("max_quads", c_int64), ("rows", c_void_p), ("groups", c_void_p), ("n_rows_idx", c_int64),
+        ("max_units", c_int64), ("rows", c_void_p), ("groups", c_void_p), ("n_rows_idx", c_int64),
         ("n_groups_idx", c_int64), ("out", c_void_p), ("out_rows", c_int64), ("out_cols", c_int64),
         ("status", c_void_p),
     ]

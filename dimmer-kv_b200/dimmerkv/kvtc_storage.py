@@ -149,19 +149,19 @@ def _restore_coefficients_device(data_d: torch.Tensor, layout: _Layout, middle: 
     seg = np.zeros(len(layout.segments), dtype=_lib.STORAGE_SEGMENT)
     rows_all, groups_all = [], []
     r_off = g_off = 0
-    max_quads = 0
+    max_units = 0
     for i, (rows, chosen, width, codes_at, low_at, scale_at) in enumerate(layout.segments):
         seg[i] = (codes_at, low_at, scale_at, rows.size, chosen.size, width, r_off, g_off, 0)
         rows_all.append(rows.astype(np.int32))
         groups_all.append(chosen.astype(np.int32))
         r_off += rows.size
         g_off += chosen.size
-        max_quads = max(max_quads, rows.size * chosen.size * 16)
+        max_units = max(max_units, rows.size * chosen.size * 4)
     seg_d = torch.from_numpy(seg.view(np.uint8).copy()).to(device)
     rows_d = torch.from_numpy(np.concatenate(rows_all)).to(device)
     groups_d = torch.from_numpy(np.concatenate(groups_all)).to(device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
-    args = _lib.StorageArgs(data_d.data_ptr(), data_d.numel(), seg_d.data_ptr(), len(layout.segments), max_quads,
+    args = _lib.StorageArgs(data_d.data_ptr(), data_d.numel(), seg_d.data_ptr(), len(layout.segments), max_units,
                             rows_d.data_ptr(), groups_d.data_ptr(), rows_d.numel(), groups_d.numel(),
                             decoded.data_ptr(), middle, features, status.data_ptr())
     lib = _lib.lib()

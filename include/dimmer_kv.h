@@ -290,7 +290,7 @@ typedef struct dkv_storage_args {
   uint64_t data_size;
   const dkv_storage_segment* segments;
   int32_t n_segments;
-  int64_t max_quads;             /* largest count * n_groups * 16 over the segments */
+  int64_t max_units;             /* largest count * n_groups * 4 (units of 16 components) over the segments */
   const int32_t* rows;
   const int32_t* groups;
   int64_t n_rows_idx;            /* entries of `rows` */

@@ -83,7 +83,7 @@ def test_storage_unpack_rejects_out_of_range_segments(golden, tmp_path):
     groups = torch.tensor([0], dtype=torch.int32, device=DEV)
     out = torch.full((2, 64), 7.0, device=DEV)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    a = _lib.StorageArgs(data.data_ptr(), 64, seg_d.data_ptr(), 1, 2 * 1 * 16, rows.data_ptr(), groups.data_ptr(),
+    a = _lib.StorageArgs(data.data_ptr(), 64, seg_d.data_ptr(), 1, 2 * 1 * 4, rows.data_ptr(), groups.data_ptr(),
                          2, 1, out.data_ptr(), 2, 64, status.data_ptr())
     _lib.check(_lib.lib().dkv_storage_unpack(a, torch.cuda.current_stream().cuda_stream), "dkv_storage_unpack")
     torch.cuda.synchronize()
