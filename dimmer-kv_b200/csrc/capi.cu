@@ -175,6 +175,11 @@ int dkv_softmax_stats(const dkv_attend_args* a, void* stream) {
   p.p_exact = a->p_exact;
   if (a->softmax_mode < 0 || a->softmax_mode > 2) return DKV_ERR_ARGS;
   p.mode = a->softmax_mode;
+  // The value stage's partial-sum buffer is free until the value weights run: it holds the softmax's
+  // per-slice partials when few long rows are split over several CTAs.
+  p.scratch = a->partial;
+  p.scratch_floats = a->partial != nullptr ? static_cast<int64_t>(a->n_v_items) * a->rows_pad * a->v_item_groups * 64 : 0;
+  p.n_sms = sm_count();
   return dkv::run_softmax_stats(p, static_cast<cudaStream_t>(stream));
 }
 

@@ -64,6 +64,9 @@ struct SoftmaxParams {
   float* row_stats;               // [n_seq][n_q_heads][q_len][4]: max, 1/sum, compressed mass, 0
   float* p_exact;                 // [n_seq][n_q_heads][q_len][n_exact], fp32 (unrounded)
   int mode;                       // kSoftmaxFull, kSoftmaxLocal or kSoftmaxGlobal
+  float* scratch;                 // optional: per-(row, slice) partials when few rows are long
+  int64_t scratch_floats;
+  int n_sms;                      // SMs of the device (sizes the slices)
 };
 constexpr int kSoftmaxFull = 0;
 constexpr int kSoftmaxLocal = 1;   // row_stats <- (max, sum of exponentials) of this shard
