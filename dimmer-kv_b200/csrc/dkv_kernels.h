@@ -117,11 +117,10 @@ struct FinalizeParams {
   int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact, layer, n_cols;
   void* out;                      // [n_seq][q_len][n_q_heads][head_dim]
   int out_f32;                    // fp32 output instead of bf16
-  float* vpart;                   // [finalize_chunks(r_v) * finalize_item_splits(n_seq)][n_seq][n_rows_pad][head_dim]
+  float* vpart;                   // [finalize_chunks(r_v)][n_seq][n_rows_pad][head_dim]
   int* status;
 };
 int finalize_chunks(int r_v);
-int finalize_item_splits(int n_seq);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);
 
 // Encode side of the progressive codec: quantize8 + per-rung errors (encode.cu).

@@ -9,9 +9,7 @@
 //             CTA stages its basis slice [128 components x head_dim] in shared memory, reduces the
 //             items' partial sums of those components for its conversations and multiplies them by
 //             the slice: the layer's value basis is read once per 8 conversations instead of once per
-//             conversation. With fewer than 8 conversations (one long context) a chunk's covering items
-//             are many, and their sum is cut into 8 shares, each CTA writing its own slot. Output: per
-//             (chunk, share) partial outputs [chunks x shares][conversations][rows][head_dim].
+//             conversation. Output: per-chunk partial outputs [chunks][conversations][rows][head_dim].
 //   combine : sums the chunks in a fixed order (deterministic), adds the mean term and the exact
 //             tokens, and writes the HF layout [batch, q_len, q_heads, head_dim].
 #include "dkv_kernels.h"
@@ -26,28 +24,23 @@ constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA (one whe
 constexpr int kRChunk = 128;   // basis components per vbasis CTA
 constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
 constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a component chunk
-constexpr int kItemSplits = 8;     // shares of a chunk's covering items (fewer than kSeqBlock conversations)
 }  // namespace
 
 __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block,
-                                                                  int row_block, int n_row_blocks, int item_splits) {
+                                                                  int row_block, int n_row_blocks) {
   extern __shared__ float smem_f[];
   const int D = p.head_dim;
   const int D2 = D / 2;
   const int G = p.q_per_kv;
   const int chunk = blockIdx.x, kvh = blockIdx.y;
-  // blockIdx.z = (conversation block, row block, item split): with few conversations the items covering a
-  // chunk are many, and each split sums its share of them into a slot of its own (combine adds the slots).
-  const int zi = static_cast<int>(blockIdx.z % item_splits);
-  const int zr = static_cast<int>(blockIdx.z / item_splits);
-  const int s0 = (zr / n_row_blocks) * seq_block;
+  const int s0 = (blockIdx.z / n_row_blocks) * seq_block;
   const int n_s = min(seq_block, p.n_seq - s0);
   const int r0 = chunk * kRChunk;
   // Rows of this KV head inside the call, then this CTA's block of them (many query rows per head,
   // few conversations: the rows are spread over more CTAs).
   const int head_lo = max(p.row_begin, kvh * G * p.q_len);
   const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
-  const int rlo = head_lo + (zr % n_row_blocks) * row_block;
+  const int rlo = head_lo + static_cast<int>(blockIdx.z % n_row_blocks) * row_block;
   const int rhi = min(head_hi, rlo + row_block);
   const int nr = rhi - rlo;
   if (nr <= 0 || n_s <= 0) return;
@@ -101,9 +94,8 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
     const int rr = (i / kRChunk) % nr, c = i % kRChunk;
     const int64_t col = (rlo - p.row_begin + rr) * static_cast<int64_t>(item_cols) + (r0 % item_cols) + c;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const int nc = n_cover[sl];
-    int j = sl * kCoverPerSeq + nc * zi / item_splits;
-    const int j1 = sl * kCoverPerSeq + nc * (zi + 1) / item_splits;
+    int j = sl * kCoverPerSeq;
+    const int j1 = j + n_cover[sl];
     for (; j + 4 <= j1; j += 4) {
 #pragma unroll
       for (int u = 0; u < 4; ++u)
@@ -128,8 +120,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
     }
     const int s = s0 + j / nr, rr = j % nr;
     float2* dst = reinterpret_cast<float2*>(
-        p.vpart + ((static_cast<int64_t>(chunk * item_splits + zi) * p.n_seq + s) * p.n_rows_pad +
-                   (rlo - p.row_begin + rr)) * D);
+        p.vpart + ((static_cast<int64_t>(chunk) * p.n_seq + s) * p.n_rows_pad + (rlo - p.row_begin + rr)) * D);
     dst[dp] = make_float2(ax, ay);
   }
 }
@@ -191,8 +182,6 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Finalize
 
 int finalize_chunks(int r_v) { return (r_v + kRChunk - 1) / kRChunk; }
 
-int finalize_item_splits(int n_seq) { return n_seq < kSeqBlock ? kItemSplits : 1; }
-
 int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   if (p.head_dim % 64 != 0 || p.head_dim > 256 || p.q_per_kv < 1 || p.n_q_heads % p.q_per_kv != 0 ||
       p.vpart == nullptr || p.item_groups % 2 != 0 || p.n_rows > p.n_rows_pad)
@@ -201,7 +190,6 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   // Rows of one KV head inside this call: at most q_per_kv * q_len and at most n_rows.
   const int nr_max = min(p.n_rows, p.q_per_kv * p.q_len);
   const int n_chunks = finalize_chunks(p.r_v);
-  const int item_splits = finalize_item_splits(p.n_seq);
   const int n_kv = p.n_q_heads / p.q_per_kv;
   // Many rows per KV head and few conversations (question-length queries): cut each head's rows into
   // blocks of 16 so that the grid covers the SMs (a call's rows then span one or two KV heads).
@@ -216,14 +204,14 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   if (cudaFuncSetAttribute(vbasis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kDkvErrCuda;
   const int seq_blocks = (p.n_seq + seq_block - 1) / seq_block;
-  vbasis_kernel<<<dim3(n_chunks, n_kv, seq_blocks * n_row_blocks * item_splits), kFinalizeThreads, smem, stream>>>(
-      p, seq_block, row_block, n_row_blocks, item_splits);
+  vbasis_kernel<<<dim3(n_chunks, n_kv, seq_blocks * n_row_blocks), kFinalizeThreads, smem, stream>>>(
+      p, seq_block, row_block, n_row_blocks);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
   const int rows_per_head = min(p.n_rows, p.q_per_kv * p.q_len);
   // Question-length queries put many rows on a head: one row per CTA then keeps the SMs busy.
   const int rows_per_cta = rows_per_head >= 32 ? 1 : kCombineRows;
   const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + rows_per_cta - 1) / rows_per_cta);
-  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks * item_splits, rows_per_cta);
+  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks, rows_per_cta);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
