@@ -418,4 +418,24 @@ int dkv_storage_unpack(const dkv_storage_args* a, void* stream) {
   return dkv::run_storage_unpack(p, static_cast<cudaStream_t>(stream));
 }
 
+int64_t dkv_alloc_workspace_bytes(int64_t slots, int32_t levels) { return dkv::alloc_workspace_bytes(slots, levels); }
+
+int dkv_allocate_rungs(const dkv_alloc_args* a, void* stream) {
+  if (a == nullptr || a->errors == nullptr || a->level_bytes == nullptr || a->counts == nullptr ||
+      a->status == nullptr)
+    return DKV_ERR_ARGS;
+  dkv::AllocParams p{};
+  p.errors = a->errors;
+  p.level_bytes = a->level_bytes;
+  p.slots = a->slots;
+  p.middle = a->middle;
+  p.levels = a->levels;
+  p.remaining = a->remaining;
+  p.counts = a->counts;
+  p.workspace = a->workspace;
+  p.workspace_bytes = a->workspace_bytes;
+  p.status = a->status;
+  return dkv::run_allocate(p, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

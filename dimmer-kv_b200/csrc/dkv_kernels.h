@@ -139,6 +139,21 @@ struct EncodeParams {
 };
 int run_encode(const EncodeParams& p, cudaStream_t stream);
 
+// Per-token rung allocator (allocate.cu).
+struct AllocParams {
+  const float* errors;            // [slots][levels], keys' slots first (middle of them), then values'
+  const int64_t* level_bytes;     // [2][levels]: bytes of each level, key stream then value stream
+  int64_t slots, middle;
+  int levels;
+  int64_t remaining;              // budget minus every slot's coarsest level
+  int64_t* counts;                // [slots]: upgrades taken
+  void* workspace;                // alloc_workspace_bytes(slots, levels) bytes, 256-byte aligned
+  int64_t workspace_bytes;
+  int* status;
+};
+int64_t alloc_workspace_bytes(int64_t slots, int levels);
+int run_allocate(const AllocParams& p, cudaStream_t stream);
+
 // Restore of the kvtc byte format (storage.cu).
 struct StorageSegment {
   uint64_t codes_offset, low_offset, scale_offset;  // byte offsets into the stored bytes

@@ -23,7 +23,8 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
            "dkv_attend_tail",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
-           "dkv_vpart_floats", "dkv_encode_groups", "dkv_storage_unpack", "dkv_version", "dkv_status_string")
+           "dkv_vpart_floats", "dkv_encode_groups", "dkv_storage_unpack", "dkv_alloc_workspace_bytes", "dkv_allocate_rungs",
+           "dkv_version", "dkv_status_string")
 
 
 class AttendArgs(ctypes.Structure):
@@ -71,6 +72,16 @@ class EncodeArgs(ctypes.Structure):
         ("coeff", c_void_p), ("coeff_stride", c_int64), ("tokens", c_int32), ("features", c_int32),
         ("rung_planes", c_void_p), ("n_rungs", c_int32), ("codes", c_void_p), ("low", c_void_p), ("span", c_void_p),
         ("rung_error", c_void_p), ("energy", c_void_p), ("status", c_void_p),
+    ]
+
+
+class AllocArgs(ctypes.Structure):
+    """Mirror of ``dkv_alloc_args``."""
+
+    _fields_ = [
+        ("errors", c_void_p), ("level_bytes", c_void_p), ("slots", c_int64), ("middle", c_int64), ("levels", c_int32),
+        ("remaining", c_int64), ("counts", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_int64),
+        ("status", c_void_p),
     ]
 
 
@@ -145,10 +156,13 @@ def lib():
         handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
         handle.dkv_unpack.restype = c_int32
         for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs),
-                         ("dkv_encode_groups", EncodeArgs), ("dkv_storage_unpack", StorageArgs)):
+                         ("dkv_encode_groups", EncodeArgs), ("dkv_storage_unpack", StorageArgs),
+                         ("dkv_allocate_rungs", AllocArgs)):
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(st), c_void_p]
             fn.restype = c_int32
+        handle.dkv_alloc_workspace_bytes.argtypes = [c_int64, c_int32]
+        handle.dkv_alloc_workspace_bytes.restype = c_int64
         handle.dkv_vpart_floats.argtypes = [c_int32, c_int32, c_int32, c_int32]
         handle.dkv_vpart_floats.restype = c_int64
         handle.dkv_version.argtypes = []

@@ -259,7 +259,13 @@ class KVTCCodec:
 
 
 def allocate_rungs(errors: torch.Tensor, level_bytes: torch.Tensor, middle: int, budget: int) -> torch.Tensor:
-    """Greedy per-slot rung choice under a byte budget (kvtc.py:277-298), host-side by design."""
+    """Greedy per-slot rung choice under a byte budget (kvtc.py:277-298). float32 errors on a CUDA device
+    go to dkv_allocate_rungs (same counts, a radix select instead of the sort); otherwise the reference's
+    torch operations."""
+    if errors.is_cuda and errors.dtype == torch.float32 and 2 <= errors.shape[1] <= 64:
+        from .allocate import allocate_rungs_gpu
+
+        return allocate_rungs_gpu(errors, level_bytes, middle, budget)
     slots, levels = errors.shape
     sizes = level_bytes.view(2, levels).repeat_interleave(middle, dim=0).double()
     base = int(sizes[:, 0].sum())

@@ -301,6 +301,27 @@ typedef struct dkv_storage_args {
 } dkv_storage_args;
 int dkv_storage_unpack(const dkv_storage_args* args, void* stream);
 
+/* The per-token rung allocator of DimmerKV, on the GPU. Replaces kvtc.allocate_rungs (scripts/kvtc.py:
+ * 277-298): upgrades valued by error drop per extra byte (made non-increasing along each slot's levels),
+ * taken greedily in descending value (ties by flat index) while they fit the budget; counts[slot] = the
+ * upgrades taken. Bit-exact with the sort-based reference (integer byte sums; a radix select on the
+ * values' order instead of a sort). The caller checks that the coarsest levels fit (the reference's
+ * ValueError) and passes what is left of the budget. */
+typedef struct dkv_alloc_args {
+  const float* errors;           /* [slots][levels] float32, the key stream's middle slots first */
+  const int64_t* level_bytes;    /* [2][levels]: each level's bytes, key stream then value stream */
+  int64_t slots;
+  int64_t middle;                /* key slots */
+  int32_t levels;                /* 2..64 */
+  int64_t remaining;             /* budget - sum over slots of the coarsest level's bytes, >= 0 */
+  int64_t* counts;               /* [slots] out */
+  void* workspace;               /* dkv_alloc_workspace_bytes(slots, levels) bytes, 256-byte aligned */
+  int64_t workspace_bytes;
+  int* status;
+} dkv_alloc_args;
+int64_t dkv_alloc_workspace_bytes(int64_t slots, int32_t levels);
+int dkv_allocate_rungs(const dkv_alloc_args* args, void* stream);
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int dkv_version(void);
 
