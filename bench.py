@@ -437,6 +437,57 @@ def storage_rate(device, middle: int = 16348, features: int = 28672, launches: i
             "peak_source": "of measured (hbm_gbs)" if peaks else "of fallback"}
 
 
+def allocate_rate(device, middle: int = 16348, levels: int = 12, launches: int = 5) -> dict:
+    """dkv_allocate_rungs on the largest cfg3 conversation's slots (16348 key + 16348 value tokens, 12
+    rungs, seeded errors, half the way from the coarsest to the finest budget), beside the reference's
+    torch sort-and-cumsum on the same device. CUDA events after 3 warm-up calls; the counts must agree."""
+    import numpy as np
+    import torch
+
+    from dimmerkv.allocate import allocate_rungs_gpu
+
+    rng = np.random.default_rng(9)
+    slots = 2 * middle
+    e = -np.sort(-rng.random((slots, levels)).astype(np.float32), axis=1)
+    sk, sv = np.cumsum(rng.integers(1, 300, size=levels)), np.cumsum(rng.integers(1, 300, size=levels))
+    level_bytes = torch.tensor(np.concatenate([sk, sv]), dtype=torch.int64)
+    base = middle * int(sk[0] + sv[0])
+    budget = base + (middle * int(sk[-1] + sv[-1]) - base) // 2
+    errors = torch.from_numpy(e).to(device)
+
+    def reference():  # the reference's arithmetic (scripts/kvtc.py:287-298) as torch ops on the device
+        sizes = level_bytes.to(device).view(2, levels).repeat_interleave(middle, dim=0).double()
+        gains = (errors[:, :-1] - errors[:, 1:]).clamp_min(0).double()
+        costs = sizes[:, 1:] - sizes[:, :-1]
+        value = (gains / costs).cummin(dim=1).values
+        order = torch.sort(value.reshape(-1), descending=True, stable=True).indices
+        taken = order[costs.reshape(-1)[order].cumsum(0) <= budget - base]
+        counts = torch.zeros(slots, dtype=torch.long, device=device)
+        counts.index_add_(0, taken // (levels - 1), torch.ones_like(taken))
+        return counts
+
+    stream = torch.cuda.current_stream(device)
+    timings = {}
+    for name, fn in (("kernel", lambda: allocate_rungs_gpu(errors, level_bytes, middle, budget)), ("torch", reference)):
+        for _ in range(3):
+            out = fn()
+        torch.cuda.synchronize(device)
+        t = []
+        for _ in range(launches):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = fn()
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            t.append(a.elapsed_time(b))
+        timings[name] = (statistics.mean(t), out)
+    same = bool(torch.equal(timings["kernel"][1], timings["torch"][1]))
+    return {"kernel": "allocate_rungs (radix select)", "slots": slots, "levels": levels,
+            "ms": round(timings["kernel"][0], 4), "torch_sort_ms": round(timings["torch"][0], 4),
+            "counts_equal": same,
+            "note": "per call through the Python wrapper (includes its argument checks and status read)"}
+
+
 def run_kernels(args, cfg, device) -> dict:
     """Profiling case: every layer's dkv_attend_layer over the packed codes, random queries, no model."""
     import torch
@@ -477,7 +528,8 @@ def run_kernels(args, cfg, device) -> dict:
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
             "gpu_launches": len(timer.events) * KERNELS_PER_LAYER, "unpack": unpack_rate(batch, device),
-            "encode": encode_rate(device), "storage": storage_rate(device)}
+            "encode": encode_rate(device), "storage": storage_rate(device),
+            "allocate": allocate_rate(device)}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
@@ -739,6 +791,7 @@ def run_ours(args, cfg, rank, world, device):
     unpack = unpack_rate(batch, device) if rank == 0 else None
     encode = encode_rate(device) if rank == 0 else None
     storage = storage_rate(device) if rank == 0 else None
+    allocate = allocate_rate(device) if rank == 0 else None
 
     result = None
     if rank == 0:
@@ -761,6 +814,7 @@ def run_ours(args, cfg, rank, world, device):
             "unpack": unpack,
             "encode": encode,
             "storage": storage,
+            "allocate": allocate,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }
