@@ -418,6 +418,25 @@ int dkv_storage_unpack(const dkv_storage_args* a, void* stream) {
   return dkv::run_storage_unpack(p, static_cast<cudaStream_t>(stream));
 }
 
+int dkv_demote(const dkv_demote_args* a, void* stream) {
+  if (a == nullptr || a->old_code == nullptr || a->old_groups == nullptr || a->new_code == nullptr ||
+      a->new_groups == nullptr || a->old_index == nullptr || a->n_tokens == nullptr || a->status == nullptr)
+    return DKV_ERR_ARGS;
+  dkv::DemoteParams p{};
+  p.old_code = a->old_code;
+  p.old_code_size = a->old_code_size;
+  p.old_groups = reinterpret_cast<const GroupDesc*>(a->old_groups);
+  p.n_old_groups = a->n_old_groups;
+  p.new_code = a->new_code;
+  p.new_code_size = a->new_code_size;
+  p.new_groups = reinterpret_cast<const GroupDesc*>(a->new_groups);
+  p.old_index = a->old_index;
+  p.n_tokens = a->n_tokens;
+  p.n_new = a->n_new;
+  p.status = a->status;
+  return dkv::run_demote(p, static_cast<cudaStream_t>(stream));
+}
+
 int64_t dkv_alloc_workspace_bytes(int64_t slots, int32_t levels) { return dkv::alloc_workspace_bytes(slots, levels); }
 
 int dkv_allocate_rungs(const dkv_alloc_args* a, void* stream) {

@@ -139,6 +139,22 @@ struct EncodeParams {
 };
 int run_encode(const EncodeParams& p, cudaStream_t stream);
 
+// Tier management: demotion by dropping planes (demote.cu).
+struct DemoteParams {
+  const uint8_t* old_code;
+  uint64_t old_code_size;
+  const GroupDesc* old_groups;
+  int64_t n_old_groups;
+  uint8_t* new_code;              // zero-filled by the caller (block padding stays zero)
+  uint64_t new_code_size;
+  const GroupDesc* new_groups;    // [n_new]: the new blocks' layout
+  const int32_t* old_index;       // [n_new]: the old block each new block comes from
+  const int32_t* n_tokens;        // [n_new]: tokens of the block's tile
+  int64_t n_new;
+  int* status;
+};
+int run_demote(const DemoteParams& p, cudaStream_t stream);
+
 // Per-token rung allocator (allocate.cu).
 struct AllocParams {
   const float* errors;            // [slots][levels], keys' slots first (middle of them), then values'

@@ -23,7 +23,7 @@ DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out wai
 EXPORTS = ("dkv_attend_layer", "dkv_key_scores", "dkv_softmax_stats", "dkv_value_weights", "dkv_finalize",
            "dkv_attend_tail",
            "dkv_unpack", "dkv_importance", "dkv_topk", "dkv_refine_merge", "dkv_attend_layer_static",
-           "dkv_vpart_floats", "dkv_encode_groups", "dkv_storage_unpack", "dkv_alloc_workspace_bytes", "dkv_allocate_rungs",
+           "dkv_vpart_floats", "dkv_encode_groups", "dkv_storage_unpack", "dkv_demote", "dkv_alloc_workspace_bytes", "dkv_allocate_rungs",
            "dkv_version", "dkv_status_string")
 
 
@@ -72,6 +72,16 @@ class EncodeArgs(ctypes.Structure):
         ("coeff", c_void_p), ("coeff_stride", c_int64), ("tokens", c_int32), ("features", c_int32),
         ("rung_planes", c_void_p), ("n_rungs", c_int32), ("codes", c_void_p), ("low", c_void_p), ("span", c_void_p),
         ("rung_error", c_void_p), ("energy", c_void_p), ("status", c_void_p),
+    ]
+
+
+class DemoteArgs(ctypes.Structure):
+    """Mirror of ``dkv_demote_args``."""
+
+    _fields_ = [
+        ("old_code", c_void_p), ("old_code_size", c_uint64), ("old_groups", c_void_p), ("n_old_groups", c_int64),
+        ("new_code", c_void_p), ("new_code_size", c_uint64), ("new_groups", c_void_p), ("old_index", c_void_p),
+        ("n_tokens", c_void_p), ("n_new", c_int64), ("status", c_void_p),
     ]
 
 
@@ -157,7 +167,7 @@ def lib():
         handle.dkv_unpack.restype = c_int32
         for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs),
                          ("dkv_encode_groups", EncodeArgs), ("dkv_storage_unpack", StorageArgs),
-                         ("dkv_allocate_rungs", AllocArgs)):
+                         ("dkv_allocate_rungs", AllocArgs), ("dkv_demote", DemoteArgs)):
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(st), c_void_p]
             fn.restype = c_int32

@@ -692,6 +692,91 @@ class CompressedBatch:
             self._refined_pos[s] = torch.cat([self._refined_pos[s], sel.to(torch.int64).cpu()])
         return fetched
 
+    # ------------------------------------------------------------------ tier management
+    def demote(self, planes: int, tiles: dict | None = None) -> int:
+        """Drop the ``planes`` least significant planes of every token of the given tiles: a token holding
+        m planes of a group keeps max(m - planes, 0) and decodes at that precision (the plane order of
+        scripts/progressive.py:47-55); the dropped planes stay in the cold tier, which ``refine`` reads
+        whole. ``tiles[kind]`` lists tiles of the key / value stream (a stream not named keeps its tiles;
+        ``tiles=None``: every tile of both). The
+        hot tier is rewritten on the device by ``dkv_demote`` into a buffer of the new size, blocks whose
+        tokens keep no plane vanish. Progressive tiles only. Returns the code bytes freed."""
+        if planes < 0:
+            raise ValueError("planes to drop must be >= 0")
+        before = self.keys.code.numel() + self.values.code.numel()
+        changed = False
+        for kind in ("key", "value"):
+            packed = self.keys if kind == "key" else self.values
+            sel = None if tiles is None else tiles.get(kind, [])
+            if packed.n_tiles == 0 or planes == 0 or (sel is not None and len(sel) == 0):
+                continue
+            drop_t = torch.zeros(packed.n_tiles, dtype=torch.int64)
+            if sel is None:
+                drop_t[:] = planes
+            else:
+                sel = torch.as_tensor(sel, dtype=torch.int64).cpu()
+                if bool(((sel < 0) | (sel >= packed.n_tiles)).any()):
+                    raise ValueError(f"{kind} tile index out of range")
+                drop_t[sel] = planes
+            self._demote_stream(packed, drop_t)
+            changed = True
+        if changed:
+            self._rebuild_key_items()
+            self._v_items_cache.clear()
+            self._work = {}
+            self._score_cache = None
+        return before - (self.keys.code.numel() + self.values.code.numel())
+
+    def _demote_stream(self, packed: PackedStream, drop_t: torch.Tensor) -> None:
+        """New layout of one stream after dropping ``drop_t[t]`` planes of tile t, and the copy."""
+        dev = self.device
+        n_blocks = int(packed.groups.shape[0])
+        tb = packed.tile_blocks.to(torch.int64)
+        blk_tile = torch.repeat_interleave(torch.arange(packed.n_tiles), tb).to(dev)
+        drop = drop_t.to(dev)[blk_tile]
+        d32 = packed.groups.view(torch.int32).view(n_blocks, 8).to(torch.int64)
+        kind_b, mp = d32[:, 3] & 0xFF, (d32[:, 3] >> 8) & 0xFF
+        touched = drop > 0
+        if bool((touched & ((kind_b != KIND_PROGRESSIVE) | (mp > 8))).any()):
+            raise ValueError("only progressive tiles (at most 8 planes) can be demoted")
+        n = packed.tiles[:, 2].to(dev, torch.int64)[blk_tile]
+        first = packed.groups[:, 16:32].to(torch.int64)
+        j = torch.arange(16, device=dev)
+        src = j[None, :] + drop[:, None]
+        new_first = torch.where(src < 16, first.gather(1, src.clamp(max=15)), n[:, None])
+        holders = n[:, None] - new_first
+        size = ((holders[:, 0] * 4 + 7) // 8 * 8 + holders.sum(dim=1) * 8 + 15) // 16 * 16
+        kept = torch.nonzero(holders[:, 0] > 0).flatten()
+        sizes = size[kept]
+        offsets = torch.cumsum(sizes, 0) - sizes
+        desc = packed.groups[kept].clone()
+        nd32 = desc.view(torch.int32).view(-1, 8)
+        nd32[:, 1] = offsets.to(torch.int32)
+        nd32[:, 2] = sizes.to(torch.int32)
+        nd32[:, 3] = (kind_b[kept] | ((mp[kept] - drop[kept]).clamp(min=0) << 8)).to(torch.int32)
+        desc[:, 16:32] = new_first[kept].to(torch.uint8)
+        code = torch.zeros(int(sizes.sum()) + 16, dtype=torch.uint8, device=dev)
+        old_index = kept.to(torch.int32)
+        n_tokens = n[kept].to(torch.int32)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        a = _lib.DemoteArgs(packed.code.data_ptr(), packed.code.numel(), packed.groups.data_ptr(), n_blocks,
+                            code.data_ptr(), code.numel(), desc.data_ptr(), old_index.data_ptr(),
+                            n_tokens.data_ptr(), int(kept.numel()), status.data_ptr())
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(self.lib.dkv_demote(a, stream), "dkv_demote")
+        _lib.check_device_status(status)
+        tile_of_kept = blk_tile[kept].cpu()
+        new_tb = torch.zeros(packed.n_tiles, dtype=torch.int64).index_add_(0, tile_of_kept,
+                                                                          torch.ones_like(tile_of_kept))
+        tiles = packed.tiles.clone()
+        tiles[:, 3] = new_tb.to(dev, torch.int32)
+        tiles[:, 4] = (torch.cumsum(new_tb, 0) - new_tb).to(dev, torch.int32)
+        present = torch.zeros_like(packed.present)
+        present[tile_of_kept, d32[kept, 0].cpu()] = True
+        packed.code, packed.groups, packed.tiles = code, desc, tiles
+        packed.present, packed.tile_blocks = present, new_tb
+        packed.max_planes = int(((mp[kept] - drop[kept]).clamp(min=0)).max()) if kept.numel() else 0
+
     # ------------------------------------------------------------------ accounting
     def code_bytes(self) -> int:
         """Bytes held for the compressed tokens (packed plane streams and their descriptors)."""

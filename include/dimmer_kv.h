@@ -301,6 +301,28 @@ typedef struct dkv_storage_args {
 } dkv_storage_args;
 int dkv_storage_unpack(const dkv_storage_args* args, void* stream);
 
+/* Tier management: demote the hot tier by dropping the least significant planes of whole tiles (the
+ * "real cold tier" of the progressive codec: the dropped planes remain in the cold tier, which holds every
+ * plane; scripts/progressive.py:11-19, 47-55 define the plane order). Each new block is copied from its
+ * old block: the headers of the tokens keeping a plane, then per plane j the words of its new holders
+ * (first'[j] = first[j + d] for tiles losing d planes). The caller lays the new blocks out (new_groups:
+ * offsets, sizes, first tables; see dimmerkv.context.CompressedBatch.demote) and zero-fills new_code.
+ * Progressive blocks only (raw and ladder blocks are rejected in the status word). */
+typedef struct dkv_demote_args {
+  const uint8_t* old_code;
+  uint64_t old_code_size;
+  const dkv_group* old_groups;
+  int64_t n_old_groups;
+  uint8_t* new_code;
+  uint64_t new_code_size;
+  const dkv_group* new_groups;   /* [n_new] */
+  const int32_t* old_index;      /* [n_new]: source block of each new block */
+  const int32_t* n_tokens;       /* [n_new]: tokens of the block's tile */
+  int64_t n_new;
+  int* status;
+} dkv_demote_args;
+int dkv_demote(const dkv_demote_args* args, void* stream);
+
 /* The per-token rung allocator of DimmerKV, on the GPU. Replaces kvtc.allocate_rungs (scripts/kvtc.py:
  * 277-298): upgrades valued by error drop per extra byte (made non-increasing along each slot's levels),
  * taken greedily in descending value (ties by flat index) while they fit the budget; counts[slot] = the

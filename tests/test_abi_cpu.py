@@ -40,7 +40,7 @@ def test_struct_mirrors_match_the_header_field_counts():
     text = HEADER.read_text()
     for struct, mirror in (("dkv_attend_args", _lib.AttendArgs), ("dkv_unpack_args", _lib.UnpackArgs),
                            ("dkv_encode_args", _lib.EncodeArgs), ("dkv_storage_args", _lib.StorageArgs),
-                           ("dkv_alloc_args", _lib.AllocArgs)):
+                           ("dkv_alloc_args", _lib.AllocArgs), ("dkv_demote_args", _lib.DemoteArgs)):
         body = re.search(r"typedef struct " + struct + r" \{(.*?)\} " + struct + ";", text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = [f for stmt in body.split(";") if stmt.strip() for f in stmt.split(",")]
