@@ -26,6 +26,20 @@ def _methods(tmp_path, inputs, model):
                    kvtc=kvtc, progressive=prog)
 
 
+def _bin_edge_distance(codec, tensors, kind, start, end, low, span):
+    """Distance (in bins) of every coefficient's float64 quantisation position to the nearest bin edge:
+    (x - low) / span * 256, with x = (matrix - mean) @ basis recomputed in float64."""
+    from dimmerkv.kvtc import rope_tables
+
+    base = codec.base
+    cos, sin = rope_tables(codec._model, tensors[0].shape[2], codec.device)
+    stream = base.streams[kind]
+    x = (base.to_matrix(tensors, kind, cos, sin)[start:end].double() - stream.mean.double()) @ stream.basis.double()
+    grouped = x.view(end - start, -1, base.group)
+    pos = (grouped - torch.from_numpy(low).double()[..., None]) / torch.from_numpy(span).double()[..., None] * 256
+    return (pos - pos.round()).abs().numpy()
+
+
 def test_prog_encode_refine_match_reference(golden, tmp_path, tiny_model):
     inputs, fix = golden("tiny_inputs"), golden("tiny_prog")
     methods = _methods(tmp_path, inputs, tiny_model)
@@ -40,12 +54,16 @@ def test_prog_encode_refine_match_reference(golden, tmp_path, tiny_model):
         flipped = np.zeros(stored.end - stored.start, dtype=bool)
         for kind in ("key", "value"):
             s = stored.stores[kind]
-            # The codes quantise the float32 product (keys - mean) @ basis, whose last bit depends on the
-            # host BLAS's blocking; a coefficient on a bin edge may then land one bin over (quantize8 itself
-            # is pinned bit-exact on fixed coefficients in test_oracle_golden). Allow a few such codes.
+            # The codes quantise the float32 product (keys - mean) @ basis, whose last bits depend on the
+            # host BLAS's blocking and thread split; a coefficient on a bin edge may then land one bin over
+            # (quantize8 itself is pinned bit-exact on fixed coefficients in test_oracle_golden). Every
+            # differing code must be one bin off and come from a coefficient within 0.01 bin of an edge.
             diff = s.codes.numpy().astype(np.int32) - fix[f"codes_{kind}"].astype(np.int32)
-            assert np.abs(diff).max() <= 1 and (diff != 0).sum() <= max(4, diff.size // 10000), \
-                (kind, int((diff != 0).sum()))
+            assert np.abs(diff).max() <= 1, kind
+            if (diff != 0).any():
+                edge = _bin_edge_distance(codec, keys if kind == "key" else values, kind, stored.start, stored.end,
+                                          f16_from_bits(fix[f"low_{kind}"]), f16_from_bits(fix[f"lowspan_{kind}"]))
+                assert edge[diff != 0].max() < 1e-2, (kind, int((diff != 0).sum()), float(edge[diff != 0].max()))
             flipped |= (diff != 0).any(axis=(1, 2))
             assert np.array_equal(s.low.numpy(), f16_from_bits(fix[f"low_{kind}"]))
             assert np.array_equal(s.span.numpy(), f16_from_bits(fix[f"lowspan_{kind}"]))
