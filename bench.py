@@ -488,6 +488,49 @@ def allocate_rate(device, middle: int = 16348, levels: int = 12, launches: int =
             "note": "per call through the Python wrapper (includes its argument checks and status read)"}
 
 
+def demote_rate(batch, device, launches: int = 5) -> dict:
+    """Tier management: CompressedBatch.demote(1) over the whole hot tier (every tile of both streams
+    loses its least significant plane), the batch's own codes. The dkv_demote launch of each stream is timed
+    alone with CUDA events after 3 warm-up launches (each rewrites the same new buffer); algorithmic
+    bytes = the surviving pieces read and written once + old and new descriptors read. The host-side
+    layout (torch ops and the status read) is what remains of the whole call's wall time."""
+    import torch
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    stream = torch.cuda.current_stream(device)
+    runs = []
+
+    def timer(launch, a):
+        for _ in range(3):
+            launch()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(launches + 1)]
+        ev[0].record(stream)
+        for i in range(launches):
+            launch()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(device)
+        ms = statistics.mean(ev[i].elapsed_time(ev[i + 1]) for i in range(launches))
+        runs.append((ms, 2 * (a.new_code_size - 16) + 64 * a.n_new))
+
+    before = batch.keys.code.numel() + batch.values.code.numel()
+    batch.demote_timer = timer
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    freed = batch.demote(1)
+    torch.cuda.synchronize(device)
+    call_s = time.perf_counter() - t0
+    batch.demote_timer = None
+    ms = sum(r[0] for r in runs)
+    nbytes = sum(r[1] for r in runs)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"kernel": "demote (drop one plane of every hot tile)", "code_bytes_before": int(before),
+            "code_bytes_freed": int(freed), "ms": round(ms, 4), "bytes": int(nbytes), "achieved_gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "peak_gbs": peak,
+            "peak_source": "of measured (hbm_gbs)" if peaks else "of fallback",
+            "layout_ms": round(call_s * 1e3 - (3 + launches) * ms, 2)}
+
+
 def run_kernels(args, cfg, device) -> dict:
     """Profiling case: every layer's dkv_attend_layer over the packed codes, random queries, no model."""
     import torch
@@ -529,7 +572,7 @@ def run_kernels(args, cfg, device) -> dict:
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
             "gpu_launches": len(timer.events) * KERNELS_PER_LAYER, "unpack": unpack_rate(batch, device),
             "encode": encode_rate(device), "storage": storage_rate(device),
-            "allocate": allocate_rate(device)}
+            "allocate": allocate_rate(device), "demote": demote_rate(batch, device)}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
@@ -792,6 +835,7 @@ def run_ours(args, cfg, rank, world, device):
     encode = encode_rate(device) if rank == 0 else None
     storage = storage_rate(device) if rank == 0 else None
     allocate = allocate_rate(device) if rank == 0 else None
+    demote = demote_rate(batch, device) if rank == 0 else None  # last: it rewrites the batch's hot tier
 
     result = None
     if rank == 0:
@@ -815,6 +859,7 @@ def run_ours(args, cfg, rank, world, device):
             "encode": encode,
             "storage": storage,
             "allocate": allocate,
+            "demote": demote,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }

@@ -18,11 +18,12 @@ namespace dkv {
 
 namespace {
 constexpr int kDemoteThreads = 128;
+static_assert(kDemoteThreads >= kTileTokens, "one thread per token slot of a tile");
 
 __device__ __forceinline__ uint32_t first_of(const GroupDesc& g, int j) { return g.first[j]; }
 }  // namespace
 
-__global__ void __launch_bounds__(kDemoteThreads) demote_kernel(const DemoteParams p) {
+__global__ void __launch_bounds__(kDemoteThreads, 8) demote_kernel(const DemoteParams p) {
   const int64_t i = blockIdx.x;
   const int oi = p.old_index[i];
   const int n = p.n_tokens[i];
@@ -51,26 +52,31 @@ __global__ void __launch_bounds__(kDemoteThreads) demote_kernel(const DemotePara
     if (threadIdx.x == 0) record_error(p.status, kErrBadDescriptor);
     return;
   }
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(p.old_code + od.code_offset);
-  uint32_t* dst = reinterpret_cast<uint32_t*>(p.new_code + nd.code_offset);
-  // Headers of the tokens that keep at least one plane.
-  {
-    const uint32_t skip = first_of(nd, 0) - first_of(od, 0);
-    const uint32_t words = n - first_of(nd, 0);
-    for (uint32_t w = threadIdx.x; w < words; w += blockDim.x) dst[w] = src[skip + w];
-  }
-  // Plane j: the 64-bit words of its new holders (plane segments start on 8-byte boundaries).
-  const uint64_t* src64 = reinterpret_cast<const uint64_t*>(src);
-  uint64_t* dst64 = reinterpret_cast<uint64_t*>(dst);
+  // Thread t owns token slot t of the new block's header segment and of every plane segment: all its
+  // loads are issued before any store, so each thread keeps up to 17 independent loads in flight.
+  const uint32_t t = threadIdx.x;
+  const uint32_t* __restrict__ src = reinterpret_cast<const uint32_t*>(p.old_code + od.code_offset);
+  uint32_t* __restrict__ dst = reinterpret_cast<uint32_t*>(p.new_code + nd.code_offset);
+  const uint64_t* __restrict__ src64 = reinterpret_cast<const uint64_t*>(src);
+  uint64_t* __restrict__ dst64 = reinterpret_cast<uint64_t*>(dst);
+  const uint32_t nf0 = first_of(nd, 0);
+  const bool has_hdr = t + nf0 < static_cast<uint32_t>(n);
+  uint32_t hdr = 0u;
+  if (has_hdr) hdr = __ldg(src + (nf0 - first_of(od, 0)) + t);  // headers of the tokens keeping a plane
+  uint64_t word[16];
+#pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const uint32_t old_holders = n - first_of(od, j), new_holders = n - first_of(nd, j);
-    if (new_holders > 0) {
-      const uint64_t* s = src64 + old_seg / 8 + (first_of(nd, j) - first_of(od, j));
-      uint64_t* d = dst64 + new_seg / 8;
-      for (uint32_t w = threadIdx.x; w < new_holders; w += blockDim.x) d[w] = s[w];
-    }
-    old_seg += old_holders * 8u;
-    new_seg += new_holders * 8u;
+    const uint32_t ofj = first_of(od, j), nfj = first_of(nd, j);
+    if (t + nfj < static_cast<uint32_t>(n)) word[j] = __ldg(src64 + old_seg / 8 + (nfj - ofj) + t);
+    old_seg += (n - ofj) * 8u;
+  }
+  if (has_hdr) dst[t] = hdr;
+  uint32_t at = new_seg / 8 + t;  // slot t's word in plane j of the new block
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t nfj = first_of(nd, j);
+    if (t + nfj < static_cast<uint32_t>(n)) dst64[at] = word[j];
+    at += n - nfj;
   }
 }
 

@@ -203,6 +203,7 @@ class CompressedBatch:
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.timer = None  # optional callable(kind, fn) wrapping launches (used by the bench)
+        self.demote_timer = None  # optional callable(launch, args) wrapping the dkv_demote launch
         self.scoring = False
         self.imp_compressed = None
         self.imp_exact = None
@@ -763,7 +764,14 @@ class CompressedBatch:
                             code.data_ptr(), code.numel(), desc.data_ptr(), old_index.data_ptr(),
                             n_tokens.data_ptr(), int(kept.numel()), status.data_ptr())
         stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(self.lib.dkv_demote(a, stream), "dkv_demote")
+
+        def launch():
+            _lib.check(self.lib.dkv_demote(a, stream), "dkv_demote")
+
+        if self.demote_timer is not None:
+            self.demote_timer(launch, a)  # launches the copy itself (repeating it rewrites the same bytes)
+        else:
+            launch()
         _lib.check_device_status(status)
         tile_of_kept = blk_tile[kept].cpu()
         new_tb = torch.zeros(packed.n_tiles, dtype=torch.int64).index_add_(0, tile_of_kept,
