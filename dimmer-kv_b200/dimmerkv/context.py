@@ -139,6 +139,37 @@ def lpt_schedule(costs: list, n_cta: int) -> tuple[torch.Tensor, torch.Tensor]:
     return torch.tensor(begin, dtype=torch.int32), torch.tensor(flat, dtype=torch.int32)
 
 
+def pair_work_lists(present: torch.Tensor, group_base: torch.Tensor, ranges: list) -> tuple[torch.Tensor, torch.Tensor]:
+    """Work lists of the paired key kernel. ``present`` bool [n_tiles, Gu]: blocks held per (tile, union
+    group); ``group_base`` int64 [n_tiles]: first descriptor of each tile; ``ranges[s]``: the (first, end)
+    tile ranges of conversation s. Neighbouring tiles of a range form a pair (t0, t1; t1 = -1 for an odd
+    last tile). Returns (pairs int32 [n_pairs, 4] = (t0, t1, groups, first entry), entries int32 [n, 4] =
+    (union group, descriptor of t0 or -1, descriptor of t1 or -1, 0)): per pair, every group either tile
+    holds, ascending. With no pair: one row (-1, -1, 0, 0) and one zero entry."""
+    pairs = [(t, t + 1 if t + 1 < t1 else -1) for seq_ranges in ranges for t0, t1 in seq_ranges
+             for t in range(t0, t1, 2)]
+    if not pairs:
+        return torch.tensor([(-1, -1, 0, 0)], dtype=torch.int32), torch.zeros(1, 4, dtype=torch.int32)
+    pr = torch.tensor(pairs, dtype=torch.int64)
+    t0, t1 = pr[:, 0], pr[:, 1]
+    t1c = t1.clamp(min=0)
+    p0 = present[t0]
+    p1 = present[t1c] & (t1 >= 0)[:, None]
+    either = p0 | p1
+    prefix = torch.zeros(present.shape[0], present.shape[1] + 1, dtype=torch.int64)
+    prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
+    pi, groups = torch.nonzero(either, as_tuple=True)  # by pair, then ascending group
+    none = torch.full_like(groups, -1)
+    d0 = torch.where(p0[pi, groups], group_base[t0[pi]] + prefix[t0[pi], groups], none)
+    d1 = torch.where(p1[pi, groups], group_base[t1c[pi]] + prefix[t1c[pi], groups], none)
+    counts = either.sum(dim=1)
+    rows = torch.stack([t0, t1, counts, torch.cumsum(counts, 0) - counts], dim=1).to(torch.int32)
+    entries = torch.stack([groups, d0, d1, torch.zeros_like(groups)], dim=1).to(torch.int32)
+    if entries.shape[0] == 0:
+        entries = torch.zeros(1, 4, dtype=torch.int32)
+    return rows, entries
+
+
 class CompressedBatch:
     """Compressed middle tokens of a batch of conversations (one row of the HF batch each)."""
 
@@ -224,30 +255,10 @@ class CompressedBatch:
             ranges = [[(t0, t1)] for t0, t1 in self.keys.seq_tiles]
             for s, t0, t1 in getattr(self, "_refined_key_tiles", []):
                 ranges[s].append((t0, t1))
-            pairs = []
-            for seq_ranges in ranges:
-                for t0, t1 in seq_ranges:
-                    for t in range(t0, t1, 2):
-                        pairs.append((t, t + 1 if t + 1 < t1 else -1))
             nblocks = self.n_cols // 512
-            present = self.keys.present
-            gb = self.keys.tiles[:, 4].to(torch.int64).cpu()
-            prefix = torch.zeros(present.shape[0], present.shape[1] + 1, dtype=torch.int64)
-            prefix[:, 1:] = present.to(torch.int64).cumsum(dim=1)
-            rows, entries, n_entries = [], [], 0
-            for t0, t1 in pairs:
-                p0 = present[t0]
-                p1 = present[t1] if t1 >= 0 else torch.zeros_like(p0)
-                groups = torch.nonzero(p0 | p1).flatten()
-                d0 = torch.where(p0[groups], gb[t0] + prefix[t0, groups], torch.full_like(groups, -1))
-                d1 = torch.where(p1[groups], gb[max(t1, 0)] + prefix[max(t1, 0), groups], torch.full_like(groups, -1))
-                rows.append((t0, t1, int(groups.numel()), n_entries))
-                n_entries += int(groups.numel())
-                entries.append(torch.stack([groups, d0, d1, torch.zeros_like(groups)], dim=1))
-            pair_t = torch.tensor(rows if rows else [(-1, -1, 0, 0)], dtype=torch.int32)
-            entry_t = torch.cat(entries).to(torch.int32) if entries else torch.zeros(1, 4, dtype=torch.int32)
+            pair_t, entry_t = pair_work_lists(self.keys.present, self.keys.tiles[:, 4].to(torch.int64).cpu(), ranges)
             self.k_pair_groups = entry_t.contiguous().to(self.device)
-            if rows:
+            if int(pair_t[0, 0]) >= 0:
                 cost = (pair_t[:, 2].to(torch.float64) + 4.0).repeat_interleave(nblocks)
             else:
                 cost = torch.zeros(0, dtype=torch.float64)
