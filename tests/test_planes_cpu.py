@@ -94,3 +94,42 @@ def test_pack_rejects_unsorted_tokens():
                     torch.zeros(2, dtype=torch.int32))
     with pytest.raises(ValueError):
         pack_streams([s])
+
+
+def _pair_lists_by_loop(present, group_base, ranges):
+    """The paired key kernel's work lists, one pair at a time (the layout the kernel reads)."""
+    prefix = np.zeros((present.shape[0], present.shape[1] + 1), dtype=np.int64)
+    prefix[:, 1:] = np.cumsum(present, axis=1)
+    rows, entries = [], []
+    for seq_ranges in ranges:
+        for t0, t1 in seq_ranges:
+            for t in range(t0, t1, 2):
+                u = t + 1 if t + 1 < t1 else -1
+                first_entry = len(entries)
+                for g in range(present.shape[1]):
+                    h0, h1 = bool(present[t, g]), u >= 0 and bool(present[u, g])
+                    if h0 or h1:
+                        entries.append((g, group_base[t] + prefix[t, g] if h0 else -1,
+                                        group_base[u] + prefix[u, g] if h1 else -1, 0))
+                rows.append((t, u, len(entries) - first_entry, first_entry))
+    if not rows:
+        rows = [(-1, -1, 0, 0)]
+    if not entries:
+        entries = [(0, 0, 0, 0)]
+    return np.array(rows, dtype=np.int32), np.array(entries, dtype=np.int32)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_pair_work_lists_match_pair_by_pair_layout(seed):
+    from dimmerkv.context import pair_work_lists
+
+    rng = np.random.default_rng(seed)
+    n_tiles, n_groups = int(rng.integers(1, 40)), int(rng.integers(1, 12))
+    present = rng.random((n_tiles, n_groups)) < rng.random()
+    group_base = rng.integers(0, 1000, n_tiles)
+    cuts = np.sort(rng.choice(np.arange(n_tiles + 1), size=min(n_tiles + 1, 5), replace=False))
+    ranges = [[(int(a), int(b))] for a, b in zip(cuts[:-1], cuts[1:])] if seed else []
+    rows, entries = pair_work_lists(torch.from_numpy(present), torch.from_numpy(group_base), ranges)
+    want_rows, want_entries = _pair_lists_by_loop(present, group_base, ranges)
+    assert np.array_equal(rows.numpy(), want_rows)
+    assert np.array_equal(entries.numpy(), want_entries)
