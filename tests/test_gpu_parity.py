@@ -202,24 +202,22 @@ def test_ragged_batch_matches_oracle_per_conversation():
             assert err < TOL_F32, (layer, s, err)
 
 
-@pytest.mark.parametrize("q", [1, 4])
-def test_ragged_batch_3b_geometry_matches_oracle(q):
-    """The bench's attention geometry (Llama-3.2-3B: 8 KV heads of 128, 24 query heads, GQA 3) on four
-    ragged conversations in one launch, up to 2100 middle tokens (an odd number of tiles, so one CTA pair
-    holds a single tile) and 16 coefficient groups, q query rows, each conversation against the oracle."""
-    rng = np.random.default_rng(11 + q)
+def _check_3b_geometry(shapes, q, seed):
+    """Conversations of the given (middle tokens, groups) at the bench's attention geometry (Llama-3.2-3B:
+    8 KV heads of 128, 24 query heads, GQA 3), one launch per layer, q query rows, each conversation
+    against the oracle."""
+    rng = np.random.default_rng(seed)
     L, H, D, HQ = 2, 8, 128, 24
     F = L * H * D
-    g = torch.Generator().manual_seed(17 + q)
+    g = torch.Generator().manual_seed(seed + 6)
     basis = {k: torch.linalg.qr(torch.randn(F, F, generator=g, dtype=torch.float64))[0].float() for k in ("key", "value")}
     mean = {k: torch.randn(F, generator=g) * 0.1 for k in ("key", "value")}
-    T = 2300
+    T = max(n for n, _ in shapes) + 200
     pos = torch.arange(T, dtype=torch.float32)
     inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
     cos_full = torch.cat([torch.cos(pos[:, None] * inv), torch.cos(pos[:, None] * inv)], dim=1)
     sin_full = torch.cat([torch.sin(pos[:, None] * inv), torch.sin(pos[:, None] * inv)], dim=1)
     convs, raw = [], []
-    shapes = ((2100, 16), (130, 3), (1000, 9), (257, 1))
     for n_mid, groups in shapes:
         c = _random_conv(rng, n_mid, groups, 4)
         toks = {}
@@ -252,3 +250,17 @@ def test_ragged_batch_3b_geometry_matches_oracle(q):
             assert out[s : s + 1].shape == want.shape
             err = np.abs(out[s : s + 1] - want).max()
             assert err < TOL_F32, (layer, s, err)
+
+
+@pytest.mark.parametrize("q", [1, 4])
+def test_ragged_batch_3b_geometry_matches_oracle(q):
+    """Four ragged conversations in one launch: up to 2100 middle tokens (an odd number of tiles, so one
+    CTA pair holds a single tile) and 16 coefficient groups."""
+    _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), q, 11 + q)
+
+
+@pytest.mark.parametrize("q", [1, 4])
+def test_long_conversation_3b_geometry_matches_oracle(q):
+    """One conversation of 16380 middle tokens: with 24 (q = 1) or 96 (q = 4) query rows the softmax
+    statistics cut each row's scores into slices scanned by separate CTAs and merged in slice order."""
+    _check_3b_geometry(((16380, 16),), q, 31 + q)
