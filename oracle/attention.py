@@ -70,7 +70,8 @@ class OracleContext:
             dec = np.asarray(decoded[kind], dtype=np.float32)
             union = np.nonzero((dec[kept] != 0).any(axis=0))[0]  # :53
             self.basis[kind] = round_dtype(np.asarray(basis[kind], dtype=np.float32)[:, union].T, dtype).astype(
-                f).reshape(len(union), layers, -1)  # :54
+                f).reshape(len(union), layers, heads * head_dim)  # :54 (the axis named: an empty union, every
+            # middle token without a plane, leaves keys and values at the mean where the reference's -1 raises)
             self.mean[kind] = round_dtype(np.asarray(mean[kind], dtype=np.float32), dtype).astype(
                 f).reshape(layers, -1)  # :45
             self.coeff[kind] = round_dtype(dec[:, union], dtype).astype(f)  # :76 (per block)

@@ -264,3 +264,58 @@ def test_long_conversation_3b_geometry_matches_oracle(q):
     """One conversation of 16380 middle tokens: with 24 (q = 1) or 96 (q = 4) query rows the softmax
     statistics cut each row's scores into slices scanned by separate CTAs and merged in slice order."""
     _check_3b_geometry(((16380, 16),), q, 31 + q)
+
+
+def test_edge_conversations_match_oracle():
+    """One launch over the edge cases of a ragged batch: a single middle token, exactly one tile, one tile
+    plus one token, and a conversation whose tokens hold no plane in either stream (keys and values are the
+    mean alone), beside an ordinary one; each against the oracle."""
+    rng = np.random.default_rng(23)
+    L, H, D, HQ = 2, 8, 64, 32
+    F = L * H * D
+    g = torch.Generator().manual_seed(29)
+    basis = {k: torch.linalg.qr(torch.randn(F, F, generator=g, dtype=torch.float64))[0].float() for k in ("key", "value")}
+    mean = {k: torch.randn(F, generator=g) * 0.1 for k in ("key", "value")}
+    T = 700
+    pos = torch.arange(T, dtype=torch.float32)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    cos_full = torch.cat([torch.cos(pos[:, None] * inv), torch.cos(pos[:, None] * inv)], dim=1)
+    sin_full = torch.cat([torch.sin(pos[:, None] * inv), torch.sin(pos[:, None] * inv)], dim=1)
+    shapes = ((1, 1, None), (128, 2, None), (129, 5, None), (300, 4, 0), (500, 7, None))
+    convs, raw = [], []
+    for n_mid, groups, fixed in shapes:
+        c = _random_conv(rng, n_mid, groups, 4)
+        if fixed is not None:
+            for kind in ("key", "value"):
+                codes, low, span, planes, m = c[kind]
+                planes[:, :groups] = fixed
+                c[kind] = (codes, low, span, planes, np.full_like(m, fixed))
+        toks = {}
+        for kind in ("key", "value"):
+            codes, low, span, planes, m = c[kind]
+            toks[kind] = _to(from_progressive(torch.from_numpy(codes), torch.from_numpy(low), torch.from_numpy(span),
+                                              torch.from_numpy(planes), torch.from_numpy(m.astype(np.int64))))
+        convs.append(ConversationCodes(4, 4 + n_mid, toks["key"], toks["value"]))
+        raw.append(c)
+    batch = CompressedBatch(convs, layers=L, kv_heads=H, head_dim=D, q_heads=HQ, basis=basis, mean=mean,
+                            cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV)
+    S, E = len(shapes), 40
+    query = torch.randn(S, HQ, 1, D, generator=g).to(torch.bfloat16)
+    ek = torch.randn(S, H, E, D, generator=g).to(torch.bfloat16)
+    ev = torch.randn(S, H, E, D, generator=g).to(torch.bfloat16)
+    for layer in range(L):
+        out = batch.attend_layer(layer, query.to(DEV), ek.to(DEV), ev.to(DEV), None, D ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        batch.check_status()
+        out = out.cpu().numpy()
+        for s, (conv, c) in enumerate(zip(convs, raw)):
+            decoded = {kind: oc.dequantize(c[kind][0], c[kind][1], c[kind][2], c[kind][3]) for kind in ("key", "value")}
+            ctx = OracleContext(start=conv.start, end=conv.end, layers=L, heads=H, head_dim=D,
+                                choice={k: c[k][4] for k in ("key", "value")}, decoded=decoded,
+                                basis={k: v.numpy() for k, v in basis.items()},
+                                mean={k: v.numpy() for k, v in mean.items()},
+                                cos=cos_full.numpy(), sin=sin_full.numpy(), dtype="bf16")
+            want = ctx.attend(layer, query[s : s + 1].float().numpy(), ek[s : s + 1].float().numpy(),
+                              ev[s : s + 1].float().numpy(), None, D ** -0.5)
+            err = np.abs(out[s : s + 1] - want).max()
+            assert np.isfinite(err) and err < TOL_F32, (layer, shapes[s], err)
