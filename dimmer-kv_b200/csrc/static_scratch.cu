@@ -31,7 +31,12 @@ __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 std::mutex g_static_mutex;
 void* g_static_addr[kMaxDevices] = {};
 
-size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// Sizes saturate at kSizeCap, one byte more than the array: an overflowing product or sum reads as a
+// request that does not fit instead of wrapping to a small size.
+constexpr size_t kSizeCap = kStaticScratchBytes + 1;
+size_t sat_mul(size_t a, size_t b) { return (a != 0 && b > kSizeCap / a) ? kSizeCap : (a * b < kSizeCap ? a * b : kSizeCap); }
+size_t sat_add(size_t a, size_t b) { return a + b < kSizeCap ? a + b : kSizeCap; }
+size_t align256(size_t x) { return x >= kSizeCap ? kSizeCap : ((x + 255) & ~size_t(255)); }
 
 // Device address of the array on the current device (looked up once per device).
 int static_scratch_address(void** out) {
@@ -50,19 +55,28 @@ int static_scratch_address(void** out) {
 }  // namespace
 
 extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_scores, void* stream) {
-  if (args == nullptr || n_scores < 0 || args->n_seq < 0 || args->q_len < 1 || args->n_exact < 0 ||
-      args->n_v_items < 0 || args->rows_pad < 0 || args->v_item_groups < 0)
+  if (args == nullptr || n_scores < 0 || args->n_seq < 0 || args->n_q_heads < 1 || args->q_len < 1 ||
+      args->n_exact < 0 || args->n_v_items < 0 || args->rows_pad < 0 || args->v_item_groups < 0)
     return DKV_ERR_ARGS;
-  const size_t rows = static_cast<size_t>(args->n_seq) * args->n_q_heads * args->q_len;
-  const size_t scores_bytes = align256(static_cast<size_t>(n_scores) * sizeof(float));
-  const size_t stats_bytes = align256(rows * 4 * sizeof(float));
-  const size_t exact_bytes = align256(rows * static_cast<size_t>(args->n_exact) * sizeof(float));
-  const size_t partial_bytes = align256(static_cast<size_t>(args->n_v_items) * args->rows_pad *
-                                        args->v_item_groups * 64 * sizeof(float));
-  const int64_t vpart_floats = dkv_vpart_floats(args->v_width, args->n_seq, args->rows_pad, args->head_dim);
-  if (vpart_floats < 0) return DKV_ERR_ARGS;
-  const size_t vpart_bytes = align256(static_cast<size_t>(vpart_floats) * sizeof(float));
-  const size_t total = scores_bytes + stats_bytes + exact_bytes + partial_bytes + vpart_bytes;
+  const size_t rows = sat_mul(sat_mul(static_cast<size_t>(args->n_seq), static_cast<size_t>(args->n_q_heads)),
+                              static_cast<size_t>(args->q_len));
+  const size_t scores_bytes = align256(sat_mul(static_cast<size_t>(n_scores), sizeof(float)));
+  const size_t stats_bytes = align256(sat_mul(rows, 4 * sizeof(float)));
+  const size_t exact_bytes = align256(sat_mul(sat_mul(rows, static_cast<size_t>(args->n_exact)), sizeof(float)));
+  const size_t partial_bytes = align256(sat_mul(sat_mul(sat_mul(static_cast<size_t>(args->n_v_items),
+                                                                static_cast<size_t>(args->rows_pad)),
+                                                        static_cast<size_t>(args->v_item_groups)),
+                                                64 * sizeof(float)));
+  // dkv_vpart_floats is a product of its arguments: take its per-(conversation, row, component) factor and
+  // multiply the rest here with saturation.
+  const int64_t vpart_chunks = dkv_vpart_floats(args->v_width, 1, 1, 1);
+  if (vpart_chunks < 0 || args->head_dim < 0) return DKV_ERR_ARGS;
+  const size_t vpart_floats = sat_mul(sat_mul(sat_mul(static_cast<size_t>(vpart_chunks), static_cast<size_t>(args->n_seq)),
+                                              static_cast<size_t>(args->rows_pad)),
+                                      static_cast<size_t>(args->head_dim));
+  const size_t vpart_bytes = align256(sat_mul(vpart_floats, sizeof(float)));
+  const size_t total =
+      sat_add(sat_add(sat_add(sat_add(scores_bytes, stats_bytes), exact_bytes), partial_bytes), vpart_bytes);
   if (total > kStaticScratchBytes) return DKV_ERR_SCRATCH;
   void* base = nullptr;
   const int rc = static_scratch_address(&base);

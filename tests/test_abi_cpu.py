@@ -45,3 +45,25 @@ def test_struct_mirrors_match_the_header_field_counts():
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = [f for stmt in body.split(";") if stmt.strip() for f in stmt.split(",")]
         assert len(fields) == len(mirror._fields_), (struct, len(fields), len(mirror._fields_))
+
+
+@pytest.mark.skipif(not _lib.LIB_PATH.exists(), reason="library not built (dimmer-kv_b200/build_lib.py)")
+def test_static_scratch_entry_rejects_oversized_requests_on_the_host():
+    """dkv_attend_layer_static sizes its scratch on the host before any CUDA call: requests larger than its
+    fixed 32 MiB array come back as DKV_ERR_SCRATCH, including ones whose byte counts overflow 64 bits
+    (2^62 scores are 2^64 bytes, which would wrap to 0), and negative sizes as DKV_ERR_ARGS."""
+    lib = _lib.lib()
+    fn = lib.dkv_attend_layer_static
+    fn.argtypes = [ctypes.POINTER(_lib.AttendArgs), ctypes.c_int64, ctypes.c_void_p]
+    fn.restype = ctypes.c_int32
+    a = _lib.AttendArgs()
+    a.n_seq, a.n_q_heads, a.q_len, a.head_dim, a.v_width, a.rows_pad = 1, 24, 1, 128, 3072, 32
+    a.n_exact, a.n_v_items, a.v_item_groups = 36, 4, 16
+    assert fn(ctypes.byref(a), 1 << 40, None) == 5
+    assert fn(ctypes.byref(a), 1 << 62, None) == 5
+    big = _lib.AttendArgs()
+    big.n_seq, big.n_q_heads, big.q_len, big.head_dim, big.v_width, big.rows_pad = (1 << 30), (1 << 30), (1 << 30), 128, 3072, 32
+    big.n_exact, big.n_v_items, big.v_item_groups = (1 << 30), (1 << 30), (1 << 30)
+    assert fn(ctypes.byref(big), 0, None) == 5
+    assert fn(ctypes.byref(a), -1, None) == 1
+    assert lib.dkv_status_string(5) != b""
