@@ -74,7 +74,8 @@ int sm_count() {
 
 int check_common(const dkv_attend_args* a) {
   if (a == nullptr) return DKV_ERR_ARGS;
-  if (a->n_seq < 0 || a->q_len < 1 || a->n_kv_heads < 1 || a->n_q_heads % a->n_kv_heads != 0) return DKV_ERR_ARGS;
+  if (a->n_seq < 0 || a->q_len < 1 || a->n_kv_heads < 1 || a->n_q_heads < 1 || a->n_q_heads % a->n_kv_heads != 0)
+    return DKV_ERR_ARGS;
   if (a->layer < 0 || a->layer >= a->n_layers) return DKV_ERR_ARGS;
   if (a->head_dim != 64 && a->head_dim != 128) return DKV_ERR_CONFIG;
   return DKV_OK;

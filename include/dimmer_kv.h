@@ -307,7 +307,9 @@ int dkv_storage_unpack(const dkv_storage_args* args, void* stream);
  * old block: the headers of the tokens keeping a plane, then per plane j the words of its new holders
  * (first'[j] = first[j + d] for tiles losing d planes). The caller lays the new blocks out (new_groups:
  * offsets, sizes, first tables; see dimmerkv.context.CompressedBatch.demote) and zero-fills new_code.
- * Progressive blocks only (raw and ladder blocks are rejected in the status word). */
+ * Progressive blocks only (raw and ladder blocks are rejected in the status word). Both code buffers and
+ * both descriptor arrays must be 16-byte aligned, old_index and n_tokens 4-byte aligned (DKV_ERR_ARGS
+ * otherwise). */
 typedef struct dkv_demote_args {
   const uint8_t* old_code;
   uint64_t old_code_size;
