@@ -284,8 +284,8 @@ def main() -> None:
         fixture["refined_keys"] = np.stack([bits16(k[0][:, rows]) for k in ref_keys])
         fixture["refined_values"] = np.stack([bits16(v[0][:, rows]) for v in ref_values])
         fixture["hot_keys_rows"] = np.stack([bits16(k[0][:, rows]) for k in hot_keys])
-        # Direct attention over the hot progressive codes: a codec shim exposing what
-        # CompressedContext reads (compressed_attention.py:36-54), as in the survey probes.
+        # Direct attention over the hot progressive codes: a codec shim exposing the fields that
+        # CompressedContext reads (compressed_attention.py:36-54).
         shim = types.SimpleNamespace(layers=layers, heads=heads, head_dim=dim, device=torch.device("cpu"),
                                      last_span=(stored.start, stored.end), streams={}, last_choice={},
                                      last_coefficients={})
