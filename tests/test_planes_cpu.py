@@ -133,3 +133,25 @@ def test_pair_work_lists_match_pair_by_pair_layout(seed):
     want_rows, want_entries = _pair_lists_by_loop(present, group_base, ranges)
     assert np.array_equal(rows.numpy(), want_rows)
     assert np.array_equal(entries.numpy(), want_entries)
+
+
+@pytest.mark.parametrize("n_items,n_cta", [(0, 148), (1, 148), (7, 3), (1000, 148), (300, 74)])
+def test_lpt_schedule_covers_every_item_once_heaviest_first(n_items, n_cta):
+    from dimmerkv.context import lpt_schedule
+
+    rng = np.random.default_rng(n_items + n_cta)
+    costs = (rng.pareto(1.5, n_items) * 10 + 1).tolist()
+    begin, order = lpt_schedule(costs, n_cta)
+    begin, order = begin.numpy(), order.numpy()
+    grid = len(begin) - 1
+    assert grid == max(1, min(n_cta, n_items))
+    assert begin[0] == 0 and begin[-1] == n_items and np.all(np.diff(begin) >= 0)
+    assert sorted(order.tolist()) == list(range(n_items))
+    loads = []
+    for b in range(grid):
+        mine = [costs[i] for i in order[begin[b] : begin[b + 1]]]
+        assert mine == sorted(mine, reverse=True)
+        loads.append(sum(mine))
+    if n_items:
+        # Greedy list scheduling: no CTA ends more than one item above the average load.
+        assert max(loads) <= sum(costs) / grid + max(costs) + 1e-9
