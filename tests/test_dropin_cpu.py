@@ -105,3 +105,17 @@ def test_out_of_path_methods_raise(golden, tmp_path, tiny_model):
         methods.apply("pca16/lex8", [], [], {})
     with pytest.raises(NotImplementedError):
         methods.codec("lex")
+
+
+def test_refine_count_formula():
+    """max(1, int(round(fraction * middle))) as scripts/methods.py:246 computes it, with Python's
+    round-half-to-even on exact halves."""
+    from dimmerkv.question import refine_count
+
+    assert refine_count(0.01, 32732) == 327  # cfg4: 32768 tokens minus 36 exact
+    assert refine_count(0.05, 604) == 30
+    assert refine_count(0.01, 10) == 1       # never fewer than one token
+    assert refine_count(0.5, 5) == 2         # 2.5 rounds to even
+    assert refine_count(0.5, 7) == 4         # 3.5 rounds to even
+    for fraction, middle in ((0.01, 1500), (0.02, 8156), (0.03, 16348), (0.25, 6)):
+        assert refine_count(fraction, middle) == max(1, int(round(fraction * middle)))

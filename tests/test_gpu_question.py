@@ -252,8 +252,3 @@ def test_refine_top_two_conversations(golden):
     assert fetched > 0
     with pytest.raises(ValueError):
         batch.refine([selected[0][:1], torch.zeros(0, dtype=torch.int64)], [cold1, cold1])  # already refined
-
-
-def test_refine_count_formula():
-    assert refine_count(0.01, 32732) == 327
-    assert refine_count(0.05, 604) == 30
