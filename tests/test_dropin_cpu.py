@@ -119,3 +119,26 @@ def test_refine_count_formula():
     assert refine_count(0.5, 7) == 4         # 3.5 rounds to even
     for fraction, middle in ((0.01, 1500), (0.02, 8156), (0.03, 16348), (0.25, 6)):
         assert refine_count(fraction, middle) == max(1, int(round(fraction * middle)))
+
+
+@pytest.mark.parametrize("tokens,features,budget,want", [
+    (1536, 16 * 8 * 64, 0.03, (4, 4)),         # configs[0]: 1B, 1536 tokens, 3%
+    (4096, 28 * 8 * 128, 0.03, (46, 50)),      # configs[2]: 3B, shortest conversation
+    (16384, 28 * 8 * 128, 0.03, (61, 65)),     # configs[2]: 3B, longest conversation
+    (131072, 28 * 8 * 128, 0.02, (44, 46)),    # configs[4]: 3B, 131K tokens, 2%
+])
+def test_bench_group_count_is_the_largest_that_fits_the_budget(tokens, features, budget, want):
+    """The bench's hot groups G: the largest count whose bytes (8 per plane and 4 per header per token and
+    group, 1 rung byte per token and stream) fit budget * T * 2 * exact_bytes minus the 36 exact tokens
+    (scripts/progressive.py:32-34, 141-142), for plane counts drawn as the workload specifies."""
+    from dimmerkv.synthetic import budget_groups, draw_planes
+
+    g = torch.Generator().manual_seed(0)
+    middle = tokens - 36
+    mk, mv = draw_planes(middle, g), draw_planes(middle, g)
+    G = budget_groups(tokens, features, budget, mk, mv, 10 ** 6)
+    assert want[0] <= G <= want[1]
+    exact_bytes = features * 2
+    remaining = int(budget * tokens * 2 * exact_bytes) - 36 * 2 * exact_bytes - 2 * middle
+    per_group = int((8 * mk + 4 * (mk > 0)).sum() + (8 * mv + 4 * (mv > 0)).sum())
+    assert G * per_group <= remaining < (G + 1) * per_group
