@@ -128,11 +128,88 @@ def storage_fixture(out: Path, methods, keys, values, scores) -> None:
     np.savez_compressed(out / "storage.npz", **fixture)
 
 
+GEOMETRY_3B = dict(tm.TINY, hidden_size=768, num_attention_heads=24, head_dim=128)  # Llama-3.2-3B heads, tiny model
+GEOMETRY_3B_TOKENS, GEOMETRY_3B_GROUPS, GEOMETRY_3B_BASIS_SEED = 230, 6, 500
+
+
+def geometry3b_fixture(out: Path) -> None:
+    """The reference's CompressedContext (_keys, attend) at the Llama-3.2-3B head geometry (8 KV heads of
+    128, 24 query heads, GQA 3) on a 2-layer random-init model, over synthetic progressive codes
+    (quantize8 of seeded coefficients, per-token plane counts {0,1,2,4,6,8} on the first groups) fed
+    through a codec shim; fp32 and bf16 runs at q = 1 and 4. The bases are rebuilt from their seed by
+    the tests (tinymodel.seeded_basis)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(4321)
+    model = LlamaForCausalLM(LlamaConfig(**GEOMETRY_3B)).float().eval()
+    layers, heads, dim = GEOMETRY_3B["num_hidden_layers"], GEOMETRY_3B["num_key_value_heads"], GEOMETRY_3B["head_dim"]
+    q_heads = GEOMETRY_3B["num_attention_heads"]
+    features, tokens, used = layers * heads * dim, GEOMETRY_3B_TOKENS, GEOMETRY_3B_GROUPS
+    start, end = tm.SINKS, tokens - tm.RECENT
+    middle = end - start
+    g = torch.Generator().manual_seed(77)
+    fixture = {"span": np.array([start, end]), "tokens": tokens, "groups_used": used}
+    shim = types.SimpleNamespace(layers=layers, heads=heads, head_dim=dim, device=torch.device("cpu"),
+                                 last_span=(start, end), streams={}, last_choice={}, last_coefficients={})
+    for index, kind in enumerate(("key", "value")):
+        coeff = torch.randn(middle, features, generator=g) * torch.logspace(0, -2, features)[None]
+        codes, low, span = progressive.quantize8(coeff, tm.GROUP)
+        pick = torch.multinomial(torch.tensor([.05, .35, .25, .2, .1, .05]), middle, replacement=True, generator=g)
+        m = torch.tensor([0, 1, 2, 4, 6, 8])[pick]
+        planes = torch.zeros(middle, features // tm.GROUP, dtype=torch.long)
+        planes[:, :used] = m[:, None]
+        basis = tm.seeded_basis(features, features, GEOMETRY_3B_BASIS_SEED + index)
+        mean = torch.randn(features, generator=g) * 0.1
+        shim.streams[kind] = types.SimpleNamespace(mean=mean, basis=basis)
+        shim.last_choice[kind] = m
+        shim.last_coefficients[kind] = progressive.dequantize(codes, low, span, planes)
+        fixture[f"codes_{kind}"] = codes[:, :used].numpy()
+        fixture[f"low_{kind}"] = bits16(low[:, :used])
+        fixture[f"span_{kind}"] = bits16(span[:, :used])
+        fixture[f"planes_{kind}"] = m.numpy()
+        fixture[f"mean_{kind}"] = mean.numpy()
+    keys = [torch.randn(1, heads, tokens, dim, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    values = [torch.randn(1, heads, tokens, dim, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    fixture["exact_keys"] = np.stack([bits16(torch.cat([k[..., :start, :], k[..., end:, :]], dim=2)[0]) for k in keys])
+    fixture["exact_values"] = np.stack([bits16(torch.cat([v[..., :start, :], v[..., end:, :]], dim=2)[0]) for v in values])
+    cos, sin = kvtc.rope_tables(model, tokens, "cpu")
+    fixture["cos"], fixture["sin"] = cos.float().numpy(), sin.float().numpy()
+    queries = {q: torch.randn(1, q_heads, q, dim, generator=g).to(torch.bfloat16) for q in (1, 4)}
+    news = {q: (torch.randn(1, heads, q, dim, generator=g).to(torch.bfloat16),
+                torch.randn(1, heads, q, dim, generator=g).to(torch.bfloat16)) for q in (1, 4)}
+    for q in (1, 4):
+        fixture[f"query_q{q}"] = queries[q].float().numpy()
+        fixture[f"newk_q{q}"] = news[q][0].float().numpy()
+        fixture[f"newv_q{q}"] = news[q][1].float().numpy()
+    module = types.SimpleNamespace(layer_idx=0, num_key_value_groups=q_heads // heads)
+    with torch.inference_mode():
+        for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+            ctx = compressed_attention.CompressedContext(shim, [k.to(dtype) for k in keys], [v.to(dtype) for v in values],
+                                                         model, dtype=dtype)
+            for layer in range(layers):
+                module.layer_idx = layer
+                ex = ctx.exact_cache.layers[layer]
+                for q in (1, 4):
+                    k = torch.cat([ex.keys, news[q][0].to(dtype)], dim=2)
+                    v = torch.cat([ex.values, news[q][1].to(dtype)], dim=2)
+                    mask = None
+                    if q > 1:
+                        e = k.shape[2]
+                        mask = torch.zeros(1, 1, q, e, dtype=dtype)
+                        causal = torch.triu(torch.ones(q, q, dtype=torch.bool), 1)
+                        mask[0, 0, :, e - q:][causal] = torch.finfo(dtype).min
+                    out_, _ = ctx.attend(module, queries[q].to(dtype), k, v, mask, dim ** -0.5)
+                    fixture[f"{tag}_attend_l{layer}_q{q}"] = out_.float().numpy()
+            if dtype == torch.float32:
+                fixture["f32_keys_l0"] = ctx._keys(0).numpy()
+    np.savez_compressed(out / "geometry3b.npz", **fixture)
+
+
 def main() -> None:
     out = HERE
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     only = sys.argv[1:]
-    standalone = {"codes", "allocator", "encode"}  # fixtures that need no model
+    standalone = {"codes", "allocator", "encode", "geometry3b"}  # fixtures that need no prefilled context
     for name in only:
         if name in standalone:  # e.g. `make_golden.py encode`: write just the named fixtures
             globals()[f"{name}_fixture"](out)
@@ -142,6 +219,7 @@ def main() -> None:
         codes_fixture(out)
         allocator_fixture(out)
         encode_fixture(out)
+        geometry3b_fixture(out)
 
     model = tm.build_model(torch.bfloat16)
     dimmer.install(model)

@@ -132,3 +132,58 @@ def test_oracle_importance_matches_reference(golden):
 def test_allocator_fixture_consistent(golden):
     g = golden("allocator")
     assert g["chosen"].shape[0] == 2 * int(g["middle"])
+
+
+def _geometry3b_oracle(fix: dict, dtype: str):
+    """Oracle context over the 3B-geometry fixture: codes decoded by the oracle, bases rebuilt from their
+    seed exactly as the fixture script built them."""
+    import tinymodel as tm
+    from oracle.attention import OracleContext
+
+    L, H, D = 2, 8, 128
+    F = L * H * D
+    used = int(fix["groups_used"])
+    decoded, choice = {}, {}
+    for kind in ("key", "value"):
+        m = fix[f"planes_{kind}"]
+        planes = np.repeat(m[:, None], used, axis=1)
+        part = oc.dequantize(fix[f"codes_{kind}"], f16_from_bits(fix[f"low_{kind}"]), f16_from_bits(fix[f"span_{kind}"]),
+                             planes).reshape(len(m), -1)
+        full = np.zeros((len(m), F), dtype=np.float32)
+        full[:, : part.shape[1]] = part
+        decoded[kind], choice[kind] = full, m
+    bases = {kind: tm.seeded_basis(F, F, 500 + i).numpy() for i, kind in enumerate(("key", "value"))}
+    start, end = (int(v) for v in fix["span"])
+    return OracleContext(start=start, end=end, layers=L, heads=H, head_dim=D, choice=choice, decoded=decoded,
+                         basis=bases, mean={k: fix[f"mean_{k}"] for k in ("key", "value")}, cos=fix["cos"],
+                         sin=fix["sin"], dtype=dtype)
+
+
+@pytest.mark.parametrize("q", [1, 4])
+def test_oracle_matches_reference_at_3b_geometry(golden, q):
+    """The oracle against the reference's CompressedContext at the Llama-3.2-3B head geometry (8 KV heads of
+    128, 24 query heads, GQA 3; tests/golden/geometry3b.npz): keys at 1e-4, attention at 1e-4 (fp32 run)
+    and within the reference's own bf16 noise (bf16 run)."""
+    import torch
+
+    fix = golden("geometry3b")
+    for dtype in ("f32", "bf16"):
+        ctx = _geometry3b_oracle(fix, dtype)
+        if dtype == "f32" and q == 1:
+            assert np.abs(ctx.keys(0) - fix["f32_keys_l0"]).max() < 1e-4
+        for layer in range(2):
+            exk, exv = f32_from_bits(fix["exact_keys"][layer]), f32_from_bits(fix["exact_values"][layer])
+            k = np.concatenate([exk, oc.round_dtype(fix[f"newk_q{q}"][0], dtype)], axis=1)[None]
+            v = np.concatenate([exv, oc.round_dtype(fix[f"newv_q{q}"][0], dtype)], axis=1)[None]
+            mask = None
+            if q > 1:
+                e = k.shape[2]
+                mask = np.zeros((1, 1, q, e), dtype=np.float32)
+                mask[0, 0, :, e - q:][np.triu(np.ones((q, q), dtype=bool), 1)] = float(
+                    torch.finfo(torch.bfloat16 if dtype == "bf16" else torch.float32).min)
+            out = ctx.attend(layer, fix[f"query_q{q}"], k, v, mask, 128 ** -0.5)
+            ref = fix[f"{dtype}_attend_l{layer}_q{q}"]
+            assert out.shape == ref.shape
+            err = np.abs(out - ref).max()
+            tol = 1e-4 if dtype == "f32" else bf16_bound(fix, layer, q)
+            assert err < tol, (dtype, layer, err, tol)
