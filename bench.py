@@ -62,6 +62,10 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the one-layer oracle check after the timing")
+    p.add_argument("--no-splitk", action="store_true", help="multi-GPU runs: skip the split-K (cfg5) leg")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the unpack / encode / storage / allocator / demote rates after the timing")
     p.add_argument("--layers", type=int, default=None,
                    help="build the model with this many layers (same per-layer shapes; for small profiling cases)")
     p.add_argument("--kernels-only", action="store_true",
@@ -122,7 +126,46 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workload
-def build_workload(cfg: dict, seqs: int, seed: int, device, layers_override=None):
+def conv_seed(seed: int, i: int) -> int:
+    """Seed of conversation i of the batch: its plane draws and token ids do not depend on which GPU builds it."""
+    return 1_000_003 * (seed + 1) + 7919 * i
+
+
+def plan_batch(cfg: dict, seqs: int, seed: int) -> list[dict]:
+    """The batch before any model runs: per conversation its length, plane draws, group count and hot code
+    bytes (both streams, the reference's accounting). Every rank computes the same plan."""
+    import torch
+
+    from dimmerkv import synthetic
+
+    arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
+    features = arch["num_hidden_layers"] * arch["num_key_value_heads"] * arch["head_dim"]
+    g = torch.Generator().manual_seed(10_000 + seed)
+    lengths = torch.randint(cfg["tmin"], cfg["tmax"] + 1, (seqs,), generator=g).tolist()
+    plans = []
+    for i, t in enumerate(lengths):
+        gi = torch.Generator().manual_seed(conv_seed(seed, i))
+        m, groups, hot = synthetic.plan_conversation(t, features, cfg["budget"], gi, cfg["max_groups"])
+        busy = int((m["key"] > 0).sum())
+        plans.append(dict(index=i, tokens=t, planes=m, groups=groups, hot=hot, busy_key=busy, gen=gi))
+    return plans
+
+
+def partition(costs: list[float], world: int) -> list[list[int]]:
+    """Longest-processing-time bin packing: items by decreasing cost, each to the least loaded rank (ties to
+    the lowest rank). Returns each rank's item indices in ascending order."""
+    load = [0.0] * world
+    parts = [[] for _ in range(world)]
+    for i in sorted(range(len(costs)), key=lambda j: (-costs[j], j)):
+        r = min(range(world), key=lambda k: (load[k], k))
+        parts[r].append(i)
+        load[r] += costs[i]
+    return [sorted(p) for p in parts]
+
+
+def build_workload(cfg: dict, seqs: int, seed: int, device, layers_override=None, subset=None, plans=None):
+    """Model, packed batch and per-conversation data of the conversations ``subset`` (default: all) of the
+    seeded batch of ``seqs`` conversations (plan_batch)."""
     import torch
 
     from dimmerkv import dimmer, synthetic
@@ -137,18 +180,28 @@ def build_workload(cfg: dict, seqs: int, seed: int, device, layers_override=None
     rank = cfg["max_groups"] * 64
     bases = {kind: synthetic.seeded_basis(features, rank, 1000 + seed * 2 + i, device)
              for i, kind in enumerate(("key", "value"))}
-    g = torch.Generator().manual_seed(10_000 + seed)
-    lengths = torch.randint(cfg["tmin"], cfg["tmax"] + 1, (seqs,), generator=g).tolist()
+    if plans is None:
+        plans = plan_batch(cfg, seqs, seed)
+    chosen = [plans[i] for i in (subset if subset is not None else range(len(plans)))]
+    if not chosen:
+        raise ValueError("no conversation to build")
+    lengths = [pl["tokens"] for pl in chosen]
     max_t = max(lengths)
     cos_f, sin_f = synthetic.rope_full(model, max_t, device)
     convs = []
-    median = sorted(range(seqs), key=lambda i: lengths[i])[seqs // 2]
-    for i, t in enumerate(lengths):
-        ids = torch.randint(0, c.vocab_size, (1, t), generator=g).to(device)
+    median = sorted(range(len(chosen)), key=lambda i: lengths[i])[len(chosen) // 2]
+    for i, pl in enumerate(chosen):
+        t = pl["tokens"]
+        if layers_override is not None and layers_override != arch["num_hidden_layers"]:
+            planes = None  # a reduced model has fewer features: the budget gives another G, drawn afresh
+        else:
+            planes = pl["planes"]
+        ids = torch.randint(0, c.vocab_size, (1, t), generator=pl["gen"]).to(device)
         keys, values = synthetic.prefill(model, ids)
         with torch.inference_mode():
-            conv = synthetic.compress_conversation(keys, values, cos_f[:t], sin_f[:t], bases, cfg["budget"], g,
-                                                   cfg["max_groups"], keep_cpu=(i == median))
+            conv = synthetic.compress_conversation(keys, values, cos_f[:t], sin_f[:t], bases, cfg["budget"],
+                                                   pl["gen"], cfg["max_groups"], keep_cpu=(i == median),
+                                                   planes=planes)
         del keys, values
         convs.append(conv)
     mean = {kind: torch.stack([cv.mean[kind] for cv in convs]) for kind in ("key", "value")}
@@ -214,13 +267,77 @@ def build_codes_only(cfg: dict, seqs: int, seed: int, device):
 
 
 def step_work(batch, convs, layers: int):
-    """Algorithmic work of one decode step: (key_scores FLOPs per layer launch, code bytes per step).
-    Key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per layer; both streams' hot codes re-read once per layer."""
-    flops_layer, code_bytes_step = 0, 0
+    """Algorithmic work of one decode step of this rank's conversations: (key_scores FLOPs per layer launch,
+    code bytes per step, FLOPs of the whole step). Key rebuild 2*M_busy*r*Hkv*D + QK 2*M*Hq*D per layer (the
+    key_scores launch); the step adds the value weighting 2*M*Hq*r and the value basis 2*Hq*r*D per layer;
+    both streams' hot codes are re-read once per layer."""
+    flops_layer, code_bytes_step, step_flops = 0, 0, 0
     for cv in convs:
-        flops_layer += 2 * cv.busy_key * cv.groups * 64 * batch.n_cols + 2 * cv.middle * batch.q_heads * batch.head_dim
+        r = cv.groups * 64
+        key = 2 * cv.busy_key * r * batch.n_cols + 2 * cv.middle * batch.q_heads * batch.head_dim
+        flops_layer += key
+        step_flops += layers * (key + 2 * cv.middle * batch.q_heads * r + 2 * batch.q_heads * r * batch.head_dim)
         code_bytes_step += cv.hot_bytes * layers
-    return flops_layer, code_bytes_step
+    return flops_layer, code_bytes_step, step_flops
+
+
+def step_roofline(step_flops: int, code_bytes_step: int, step_s: float) -> dict:
+    """The whole decode step against its binding roofline: max(step FLOPs / sustained bf16 peak, code bytes /
+    HBM peak) over the measured step time."""
+    peaks = measured_peaks()
+    t_tensor = step_flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    t_hbm = code_bytes_step / (peaks["hbm_gbs"] * 1e9)
+    bound = max(t_tensor, t_hbm)
+    return {"bound": "tensor" if t_tensor >= t_hbm else "hbm", "step_tflop": round(step_flops / 1e12, 3),
+            "min_ms": round(bound * 1e3, 3), "ms": round(step_s * 1e3, 3), "frac": round(bound / step_s, 4),
+            "achieved_tflops": round(step_flops / step_s / 1e12, 1),
+            "peak": peaks["bf16_tflops_sustained"], "peak_source": peaks["source"] + " (bf16_tflops_sustained)",
+            "code_read_frac_of_hbm": round(code_bytes_step / step_s / (peaks["hbm_gbs"] * 1e9), 4)}
+
+
+def bench_parity(model, batch, convs, bases, layer: int | None = None) -> dict:
+    """Outside the timed region: one attention layer (the last by default) of the timed batch on a random
+    query, every conversation in one launch, and the conversation whose codes were kept on the host checked
+    against the oracle (oracle/attention.py, float64 sums, the reference's operand rounding)."""
+    import numpy as np
+    import torch
+
+    from oracle import codes as oc
+    from oracle.attention import OracleContext
+    from dimmerkv.synthetic import rope_full
+
+    c = model.config
+    L, H, D, HQ = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
+    layer = L - 1 if layer is None else layer
+    j = next(i for i, cv in enumerate(convs) if cv.cpu_codes is not None)
+    cv = convs[j]
+    dev = batch.device
+    g = torch.Generator().manual_seed(77)
+    query = torch.randn(len(convs), HQ, 1, D, generator=g).to(torch.bfloat16)
+    ek = torch.cat([x.exact_keys[layer] for x in convs]).to(dev)
+    ev = torch.cat([x.exact_values[layer] for x in convs]).to(dev)
+    with torch.inference_mode():
+        out = batch.attend_layer(layer, query.to(dev), ek, ev, None, D ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize(dev)
+    batch.check_status()
+    got = out[j : j + 1].cpu().numpy()
+    decoded, choice = {}, {}
+    for kind in ("key", "value"):
+        codes, low, span, planes, m = cv.cpu_codes[kind]
+        width = cv.groups * 64  # planes beyond the first G groups are zero: decode only those columns
+        decoded[kind] = oc.dequantize(codes[:, : cv.groups], low[:, : cv.groups], span[:, : cv.groups],
+                                      planes[:, : cv.groups]).reshape(len(m), width)
+        choice[kind] = m
+    cos, sin = rope_full(model, cv.tokens, dev)
+    ctx = OracleContext(start=4, end=cv.tokens - 32, layers=L, heads=H, head_dim=D, choice=choice, decoded=decoded,
+                        basis={k: v.cpu().numpy() for k, v in bases.items()},
+                        mean={k: v.cpu().numpy() for k, v in cv.mean.items()},
+                        cos=cos.cpu().numpy(), sin=sin.cpu().numpy(), dtype="bf16")
+    want = ctx.attend(layer, query[j : j + 1].float().numpy(), ek[j : j + 1].float().cpu().numpy(),
+                      ev[j : j + 1].float().cpu().numpy(), None, D ** -0.5)
+    err = float(np.abs(got - want).max())
+    return {"max_abs": err, "tolerance": 1e-4, "layer": layer, "conversation_tokens": cv.tokens,
+            "groups": cv.groups, "oracle": "oracle/attention.py (float64 sums)", "pass": bool(err < 1e-4)}
 
 
 class StageTimer:
@@ -254,21 +371,53 @@ class StageTimer:
                 for i, name in enumerate(self.NAMES)}
 
 
+def measured_peaks() -> dict:
+    """Roofline denominators: MEASURED_PEAKS.json (driver-measured on this pool's B200s), else the fallback."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+        return {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
+                "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "source": "of measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "of fallback"}
+
+
+KEY_KERNEL_SOURCES = ("key_scores_pair.cu", "dkv_ptx.cuh", "dkv_format.cuh", "dkv_kernels.h")
+
+
+def key_kernel_source_hash() -> str:
+    """sha256 (first 16 hex digits) of the sources the CTA-pair key kernel is compiled from: a profile of the
+    kernel is used for the line's traffic only while it was captured from these exact sources."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in KEY_KERNEL_SOURCES:
+        h.update((ROOT / "dimmer-kv_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def roofline(flops_layer: int, key_ms: list) -> dict:
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    peak_tf = peaks.get("bf16_tflops_sustained", 1400.0)
-    peak_name = "of measured (bf16_tflops_sustained)" if peaks else "of fallback"
+    peaks = measured_peaks()
+    peak_tf = peaks["bf16_tflops_sustained"]
+    peak_name = peaks["source"] + " (bf16_tflops_sustained)"
     key_avg_ms = statistics.mean(key_ms) if key_ms else float("nan")
     achieved = flops_layer / (key_avg_ms / 1e3) / 1e12
-    traffic = None
+    traffic, traffic_note = None, "no ncu capture of this build"
     prof = ROOT / "profiles" / "key_scores_traffic.json"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get("bytes_per_launch")
+        rec = json.loads(prof.read_text())
+        if rec.get("source_sha16") == key_kernel_source_hash():
+            # The capture's DRAM bytes per launch, scaled to this launch by the algorithmic FLOPs (traffic grows
+            # with the tokens rebuilt).
+            traffic = int(rec["bytes_per_launch"] * flops_layer / rec["flop_per_launch"])
+            traffic_note = rec.get("note", "")
+        else:
+            traffic_note = "the ncu capture in profiles/ is of other sources than this build's"
     return {"bound": "tensor", "kernel": "key_scores (tcgen05 key rebuild + RoPE + QK)",
             "achieved": round(achieved, 2), "peak": peak_tf, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tf, 4), "peak_source": peak_name,
             "avg_launch_ms": round(key_avg_ms, 4), "launches": len(key_ms),
-            "algorithmic_flop_per_launch": flops_layer, "traffic": traffic}
+            "algorithmic_flop_per_launch": flops_layer, "traffic": traffic, "traffic_note": traffic_note,
+            "source_sha16": key_kernel_source_hash()}
 
 
 def unpack_rate(batch, device, launches: int = 5) -> dict:
@@ -563,7 +712,7 @@ def run_kernels(args, cfg, device) -> dict:
     batch.timer = None
     batch.check_status()
     elapsed = start.elapsed_time(end) / 1e3
-    flops_layer, code_bytes_step = step_work(batch, convs, layers)
+    flops_layer, code_bytes_step, _ = step_work(batch, convs, layers)
     return {"mode": "kernels-only", "config": {"workload": cfg["workload"] + " (attention kernels only, no model)",
                                                "conversations": seqs, "context_mean": sum(lengths) / len(lengths)},
             "ms_per_step": round(elapsed / args.steps * 1e3, 3), "steps": args.steps, "warmup": args.warmup,
@@ -575,15 +724,16 @@ def run_kernels(args, cfg, device) -> dict:
             "allocate": allocate_rate(device), "demote": demote_rate(batch, device)}
 
 
-def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None):
-    """Model + one prefilled, compressed conversation of cfg["tmin"] tokens."""
+def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None, model=None):
+    """Model (built from ``seed`` unless given) + one prefilled, compressed conversation of cfg["tmin"] tokens."""
     import torch
 
     from dimmerkv import dimmer, synthetic
     from dimmerkv.context import rope_tables
 
     arch = synthetic.LLAMA_3B if cfg["arch"] == "3b" else synthetic.LLAMA_1B
-    model = synthetic.build_model(arch, device=device, seed=seed)
+    if model is None:
+        model = synthetic.build_model(arch, device=device, seed=seed)
     dimmer.install(model)
     c = model.config
     features = c.num_hidden_layers * c.num_key_value_heads * c.head_dim
@@ -695,22 +845,26 @@ class _LocalComm:
         return t
 
 
-def run_splitk(args, cfg, rank, world, device) -> dict | None:
-    """Config 5: one 131K-token conversation, its codes sharded over the ranks (split-K). Every rank
-    builds the same model and conversation (same seeds) and keeps its shard; bs1 decode steps, timed
-    between barriers with CUDA events, max over ranks."""
+def splitk_measure(cfg, rank, world, device, seed: int, steps: int, warmup: int, model=None) -> dict | None:
+    """One long conversation, its codes sharded over the ranks (split-K, dimmerkv.parallel): bs1 decode steps
+    timed between barriers with CUDA events on every rank, max over ranks. Every rank builds the same
+    conversation (same seeds) and keeps its shard. Outside the timed region rank 0 checks one layer of the
+    sharded attention against the same layer of one unsharded batch of the whole conversation on its own GPU
+    (the kernels that the single-GPU parity tests pin to the oracle)."""
     import torch
     import torch.distributed as dist
 
     from dimmerkv import dimmer
+    from dimmerkv.context import CompressedBatch
     from dimmerkv.parallel import SplitKContext, TorchComm
 
-    model, conv, bases, cos, sin = _one_conversation(cfg, args.seed, device)
+    model, conv, bases, cos, sin = _one_conversation(cfg, seed, device, model=model)
     c = model.config
     comm = TorchComm() if world > 1 else _LocalComm()
     ctx = SplitKContext(conv.codes, comm, layers=c.num_hidden_layers, kv_heads=c.num_key_value_heads,
                         head_dim=c.head_dim, q_heads=c.num_attention_heads, basis=bases, mean=conv.mean,
                         cos=cos, sin=sin, device=device)
+    full = conv.codes if rank == 0 else None
     conv.codes = None
     cache = exact_cache(model, [conv])
     ids = torch.zeros(1, 1, dtype=torch.int64, device=device)
@@ -719,21 +873,41 @@ def run_splitk(args, cfg, rank, world, device) -> dict | None:
     stream = torch.cuda.current_stream(device)
     try:
         with torch.inference_mode():
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 ids = model(input_ids=ids, past_key_values=cache, position_ids=pos).logits[:, -1].argmax(-1, keepdim=True)
                 pos = pos + 1
+                ctx.batch.poll_status()
+            ctx.batch.poll_status(depth=0)
             torch.cuda.synchronize(device)
             if world > 1:
                 dist.barrier()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with ClockSampler(device.index or 0) as clocks:
                 start.record(stream)
-                for _ in range(args.steps):
+                for _ in range(steps):
                     ids = model(input_ids=ids, past_key_values=cache, position_ids=pos).logits[:, -1].argmax(-1, keepdim=True)
                     pos = pos + 1
+                    ctx.batch.poll_status()
                 end.record(stream)
+                ctx.batch.poll_status(depth=0)
                 torch.cuda.synchronize(device)
             ctx.check_status()
+            # Parity, one layer (the last) on a random query: the sharded result against one unsharded batch.
+            g = torch.Generator().manual_seed(seed + 5)
+            L, H, D, HQ = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
+            q = torch.randn(1, HQ, 1, D, generator=g).to(device, torch.bfloat16)
+            ek = conv.exact_keys[L - 1].to(device)
+            ev = conv.exact_values[L - 1].to(device)
+            got = ctx.attend_layer(L - 1, q, ek, ev, None, D ** -0.5, out_dtype=torch.float32)
+            err = None
+            if rank == 0:
+                one = CompressedBatch([full], layers=L, kv_heads=H, head_dim=D, q_heads=HQ, basis=bases,
+                                      mean={k: v[None] for k, v in conv.mean.items()}, cos=cos, sin=sin, device=device)
+                want = one.attend_layer(L - 1, q, ek, ev, None, D ** -0.5, out_dtype=torch.float32)
+                one.check_status()
+                err = float((got - want).abs().max())
+                del one
+            torch.cuda.synchronize(device)
     finally:
         dimmer.STATE.compressed = None
     elapsed = torch.tensor([start.elapsed_time(end) / 1e3], device=device, dtype=torch.float64)
@@ -744,12 +918,27 @@ def run_splitk(args, cfg, rank, world, device) -> dict | None:
         return None
     code_bytes_step = conv.hot_bytes * c.num_hidden_layers
     return {"metric": "decode tok/s, one 131K-token conversation split over GPUs (bs1)",
-            "value": round(args.steps / t, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True,
+            "value": round(steps / t, 3), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": round(t / steps * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded random-init weights, random ids)",
             "config": {"workload": cfg["workload"], "context": conv.tokens, "groups": conv.groups,
-                       "parallelism": f"split-K x{world}"},
-            "code_read_gbs": round(code_bytes_step / (t / args.steps) / 1e9, 2), "clocks": clocks.summary()}
+                       "parallelism": f"split-K x{world}", "collectives_per_layer": 2},
+            "code_read_gbs": round(code_bytes_step / (t / steps) / 1e9, 2),
+            "parity_vs_one_gpu_max_abs": err, "clocks": clocks.summary()}
+
+
+def run_splitk(args, cfg, rank, world, device) -> dict | None:
+    """Config 5 on its own (--config cfg5)."""
+    return splitk_measure(cfg, rank, world, device, args.seed, args.steps, args.warmup)
+
+
+def run_splitk_leg(args, rank, world, device, model=None) -> dict | None:
+    """Config 5 after the conversation-parallel timing of a multi-GPU run (bounded: at most 32 timed steps), on
+    the same model (same architecture and seed)."""
+    import torch
+
+    torch.cuda.empty_cache()
+    return splitk_measure(CONFIGS["cfg5"], rank, world, device, args.seed, min(args.steps, 32), 3, model=model)
 
 
 # ----------------------------------------------------------------------------- runs
@@ -761,14 +950,24 @@ def run_ours(args, cfg, rank, world, device):
 
     seqs = args.seqs or cfg["seqs"]
     t0 = time.time()
-    model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed + 7919 * rank, device, args.layers)
+    # One seeded batch of `seqs` conversations for the whole job; each rank builds and decodes the share that
+    # the longest-first bin packing of hot code bytes gives it (strong scaling: the total work is fixed).
+    plans = plan_batch(cfg, seqs, args.seed)
+    if world > seqs:
+        raise SystemExit(f"{world} GPUs for {seqs} conversations: every GPU needs at least one")
+    parts = partition([float(pl["hot"]) for pl in plans], world)
+    mine = parts[rank]
+    model, batch, convs, lengths, bases = build_workload(cfg, seqs, args.seed, device, args.layers, subset=mine,
+                                                         plans=plans)
     setup_s = time.time() - t0
     layers = model.config.num_hidden_layers
-    flops_layer, code_bytes_step = step_work(batch, convs, layers)
+    flops_layer, code_bytes_step, step_flops = step_work(batch, convs, layers)
+    rank_bytes = [sum(plans[i]["hot"] for i in part) for part in parts]
+    rank_flops = [sum(plans[i]["busy_key"] * plans[i]["groups"] for i in part) for part in parts]
 
     cache = exact_cache(model, convs)
-    ids = torch.randint(0, model.config.vocab_size, (seqs, 1), device=device,
-                        generator=torch.Generator(device=device).manual_seed(args.seed + rank))
+    ids = torch.randint(0, model.config.vocab_size, (seqs, 1),
+                        generator=torch.Generator().manual_seed(args.seed + 1))[mine].to(device)
     positions = torch.tensor(lengths, device=device)[:, None]
     dimmer.STATE.compressed = batch
     stream = torch.cuda.current_stream(device)
@@ -777,14 +976,16 @@ def run_ours(args, cfg, rank, world, device):
 
     def step(ids_, pos_):
         out = model(input_ids=ids_, past_key_values=cache, position_ids=pos_, use_cache=True)
-        return out.logits[:, -1].argmax(-1, keepdim=True)
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        batch.poll_status()  # bounded host wait on the step two back: a device error raises within a step
+        return nxt
 
     with torch.inference_mode():
         for _ in range(args.warmup):
             ids = step(ids, positions)
             positions = positions + 1
+        batch.poll_status(depth=0)
         torch.cuda.synchronize(device)
-        batch.check_status()
         if world > 1:
             dist.barrier()
         batch.timer = timer
@@ -798,6 +999,7 @@ def run_ours(args, cfg, rank, world, device):
                 positions = positions + 1
                 torch.cuda.nvtx.range_pop()
             end.record(stream)
+            batch.poll_status(depth=0)
             torch.cuda.synchronize(device)
         batch.timer = None
         batch.check_status()
@@ -806,10 +1008,18 @@ def run_ours(args, cfg, rank, world, device):
         stage_ms = timer.stage_ms(args.steps)
 
     t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+    per_rank = [elapsed]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        per_rank = [float(x.item()) for x in gathered]
         dist.barrier()
-    elapsed_max = float(t.item())
+    elapsed_max = max(per_rank)
+
+    # One layer of one conversation of the timed batch against the oracle, outside the timed region.
+    parity = None
+    if rank == 0 and not args.no_parity:
+        parity = bench_parity(model, batch, convs, bases)
 
     # End to end through the public API: host token ids in, host next tokens out, every step.
     e2e = None
@@ -828,41 +1038,61 @@ def run_ours(args, cfg, rank, world, device):
         t = torch.tensor([e2e_s], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * seqs * args.steps / float(t.item()), "unit": "tok/s",
-               "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"]}
+        e2e = {"value": seqs * args.steps / float(t.item()), "unit": "tok/s",
+               "h2d_bytes_per_step": stats["h2d_bytes_per_step"] * world,
+               "d2h_bytes_per_step": stats["d2h_bytes_per_step"] * world}
     dimmer.STATE.compressed = None
-    unpack = unpack_rate(batch, device) if rank == 0 else None
-    encode = encode_rate(device) if rank == 0 else None
-    storage = storage_rate(device) if rank == 0 else None
-    allocate = allocate_rate(device) if rank == 0 else None
-    demote = demote_rate(batch, device) if rank == 0 else None  # last: it rewrites the batch's hot tier
+
+    splitk = None
+    if world > 1 and not args.no_splitk:
+        del cache
+        splitk = run_splitk_leg(args, rank, world, device, model)
+
+    extras = {}
+    if rank == 0 and not args.no_extras:
+        extras["unpack"] = unpack_rate(batch, device)
+        extras["encode"] = encode_rate(device)
+        extras["storage"] = storage_rate(device)
+        extras["allocate"] = allocate_rate(device)
+        extras["demote"] = demote_rate(batch, device)  # last: it rewrites the batch's hot tier
 
     result = None
     if rank == 0:
         clk = clocks.summary()
-        tokps = world * seqs * args.steps / elapsed_max
+        tokps = seqs * args.steps / elapsed_max
+        mean_b = sum(rank_bytes) / world
         result = {
             "metric": METRIC, "value": round(tokps, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, "
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, "
             "random token ids, synthetic PCA basis and plane counts)",
-            "config": {"workload": cfg["workload"], "conversations_per_gpu": seqs, "context_min": min(lengths),
-                       "context_max": max(lengths), "context_mean": round(sum(lengths) / len(lengths), 1),
-                       "budget": cfg["budget"], "parallelism": f"conversation-parallel x{world}",
+            "config": {"workload": cfg["workload"], "conversations": seqs, "context_min": min(pl["tokens"] for pl in plans),
+                       "context_max": max(pl["tokens"] for pl in plans),
+                       "context_mean": round(sum(pl["tokens"] for pl in plans) / seqs, 1),
+                       "budget": cfg["budget"], "parallelism": f"conversation-parallel x{world} (one batch, "
+                       "longest-first bin packing of hot code bytes)",
                        "l2": "inputs larger than L2 (codes re-read per layer, > 1 GB per layer)"},
-            "code_read_gbs": round(code_bytes_step / (elapsed_max / args.steps) / 1e9, 2),
+            "partition": {"conversations_per_rank": [len(p_) for p_ in parts],
+                          "hot_bytes_per_rank": rank_bytes,
+                          "bytes_max_over_mean": round(max(rank_bytes) / mean_b, 4),
+                          "rebuild_work_max_over_mean": round(max(rank_flops) / (sum(rank_flops) / world), 4),
+                          "ms_per_step_per_rank": [round(x / args.steps * 1e3, 3) for x in per_rank]},
+            "code_read_gbs": round(sum(rank_bytes) * layers / (elapsed_max / args.steps) / 1e9, 2),
             "roofline": roofline(flops_layer, key_ms),
             "clocks": clk,
             "stage_ms_per_step": stage_ms,
             "gpu_launches": len(key_ms) * KERNELS_PER_LAYER,
-            "unpack": unpack,
-            "encode": encode,
-            "storage": storage,
-            "allocate": allocate,
-            "demote": demote,
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }
+        if world == 1:
+            result["step_roofline"] = step_roofline(step_flops, code_bytes_step, elapsed_max / args.steps)
+        if parity is not None:
+            result["parity_max_abs"] = parity["max_abs"]
+            result["parity"] = parity
+        result.update(extras)
+        if splitk is not None:
+            result["splitk"] = splitk
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_sample(model, convs, bases, lengths, layers=2)
     return result
@@ -989,7 +1219,10 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(minutes=10), device_id=device)
+        # A short collective timeout: a rank that fails raises within a step (bounded kernel waits and the
+        # per-step status poll) and exits at once below, so the others need not wait out NCCL's default.
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    ok = False
     try:
         if args.kernels_only:
             if world > 1:
@@ -1007,8 +1240,19 @@ def main():
             result = run_ours(args, cfg, rank, world, device)
         if result is not None:
             print(json.dumps(result), flush=True)
+        ok = True
     finally:
         if world > 1:
+            if not ok:
+                # Leave without the process-group teardown (it may wait on peers): the launcher then stops
+                # the other ranks at once.
+                import traceback
+
+                traceback.print_exc()
+                sys.stdout.flush()
+                sys.stderr.flush()
+                os._exit(1)
+            dist.barrier()
             dist.destroy_process_group()
 
 

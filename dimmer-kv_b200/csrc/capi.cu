@@ -181,6 +181,7 @@ int dkv_softmax_stats(const dkv_attend_args* a, void* stream) {
   p.scratch = a->partial;
   p.scratch_floats = a->partial != nullptr ? static_cast<int64_t>(a->n_v_items) * a->rows_pad * a->v_item_groups * 64 : 0;
   p.n_sms = sm_count();
+  p.status = a->status;
   return dkv::run_softmax_stats(p, static_cast<cudaStream_t>(stream));
 }
 

@@ -67,6 +67,7 @@ struct SoftmaxParams {
   float* scratch;                 // optional: per-(row, slice) partials when few rows are long
   int64_t scratch_floats;
   int n_sms;                      // SMs of the device (sizes the slices)
+  const int* status;              // the call's status word (read at entry: non-zero means no work)
 };
 constexpr int kSoftmaxFull = 0;
 constexpr int kSoftmaxLocal = 1;   // row_stats <- (max, sum of exponentials) of this shard

@@ -2,10 +2,12 @@
 // mbarriers with bounded waits, bulk / tensor (TMA) copies, tcgen05 MMA,
 // TMEM allocation and loads, shared-memory matrix descriptors.
 //
-// Every wait in this file is bounded by a wall-clock deadline (globaltimer).
-// A wait that runs out records an error code in the caller's status word and
-// returns false; callers then stop issuing work and leave through the normal
-// exit path (TMEM freed, no copy left in flight that the CTA still waits on).
+// Every wait in this file is bounded (about two seconds, on two independent
+// clocks). A wait that runs out records an error code in the caller's status
+// word and returns false; callers then stop issuing work and leave through the
+// normal exit path (TMEM freed, no copy left in flight that the CTA still waits
+// on). Kernels also read the status word as they start and do no work when an
+// earlier kernel has recorded an error.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -28,9 +30,16 @@ enum DeviceError : int {
   kErrBadDescriptor = 110, // a tile / group descriptor failed its bounds check
 };
 
-// Deadline for one wait: 2 s of wall-clock time. Healthy waits in these
-// kernels last microseconds.
-constexpr uint64_t kWaitDeadlineNs = 2000000000ull;
+// Bound on one wait. Healthy waits in these kernels last microseconds. A wait gives up only when
+// BOTH clocks say that more than the deadline has passed and it has polled at least kWaitMinPolls
+// times: %globaltimer follows the host's clock (a time step on the host moves it), and %clock64 is
+// the cycle counter of the SM the thread runs on (a context switch can resume the CTA on another
+// SM), so neither alone can end a healthy wait early. A clock seen running backwards restarts its
+// measurement. 2e9 cycles is 1.02 s at the B200's 1965 MHz maximum SM clock, longer at lower clocks.
+// Both clocks are kept in units of 1024 (ns, cycles) modulo 2^32, which wraps after 73 minutes.
+constexpr uint32_t kWaitDeadlineNs1024 = 2000000000u / 1024u;
+constexpr uint32_t kWaitDeadlineCycles1024 = 2000000000u / 1024u;
+constexpr uint32_t kWaitMinPolls = 1u << 16;
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -38,8 +47,40 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+__device__ __forceinline__ uint64_t sm_cycles() {
+  uint64_t c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+
+// Elapsed-time bookkeeping of one bounded wait (started after its first unsuccessful poll).
+struct WaitClock {
+  uint32_t t0, c0, polls;
+  __device__ __forceinline__ WaitClock()
+      : t0(static_cast<uint32_t>(global_ns() >> 10)), c0(static_cast<uint32_t>(sm_cycles() >> 10)), polls(0) {}
+  // Counts one poll; true once the wait has run out.
+  __device__ __forceinline__ bool expired() {
+    if ((++polls & 63u) != 0u) return false;
+    const uint32_t t = static_cast<uint32_t>(global_ns() >> 10), c = static_cast<uint32_t>(sm_cycles() >> 10);
+    if (static_cast<int32_t>(t - t0) < 0) t0 = t;
+    if (static_cast<int32_t>(c - c0) < 0) c0 = c;
+    return polls >= kWaitMinPolls && t - t0 > kWaitDeadlineNs1024 && c - c0 > kWaitDeadlineCycles1024;
+  }
+};
+
 __device__ __forceinline__ void record_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+// The call's status word as the kernel starts: non-zero when an earlier kernel of the call (or of an
+// earlier call sharing the word) failed. Kernels that find it set do no work and leave at once.
+__device__ __forceinline__ int status_at_entry(const int* status) {
+  return status != nullptr ? *reinterpret_cast<const volatile int*>(status) : 0;
+}
+
+// CTA-uniform entry check for kernels that use __syncthreads: every thread gets the same answer.
+__device__ __forceinline__ bool cta_failed_at_entry(const int* status) {
+  return __syncthreads_or(threadIdx.x == 0 && status_at_entry(status) != 0) != 0;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -89,28 +130,43 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// Bounded wait for the phase with the given parity to complete. With `abort` (the CTA's abort flag in
+// shared memory), the wait also ends, without an error of its own, as soon as another role of the CTA
+// (or of its cluster) has given up, so that one failure ends every wait within microseconds. Waits
+// that drain the thread's own copies or MMAs in flight pass no abort flag: those always complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          const volatile int* abort = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
+  WaitClock clock;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitDeadlineNs) {
+    if (abort != nullptr && *abort != 0) return false;
+    if (clock.expired()) {
       record_error(status, code);
       return false;
     }
   }
 }
 
+// The same wait taken by every lane of a warp, with one answer for the whole warp (a warp vote), so
+// that the lanes never split between a loop's exit and the warp-wide (.sync.aligned) instructions that
+// follow a wait (tcgen05.ld, setmaxnreg, __syncwarp). All 32 lanes must call it.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          const volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, status, code, abort)) != 0;
+}
+
 // Rendezvous of a fixed group of threads on one of two mbarriers used alternately (each initialised
 // with the group's size), bounded like every other wait, so a thread that gave up on an earlier wait
-// never leaves the rest of the group blocked. n counts this thread's rendezvous so far.
-__device__ __forceinline__ bool group_sync(uint64_t* bars2, uint32_t& n, int* status, int code) {
+// never leaves the rest of the group blocked. n counts this thread's rendezvous so far. Called by whole
+// warps; the answer is the same for every lane of a warp.
+__device__ __forceinline__ bool group_sync(uint64_t* bars2, uint32_t& n, int* status, int code,
+                                           const volatile int* abort) {
   uint64_t* bar = bars2 + (n & 1);
   const uint32_t parity = (n >> 1) & 1;
   ++n;
   mbar_arrive(bar);
-  return mbar_wait(bar, parity, status, code);
+  return warp_wait(bar, parity, status, code, abort);
 }
 
 // ---------------------------------------------------------------- copies
@@ -244,6 +300,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 // per arrival.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Store a 32-bit word at a shared::cluster address (this CTA's or the peer's shared memory).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {

@@ -28,6 +28,7 @@ constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a com
 
 __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block,
                                                                   int row_block, int n_row_blocks) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   extern __shared__ float smem_f[];
   const int D = p.head_dim;
   const int D2 = D / 2;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
 // One CTA per (conversation, KV head, block of 8 rows of the head); a thread per output dim.
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const FinalizeParams p, int n_chunks,
                                                                    int rows_per_cta) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   const int G = p.q_per_kv;
   const int n_kv = p.n_q_heads / G;
   const int s = blockIdx.x / n_kv, kvh = blockIdx.x % n_kv;

@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accum_full = b_empty + kStagesB;
   uint64_t* accum_empty = accum_full + 1;
   uint64_t* ep_sync = accum_empty + 1;  // [2] epilogue rendezvous (256 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_sync + 2);
+  uint64_t* mma_done = ep_sync + 2;      // every issued MMA has completed (exit path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -140,7 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(accum_empty, 256);
     mbar_init(&ep_sync[0], 256);
     mbar_init(&ep_sync[1], 256);
-    *abort_flag = 0;
+    mbar_init(mma_done, 1);
+    // A kernel whose call has already failed does no work (every role sees the flag and skips).
+    *abort_flag = status_at_entry(p.status) != 0 ? 1 : 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, NB);
@@ -156,7 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       cc.load(p, nblocks);
       cb.load(p, nblocks);
       uint32_t c_iter = 0, b_iter = 0;
-      uint64_t idle_since = 0;
+      WaitClock idle;
+      bool idling = false;
       while ((!cc.done() || !cb.done()) && !*abort_flag) {
         bool progress = false;
         if (!cc.done()) {
@@ -192,16 +196,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (progress) {
-          idle_since = 0;
-        } else {
-          const uint64_t now = global_ns();
-          if (idle_since == 0) {
-            idle_since = now;
-          } else if (now - idle_since > kWaitDeadlineNs) {
-            record_error(p.status, kErrWaitEmpty);
-            *abort_flag = 1;
-          }
+          idling = false;
+        } else if (!idling) {
+          idle = WaitClock();
+          idling = true;
+        } else if (idle.expired()) {
+          record_error(p.status, kErrWaitEmpty);
+          *abort_flag = 1;
         }
+      }
+      // Drain: every copy this producer issued has landed before the CTA can leave.
+      for (int s = 0; s < kStagesC && s < static_cast<int>(c_iter); ++s) {
+        const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kStagesC);
+        mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kErrWaitDrain);
+      }
+      for (int s = 0; s < kStagesB && s < static_cast<int>(b_iter); ++s) {
+        const uint32_t last = b_iter - 1 - ((b_iter - 1 - s) % kStagesB);
+        mbar_wait(&b_full[s], (last / kStagesB) & 1, p.status, kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -217,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int item = p.items[it];
         const TileDesc tile = p.tiles[item / nblocks];
-        if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
+        if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -225,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int gi = 0; gi < tile.n_groups; ++gi) {
           const int sa = a_iter % kStagesA, sb = b_iter % kStagesB;
-          if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA) ||
-              !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis)) {
+          if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA, abort_flag) ||
+              !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
             ok = false;
             break;
           }
@@ -254,6 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(accum_full);
         ++item_iter;
       }
+      // Also on an early exit: no MMA may still read shared memory or TMEM past this point.
+      if (a_iter > 0) {
+        mma_commit(mma_done);
+        mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+      }
     }
   } else if (warp >= 2 && warp < 10) {
     // ------------------------------------------------------------ decode warps
@@ -273,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int gi = 0; gi < tile.n_groups; ++gi) {
         const int cs = c_iter % kStagesC;
         const int sa = a_iter % kStagesA;
-        if (!mbar_wait(&code_full[cs], (c_iter / kStagesC) & 1, p.status, kErrWaitCodes)) {
+        if (!warp_wait(&code_full[cs], (c_iter / kStagesC) & 1, p.status, kErrWaitCodes, abort_flag)) {
           *abort_flag = 1;
           break;
         }
         if (a_iter >= kStagesA &&
-            !mbar_wait(&a_empty[sa], ((a_iter / kStagesA) - 1) & 1, p.status, kErrWaitEmpty)) {
+            !warp_wait(&a_empty[sa], ((a_iter / kStagesA) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -328,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pos = hidden ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
       const __nv_bfloat16* cosrow = p.cos_t + static_cast<int64_t>(pos) * (D / 2);
       const __nv_bfloat16* sinrow = p.sin_t + static_cast<int64_t>(pos) * (D / 2);
-      if (!mbar_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum)) {
+      if (!warp_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum, abort_flag)) {
         *abort_flag = 1;
         break;
       }
@@ -337,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* out_base = p.scores + p.seq_score_off[s];
       const int kv0 = nblk * kHeads;
       for (int qi = 0; qi < p.q_len; ++qi) {
-        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           failed = true;
           break;
@@ -353,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       static_cast<int64_t>(p.layer) * p.n_cols + nblk * NB;
           for (int i = et; i < NB; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
         }
-        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
+        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           failed = true;
           break;
@@ -436,6 +452,7 @@ template <int D, int NB, int G, bool RAW>
 static int launch_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   using L = KeySmem<NB, RAW>;
   const int smem = 1024 + L::kQ + (NB / D) * G * D * 4 + NB * 4 + 24 * 8 + 32;
+  static_assert(2 * (L::kStagesC + L::kStagesA + kStagesB) + 5 <= 24, "barrier space");
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_kernel<D, NB, G, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

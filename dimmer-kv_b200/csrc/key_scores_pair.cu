@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     mbar_init(mma_done, 1);
     mbar_init(&ep_sync[0], 256);
     mbar_init(&ep_sync[1], 256);
-    *abort_flag = 0;
+    // A kernel whose call has already failed does no work (every role sees the flag and skips).
+    *abort_flag = status_at_entry(p.status) != 0 ? 1 : 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kPairCols);
@@ -199,6 +200,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const uint32_t a_full_lead = mapa_shared(smem_u32(a_full), 0);
   const uint32_t b_peer_lead = mapa_shared(smem_u32(b_peer), 0);
   const uint32_t accum_empty_lead = mapa_shared(smem_u32(accum_empty), 0);
+  // The abort flag is cluster-wide: a role that gives up sets it in both CTAs (its own and, through
+  // st.shared::cluster, the peer's), so that no role of either CTA keeps waiting on a partner that has
+  // stopped. Both CTAs stay resident until the final cluster barrier, so the peer's flag is valid.
+  auto give_up = [abort_flag]() {
+    *abort_flag = 1;
+    st_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(abort_flag)), cluster_ctarank() ^ 1u), 1u);
+  };
+  if (tid == 0 && *abort_flag) give_up();  // the entry check of either CTA stops both
 
   // Each role's register budget is set at the top of its warpgroup's branch (so that it governs the
   // role's code) and the launch budget restored at the bottom, before the common exit path; the
@@ -215,8 +224,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       while (!c_ended && !*abort_flag) {
         const int cs = c_iter % kStagesC;
         if (c_iter >= kStagesC &&
-            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitEmpty)) {
-          *abort_flag = 1;
+            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          give_up();
           break;
         }
         if (cc.done()) {
@@ -238,7 +247,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size ||
               gr.group >= p.n_union_groups) {
             record_error(p.status, kErrBadDescriptor);
-            *abort_flag = 1;
+            give_up();
             break;
           }
           w0.w = (w0.w & 0xFFFFu) | (n_tok << 16);  // pad0: the tile's token count
@@ -259,7 +268,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int e = 0; e < 2; ++e) {
         const int cs = c_iter % kStagesC;
         if (c_iter >= kStagesC &&
-            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitDrain))
+            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitDrain, abort_flag))
           break;
         uint4* stash = reinterpret_cast<uint4*>(c_slots + (cs + 1) * kCodeSlot - 32);
         stash[0] = make_uint4(0u, 0u, 0u, kStashEnd << 24);
@@ -283,8 +292,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       while (!cb.done() && !*abort_flag) {
         const int sb = b_iter % kStagesB;
         if (b_iter >= kStagesB &&
-            !mbar_wait(&b_empty[sb], ((b_iter / kStagesB) - 1) & 1, p.status, kErrWaitEmpty)) {
-          *abort_flag = 1;
+            !mbar_wait(&b_empty[sb], ((b_iter / kStagesB) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          give_up();
           break;
         }
         int desc;
@@ -312,23 +321,23 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const int it = items.at(k);
           if (it < 0) {
             record_error(p.status, kErrBadDescriptor);
-            *abort_flag = 1;
+            give_up();
             break;
           }
           const int n_merged = p.pairs[4 * (p.items[it] / nblocks) + 2];
           if (n_merged <= 0) continue;  // nothing accumulated; the epilogue writes the mean-only keys
           if (item_iter >= 1 &&
-              !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree)) {
-            *abort_flag = 1;
+              !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
+            give_up();
             break;
           }
           tc_fence_after();
           bool ok = true;
           for (int gi = 0; gi < n_merged; ++gi) {
             const int sa = a_iter % kStagesA, sb = b_iter % kStagesB;
-            if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA) ||
-                !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis) ||
-                !mbar_wait(&b_peer[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis)) {
+            if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA, abort_flag) ||
+                !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag) ||
+                !mbar_wait(&b_peer[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
               ok = false;
               break;
             }
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             ++b_iter;
           }
           if (!ok) {
-            *abort_flag = 1;
+            give_up();
             break;
           }
           mma_commit_pair(accum_full, 0x3);
@@ -370,8 +379,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         uint32_t b_iter = 0;
         while (!cf.done() && !*abort_flag) {
           const int sb = b_iter % kStagesB;
-          if (!mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis)) {
-            *abort_flag = 1;
+          if (!mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
+            give_up();
             break;
           }
           mbar_arrive_cluster(b_peer_lead + sb * 8);
@@ -392,8 +401,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int h = u >> 7;
     for (uint32_t i = set;; i += 2) {  // position in the sequence: code slot i % kStagesC, A stage i % kStagesA
       const int cs = i % kStagesC;
-      if (!mbar_wait(&code_full[cs], (i / kStagesC) & 1, p.status, kErrWaitCodes)) {
-        *abort_flag = 1;
+      if (!warp_wait(&code_full[cs], (i / kStagesC) & 1, p.status, kErrWaitCodes, abort_flag)) {
+        give_up();
         break;
       }
       const uint8_t* slot = c_slots + cs * kCodeSlot;
@@ -401,8 +410,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       if ((w0.w >> 24) & kStashEnd) break;
       const int sa = i % kStagesA;
       if (i >= static_cast<uint32_t>(kStagesA) &&
-          !mbar_wait(&a_empty[sa], ((i / kStagesA) - 1) & 1, p.status, kErrWaitEmpty)) {
-        *abort_flag = 1;
+          !warp_wait(&a_empty[sa], ((i / kStagesA) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+        give_up();
         break;
       }
       const GroupRegs gr = group_from_words(w0, *reinterpret_cast<const uint4*>(slot + kCodeSlot - 16));
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int it = items.at(k);
       if (it < 0) {
         record_error(p.status, kErrBadDescriptor);
-        *abort_flag = 1;
+        give_up();
         break;
       }
       const int code = p.items[it];
@@ -452,8 +461,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const __nv_bfloat16* cosrow = p.cos_t + static_cast<int64_t>(pos) * (D / 2);
       const __nv_bfloat16* sinrow = p.sin_t + static_cast<int64_t>(pos) * (D / 2);
       if (accumulated) {
-        if (!mbar_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum)) {
-          *abort_flag = 1;
+        if (!warp_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum, abort_flag)) {
+          give_up();
           break;
         }
         tc_fence_after();
@@ -465,8 +474,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int kv0 = nblk * kHeads;
         const int h0 = head_half * kHalfHeads;  // first head of this half
         for (int qi = 0; qi < p.q_len; ++qi) {
-          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
-            *abort_flag = 1;
+          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+            give_up();
             failed = true;
             break;
           }
@@ -480,8 +489,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                                         static_cast<int64_t>(p.layer) * p.n_cols + nblk * kPairCols;
             for (int i = et; i < kPairCols; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
           }
-          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum)) {
-            *abort_flag = 1;
+          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+            give_up();
             failed = true;
             break;
           }

@@ -11,6 +11,7 @@
 // shard rounds its probabilities exactly as one softmax over all tokens would.
 #include <cfloat>
 #include <cmath>
+#include "dkv_ptx.cuh"
 #include "dkv_kernels.h"
 
 namespace dkv {
@@ -88,6 +89,7 @@ __device__ __forceinline__ void block_max_sum(const float* sc, int64_t lo, int64
 // Few long rows (one long conversation): each row's compressed scores are cut into `splits` slices, one
 // CTA per (row, slice) writes the slice's (max, sum of exponentials) to scratch[row][slice].
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_partial_kernel(const SoftmaxParams p, int splits) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   __shared__ float red_m[16], red_l[16];
   const int row = blockIdx.x, slice = blockIdx.y;
   const RowSlice r = row_slice(p, row, slice, splits);
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_partial_kernel(const 
 // The compressed probability mass of each slice with the row's final (max, 1 / sum): the sum of the
 // bf16-rounded probabilities (the reference's p_c.to(dtype), compressed_attention.py:127-130).
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_mass_kernel(const SoftmaxParams p, int splits) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   __shared__ float red[8];
   const int row = blockIdx.x, slice = blockIdx.y;
   const RowSlice r = row_slice(p, row, slice, splits);
@@ -127,6 +130,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_mass_kernel(const Sof
 
 // Sums each row's slice masses in slice order into row_stats[2].
 __global__ void softmax_mass_sum_kernel(const SoftmaxParams p, int splits, int rows) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   const float* part = p.scratch + static_cast<int64_t>(rows) * splits * 2 + static_cast<int64_t>(row) * splits;
@@ -136,6 +140,7 @@ __global__ void softmax_mass_sum_kernel(const SoftmaxParams p, int splits, int r
 }
 
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const SoftmaxParams p, int splits) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   extern __shared__ float sh[];
   const int D = p.head_dim;
   float* qv = sh;                     // [D]

@@ -89,6 +89,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed: no work
   const TileDesc tile = p.tiles[blockIdx.x];
   const int n_union = static_cast<int>(p.out_cols / kGroup);
   if (tile.n_tokens < 1 || tile.n_tokens > kTileTokens || tile.n_groups < 0 || tile.n_groups > n_union) {
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
         }
         const int s = issued % kUnpackSlots;
         if (issued >= kUnpackSlots &&
-            !mbar_wait(&empty[s], ((issued / kUnpackSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
+            !mbar_wait(&empty[s], ((issued / kUnpackSlots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   for (int i = 0; i < tile.n_groups; ++i) {
     const int s = i % kUnpackSlots;
     // The warp leaves together (its stores end in __syncwarp): one lane giving up ends the warp.
-    const bool landed = mbar_wait(&full[s], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes);
+    const bool landed = mbar_wait(&full[s], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes, abort_flag);
     if (!__all_sync(0xffffffffu, landed)) {
       *abort_flag = 1;
       return;

@@ -65,6 +65,7 @@ __device__ __forceinline__ int next_pair(const GroupDesc* d, int n, int g0, int&
 // B operand sits in shared memory (two atoms of 64 tokens, n_rows_pad rows x 128 B, 128B swizzle),
 // built in shared memory and written out whole.
 __global__ void __launch_bounds__(256) vprobs_kernel(const ValueWeightParams p) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   extern __shared__ __align__(16) uint8_t img[];  // [2][NR][128]
   const int NR = p.n_rows_pad;
   const int t = blockIdx.x;
@@ -150,7 +151,8 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       mbar_init(&accum_empty[i], 128);
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    // A kernel whose call has already failed does no work (every role sees the flag and skips).
+    *abort_flag = status_at_entry(p.status) != 0 ? 1 : 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               break;
             }
             const int pb = p_iter & 1;
-            if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+            if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
               *abort_flag = 1;
               break;
             }
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             bulk_load(p_tiles + pb * p_tile, p.p_img + static_cast<int64_t>(t) * p_tile, p_tile, &p_full[pb]);
             ++p_iter;
           }
-          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -241,7 +243,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                         p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
           const int db = d_iter & 1;
-          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
+          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               }
               const int cs = c_iter % kCodeSlots;
               if (c_iter >= kCodeSlots &&
-                  !mbar_wait(&r_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty)) {
+                  !mbar_wait(&r_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -302,7 +304,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         // drains one half while the next item accumulates into the other.
         const uint32_t acc_base = tmem + (item_iter & 1) * kAccumCols;
         if (item_iter >= 2 &&
-            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kErrWaitAccumFree)) {
+            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -313,8 +315,8 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int pb = p_iter & 1, db = d_iter & 1;
           const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                         p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
-          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA) ||
-              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
+          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA, abort_flag) ||
+              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
             ok = false;
             break;
           }
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
             const int set = ord & 1;
             const int slot = a_iter[set] % a_slots;
-            if (!mbar_wait(&a_full[set * 2 + slot], (a_iter[set] / a_slots) & 1, p.status, kErrWaitA)) {
+            if (!mbar_wait(&a_full[set * 2 + slot], (a_iter[set] / a_slots) & 1, p.status, kErrWaitA, abort_flag)) {
               ok = false;
               break;
             }
@@ -356,8 +358,9 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         mma_commit(&accum_full[item_iter & 1]);
         ++item_iter;
       }
-      if (issued && *abort_flag) {
-        // Early exit: no MMA may still read shared memory or TMEM past this point.
+      if (issued) {
+        // Every exit (also one where the epilogue gave up): no MMA may still read shared memory or TMEM
+        // past this point.
         mma_commit(mma_done);
         mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
       }
@@ -396,7 +399,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         st_s[2 * w + 1] = inv;
       }
       mbar_arrive(&stats_ready[item_iter % 3]);
-      if (!mbar_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kErrWaitA)) {
+      if (!warp_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kErrWaitA, abort_flag)) {
         *abort_flag = 1;
         break;
       }
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype); set s builds
         //      rows [s*NR/2, (s+1)*NR/2), thread half h a quarter of them.
         const int pb = p_iter & 1;
-        if (!PIMG && p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty)) {
+        if (!PIMG && p_iter >= 2 && !warp_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         const int db = d_iter & 1;
         const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                       p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
-        if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes)) {
+        if (!warp_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           }
           const int slot = a_iter % a_slots;
           if (a_iter >= static_cast<uint32_t>(a_slots) &&
-              !mbar_wait(&a_empty[set * 2 + slot], ((a_iter / a_slots) - 1) & 1, p.status, kErrWaitEmpty)) {
+              !warp_wait(&a_empty[set * 2 + slot], ((a_iter / a_slots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -464,7 +467,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             uint32_t out[16];
             if (gi >= 0) {
               const int cs = set * kCodeSlots + c_iter % kCodeSlots;  // this set's ring
-              if (!mbar_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kErrWaitCodes)) {
+              if (!warp_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kErrWaitCodes, abort_flag)) {
                 *abort_flag = 1;
                 break;
               }
@@ -494,7 +497,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       if (*abort_flag) break;
       // ---- epilogue (warps 4..7, one per TMEM lane quarter): TMEM -> partial sums
       if (warp == 4 || warp == 5 || warp == 14 || warp == 15) {
-        if (!mbar_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kErrWaitAccum)) {
+        if (!warp_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           break;
         }

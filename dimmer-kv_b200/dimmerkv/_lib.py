@@ -193,3 +193,54 @@ def check_device_status(status) -> None:
     code = int(status.item())
     if code != 0:
         raise DimmerKVError(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown')}")
+
+
+class StatusPoller:
+    """Bounded host-side watch over a device status word, for decode loops that never synchronise.
+
+    Every ``poll()`` enqueues, on the current stream, a copy of the status word into pinned host memory
+    behind the work queued so far, then waits for the copy enqueued ``depth`` polls earlier: at most
+    ``max_wait_s`` seconds, checking the event every half millisecond. It raises ``DimmerKVError`` when a
+    kernel recorded an error or when the device has not reached that point in time, so that a stalled or
+    failed device surfaces as a Python error within one step instead of blocking the host (and, under
+    ``torch.distributed``, the other ranks) until a collective times out. With ``depth`` = 0 the poll
+    waits for everything enqueued so far; with ``depth`` = 2 the host stays at most two steps ahead."""
+
+    def __init__(self, status, depth: int = 2, max_wait_s: float = 60.0):
+        import collections
+
+        import torch
+
+        if depth < 0 or max_wait_s <= 0:
+            raise ValueError("depth must be >= 0 and max_wait_s > 0")
+        self.status, self.depth, self.max_wait_s = status, depth, max_wait_s
+        self._host = torch.zeros(depth + 1, dtype=torch.int32).pin_memory()
+        self._queue = collections.deque()
+        self._next = 0
+
+    def poll(self, depth: int | None = None) -> None:
+        import time
+
+        import torch
+
+        depth = self.depth if depth is None else min(depth, self.depth)
+        slot = self._next
+        self._next = (self._next + 1) % self._host.numel()
+        self._host[slot:slot + 1].copy_(self.status, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(self.status.device))
+        self._queue.append((event, slot))
+        while len(self._queue) > depth:
+            event, slot = self._queue.popleft()
+            deadline = time.monotonic() + self.max_wait_s
+            while not event.query():
+                if time.monotonic() > deadline:
+                    raise DimmerKVError(f"the device did not finish a step within {self.max_wait_s:.0f} s")
+                time.sleep(0.0005)
+            code = int(self._host[slot])
+            if code != 0:
+                raise DimmerKVError(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown')}")
+
+    def drain(self) -> None:
+        """Wait (bounded) for every poll still queued and check it."""
+        self.poll(depth=0)

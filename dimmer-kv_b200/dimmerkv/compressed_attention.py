@@ -143,7 +143,9 @@ def greedy_decode_batch(model, batch: CompressedBatch, cache, host_ids: torch.Te
     """Greedy decode of every conversation of ``batch`` for ``steps`` tokens.
 
     ``host_ids`` / ``host_positions``: [B, 1] int64 in (pinned) host memory. Every step copies the
-    ids to the device, runs the model with attention over the codes and reads the next ids back.
+    ids to the device, runs the model with attention over the codes and reads the next ids back, with
+    the batch's status word behind them; the host waits for them at most ``batch.poll_wait_s`` seconds
+    and raises ``DimmerKVError`` on a device error (``CompressedBatch.poll_status``).
     Returns (tokens [B, steps] int64 on the host, byte counts of the per-step copies)."""
     device = batch.device
     ids_host = host_ids.clone().pin_memory() if not host_ids.is_pinned() else host_ids.clone()
@@ -155,10 +157,11 @@ def greedy_decode_batch(model, batch: CompressedBatch, cache, host_ids: torch.Te
             ids = ids_host.to(device, non_blocking=True)
             logits = model(input_ids=ids, past_key_values=cache, position_ids=pos, use_cache=True).logits
             nxt = logits[:, -1].argmax(-1, keepdim=True)
-            ids_host.copy_(nxt)  # device -> pinned host, synchronising
+            ids_host.copy_(nxt, non_blocking=True)  # device -> pinned host
+            batch.poll_status(depth=0)  # bounded wait for the ids and the status word behind them
             out[:, i] = ids_host[:, 0]
             pos = pos + 1
     finally:
         dimmer.STATE.compressed = None
     nbytes = ids_host.numel() * ids_host.element_size()
-    return out, {"h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes}
+    return out, {"h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes + batch.status.element_size()}

@@ -233,6 +233,8 @@ class CompressedBatch:
         self._v_items_cache: dict[int, tuple] = {}
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._poller = None
+        self.poll_wait_s = 60.0  # bound of one host wait in poll_status
         self.timer = None  # optional callable(kind, fn) wrapping launches (used by the bench)
         self.demote_timer = None  # optional callable(launch, args) wrapping the dkv_demote launch
         self.scoring = False
@@ -448,6 +450,19 @@ class CompressedBatch:
 
     def check_status(self) -> None:
         _lib.check_device_status(self.status)
+
+    def poll_status(self, depth: int | None = None) -> None:
+        """Bounded per-step check of the status word (``_lib.StatusPoller``): raises ``DimmerKVError``
+        when a kernel recorded an error or the device has not finished the step ``depth`` polls back
+        within ``poll_wait_s`` seconds. Call it once per decode step."""
+        if self._poller is None:
+            self._poller = _lib.StatusPoller(self.status, depth=2, max_wait_s=self.poll_wait_s)
+        self._poller.poll(depth)
+
+    def reset_status(self) -> None:
+        """Clear a recorded device error. Kernels read the status word as they start and do no work while
+        it is set, so a batch whose call failed stays inert until this is called."""
+        self.status.zero_()
 
     # ------------------------------------------------------------------ question time
     def begin_scoring(self) -> None:

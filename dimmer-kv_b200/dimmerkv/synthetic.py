@@ -132,18 +132,35 @@ class SyntheticConversation:
     full: dict | None = None       # kind -> device (codes, low, span, hot planes) for a cold tier
 
 
+def plan_conversation(tokens: int, features: int, budget: float, generator: torch.Generator,
+                      max_groups: int) -> tuple[dict, int, int]:
+    """Plane counts of one conversation's middle tokens (key, value), drawn as compress_conversation
+    draws them, with the group count G and the hot bytes they give: (planes, G, hot bytes). Needs no
+    model, so that a batch can be partitioned across GPUs by its code bytes before it is built."""
+    middle = tokens - SINKS - RECENT
+    m = {kind: draw_planes(middle, generator) for kind in ("key", "value")}
+    G = budget_groups(tokens, features, budget, m["key"], m["value"], max_groups)
+    hot = sum(int(G * (8 * m[k] + 4 * (m[k] > 0)).sum()) + middle for k in ("key", "value"))
+    return m, G, hot
+
+
 def compress_conversation(keys: list[torch.Tensor], values: list[torch.Tensor], cos, sin, bases: dict,
                           budget: float, generator: torch.Generator, max_groups: int,
                           keep_cpu: bool = False, fixed_planes: int | None = None,
-                          keep_full: bool = False) -> SyntheticConversation:
+                          keep_full: bool = False, planes: dict | None = None) -> SyntheticConversation:
     """Compress one prefilled conversation with progressive codes: every middle token's plane count is
-    drawn from PLANE_CHOICES (or ``fixed_planes`` for all), applied to the first G groups, G the largest
-    that fits ``budget``. ``keep_full`` keeps the full 8-bit codes on the device for a cold tier."""
+    drawn from PLANE_CHOICES (or ``fixed_planes`` for all, or given per token by ``planes``), applied to
+    the first G groups, G the largest that fits ``budget``. ``keep_full`` keeps the full 8-bit codes on
+    the device for a cold tier."""
     tokens = keys[0].shape[2]
     start, end = SINKS, tokens - RECENT
     middle = end - start
     features = sum(k.shape[1] * k.shape[3] for k in keys)
-    if fixed_planes is not None:
+    if planes is not None:
+        m = {kind: planes[kind].to(torch.int64).cpu() for kind in ("key", "value")}
+        if any(int(v.numel()) != middle for v in m.values()):
+            raise ValueError("planes must give one count per middle token of each stream")
+    elif fixed_planes is not None:
         m = {kind: torch.full((middle,), fixed_planes, dtype=torch.int64) for kind in ("key", "value")}
     else:
         m = {kind: draw_planes(middle, generator) for kind in ("key", "value")}
