@@ -46,8 +46,8 @@ CONFIGS = {
                           "(split-K, log-sum-exp merge over NCCL), bs1 decode"),
 }
 METRIC = "decode tok/s over compressed KV (3B,16K,bs64)"
-# Kernels of one attention layer (one row chunk): key_scores_pair, softmax_stats, vprobs, value_weights,
-# vbasis, combine.
+# Kernels of one attention layer (one row chunk): key_scores_pair, softmax_stats, vprobs, value_dense (or
+# value_weights), vbasis, combine; plus, once per step, the unpack of the value planes.
 KERNELS_PER_LAYER = 6
 
 
@@ -346,7 +346,17 @@ class StageTimer:
     NAMES = ("key_scores", "softmax_stats", "value_weights", "finalize")
 
     def __init__(self, batch, stream):
-        self.batch, self.stream, self.events = batch, stream, []
+        self.batch, self.stream, self.events, self.unpack_events = batch, stream, [], []
+
+    def unpack(self, launch):
+        """Events around the once-per-step decode of the value planes (CompressedBatch._dense_values)."""
+        import torch
+
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(self.stream)
+        launch()
+        ev[1].record(self.stream)
+        self.unpack_events.append(ev)
 
     def __call__(self, layer, call, a, s):
         import torch
@@ -367,8 +377,10 @@ class StageTimer:
         return [ev[0].elapsed_time(ev[1]) for ev in self.events]
 
     def stage_ms(self, steps: int):
-        return {name: round(sum(ev[i].elapsed_time(ev[i + 1]) for ev in self.events) / steps, 3)
-                for i, name in enumerate(self.NAMES)}
+        out = {name: round(sum(ev[i].elapsed_time(ev[i + 1]) for ev in self.events) / steps, 3)
+               for i, name in enumerate(self.NAMES)}
+        out["value_unpack"] = round(sum(a.elapsed_time(b) for a, b in self.unpack_events) / steps, 3)
+        return out
 
 
 def measured_peaks() -> dict:
@@ -719,7 +731,8 @@ def run_kernels(args, cfg, device) -> dict:
             "attention_tok_s": round(seqs * args.steps / elapsed, 2),
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
-            "gpu_launches": len(timer.events) * KERNELS_PER_LAYER, "unpack": unpack_rate(batch, device),
+            "gpu_launches": len(timer.events) * KERNELS_PER_LAYER + len(timer.unpack_events),
+            "unpack": unpack_rate(batch, device),
             "encode": encode_rate(device), "storage": storage_rate(device),
             "allocate": allocate_rate(device), "demote": demote_rate(batch, device)}
 
@@ -1081,7 +1094,7 @@ def run_ours(args, cfg, rank, world, device):
             "roofline": roofline(flops_layer, key_ms),
             "clocks": clk,
             "stage_ms_per_step": stage_ms,
-            "gpu_launches": len(key_ms) * KERNELS_PER_LAYER,
+            "gpu_launches": len(key_ms) * KERNELS_PER_LAYER + len(timer.unpack_events),
             "e2e": e2e,
             "setup_s": round(setup_s, 1),
         }

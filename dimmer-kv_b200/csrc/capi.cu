@@ -216,6 +216,14 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
   if ((a->v_item_order != nullptr && a->v_cta_begin == nullptr) || (a->v_cta_begin != nullptr && a->grid_v <= 0))
     return DKV_ERR_ARGS;
   const int grid = a->grid_v > 0 ? a->grid_v : (a->n_v_items < sm_count() ? a->n_v_items : sm_count());
+  if (a->v_dense != nullptr && a->p_img != nullptr) {
+    // Coefficients decoded once per step: TMA boxes of 64 components x 128 token rows.
+    CUtensorMap map;
+    const int rc = basis_map(a->v_dense, static_cast<uint64_t>(a->n_v_tiles) * 128, static_cast<uint64_t>(a->v_width),
+                             128u, &map);
+    if (rc != DKV_OK) return rc;
+    return dkv::run_value_dense(map, p, grid, static_cast<cudaStream_t>(stream));
+  }
   return dkv::run_value_weights(p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -375,6 +383,7 @@ int dkv_unpack(const dkv_unpack_args* a, void* stream) {
   p.out_bf16 = a->out_bf16;
   p.max_planes = a->max_planes;
   p.status = a->status;
+  p.out_tile_rows = a->out_tile_rows;
   return dkv::run_unpack(p, static_cast<cudaStream_t>(stream));
 }
 

@@ -101,6 +101,12 @@ struct ValueWeightParams {
   int n_tiles;                    // value tiles (with p_img)
 };
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream);
+// P^T images of every value tile (vprobs_kernel), used by both value kernels.
+int run_vprobs(const ValueWeightParams& p, cudaStream_t stream);
+// The value stage over coefficients decoded once per step (value_dense.cu): vmap is a 2-D tensor map of
+// the tile-padded bf16 buffer [n_tiles * 128][width], box 64 components x 128 rows, 128B swizzle.
+int run_value_dense(const CUtensorMap& vmap, const ValueWeightParams& p, int grid, cudaStream_t stream);
+int dense_value_stages(int n_rows_pad);
 
 // Value basis, mean and exact tokens -> attention output (finalize.cu).
 struct FinalizeParams {
@@ -199,11 +205,12 @@ struct UnpackParams {
   const TileDesc* tiles;
   const GroupDesc* groups;
   int n_tiles;
-  void* out;                      // [tokens][out_cols] fp32 or bf16, stream order
+  void* out;                      // [tokens][out_cols] fp32 or bf16, stream order (or tile-padded)
   int64_t out_cols;
   int out_bf16;
   int max_planes;                 // 0: unknown (slots sized for raw blocks)
   int* status;
+  int out_tile_rows;              // 0: rows in stream order; 128: tile t's tokens at rows t * 128 ..
 };
 int run_unpack(const UnpackParams& p, cudaStream_t stream);
 

@@ -13,11 +13,16 @@
 //     process exits. A call whose scratch does not fit returns DKV_ERR_SCRATCH and launches nothing.
 //     One conversation of 16K tokens of a Llama-3.2-3B-shaped model needs about 6 MiB per decode step.
 //   - the first call on a device looks the array's device address up (cudaGetSymbolAddress, with that
-//     device current) and caches it; make that first call before any stream capture.
+//     device current) and caches it with the device's current CUDA context; make that first call before
+//     any stream capture. After a cudaDeviceReset (or any new primary context) the module is loaded again,
+//     possibly at another address: the next call sees the new context and looks the address up again.
 //   - all calls share the array and it keeps the last call's contents. Every scratch byte the kernels
 //     read is written earlier in the same call, so nothing needs clearing between calls, but two calls
 //     that overlap on the GPU (different streams, or different host threads) race on it.
 #include <mutex>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
 
 #include "../../include/dimmer_kv.h"
 
@@ -30,6 +35,24 @@ __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_static_mutex;
 void* g_static_addr[kMaxDevices] = {};
+CUcontext g_static_ctx[kMaxDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The calling thread's current driver context (the runtime's primary context of the current device).
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 
 // Sizes saturate at kSizeCap, one byte more than the array: an overflowing product or sum reads as a
 // request that does not fit instead of wrapping to a small size.
@@ -38,15 +61,18 @@ size_t sat_mul(size_t a, size_t b) { return (a != 0 && b > kSizeCap / a) ? kSize
 size_t sat_add(size_t a, size_t b) { return a + b < kSizeCap ? a + b : kSizeCap; }
 size_t align256(size_t x) { return x >= kSizeCap ? kSizeCap : ((x + 255) & ~size_t(255)); }
 
-// Device address of the array on the current device (looked up once per device).
+// Device address of the array on the current device, looked up once per device and context.
 int static_scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DKV_ERR_CUDA;
+  void* ptr = nullptr;
+  // cudaGetSymbolAddress also makes the device's primary context current if none was yet.
   std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_addr[dev] == nullptr) {
-    void* ptr = nullptr;
+  CUcontext ctx = current_context();
+  if (g_static_addr[dev] == nullptr || ctx == nullptr || ctx != g_static_ctx[dev]) {
     if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr) return DKV_ERR_CUDA;
     g_static_addr[dev] = ptr;
+    g_static_ctx[dev] = current_context();
   }
   *out = g_static_addr[dev];
   return DKV_OK;

@@ -151,7 +151,8 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   const int n_valid = tile.n_tokens - row0;  // rows of this warp inside the tile (may be <= 0)
   uint8_t* stage = smem + S::kStage + warp * S::kStageWarp;
   const int64_t stride = p.out_cols * (BF16 ? 2 : 4);
-  uint8_t* out_base = reinterpret_cast<uint8_t*>(p.out) + (static_cast<int64_t>(tile.token_base) + row0) * stride +
+  const int64_t first_row = p.out_tile_rows > 0 ? static_cast<int64_t>(blockIdx.x) * p.out_tile_rows : tile.token_base;
+  uint8_t* out_base = reinterpret_cast<uint8_t*>(p.out) + (first_row + row0) * stride +
                       static_cast<int64_t>(h) * S::kHalfBytes;
   // Blocks arrive in the tile's order (ascending union group); the groups before each block and after
   // the last one are written as zeros.
@@ -215,6 +216,7 @@ int run_unpack(const UnpackParams& p, cudaStream_t stream) {
   if (p.n_tiles == 0) return kDkvOk;
   if (p.out_cols % 64 != 0 || p.out_cols <= 0) return kDkvErrArgs;
   if (reinterpret_cast<uintptr_t>(p.out) & 15u) return kDkvErrArgs;
+  if (p.out_tile_rows != 0 && p.out_tile_rows != kTileTokens) return kDkvErrArgs;
   const bool raw = p.max_planes <= 0 || p.max_planes > 8;
   if (p.out_bf16)
     return raw ? launch_unpack<true, true>(p, stream) : launch_unpack<true, false>(p, stream);

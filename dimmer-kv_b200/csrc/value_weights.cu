@@ -548,6 +548,12 @@ static int launch_vw(const ValueWeightParams& p, int grid, int smem, int a_slots
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
+int run_vprobs(const ValueWeightParams& p, cudaStream_t stream) {
+  if (p.n_tiles <= 0 || p.p_img == nullptr || (reinterpret_cast<uintptr_t>(p.p_img) & 15u)) return kDkvErrArgs;
+  vprobs_kernel<<<p.n_tiles, 256, p.n_rows_pad * 256, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream) {
   if (p.n_rows_pad % 16 != 0 || p.n_rows_pad < 16 || p.n_rows_pad > 128 || p.n_rows > p.n_rows_pad)
     return kDkvErrConfig;
@@ -563,9 +569,8 @@ int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream)
   if (smem > 232448) return kDkvErrConfig;
   if (p.p_img != nullptr) {
     // P^T images of every value tile for this call's rows, then the weighting that fetches them.
-    if (p.n_tiles <= 0 || (reinterpret_cast<uintptr_t>(p.p_img) & 15u)) return kDkvErrArgs;
-    vprobs_kernel<<<p.n_tiles, 256, p.n_rows_pad * 256, stream>>>(p);
-    if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
+    const int rc = run_vprobs(p, stream);
+    if (rc != kDkvOk) return rc;
     return raw ? launch_vw<true, true>(p, grid, smem, a_slots, stream) : launch_vw<false, true>(p, grid, smem, a_slots, stream);
   }
   return raw ? launch_vw<true, false>(p, grid, smem, a_slots, stream) : launch_vw<false, false>(p, grid, smem, a_slots, stream);

@@ -14,7 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libdimmerkv.so"
 
 DKV_OK = 0
 STATUS_TEXT = {0: "ok", 1: "invalid argument", 2: "unsupported configuration", 3: "CUDA error",
-               4: "tensor map encoding failed"}
+               4: "tensor map encoding failed", 5: "scratch larger than the static array of dkv_attend_layer_static"}
 DEVICE_ERRORS = {101: "timed out waiting for a plane block", 102: "timed out waiting for a basis tile",
                  103: "timed out waiting for an operand tile", 104: "timed out waiting for a free stage",
                  105: "timed out waiting for the accumulator", 106: "timed out waiting for TMEM to drain",
@@ -51,7 +51,7 @@ class AttendArgs(ctypes.Structure):
         ("vpart", c_void_p),
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
         ("k_pairs", c_void_p), ("k_pair_groups", c_void_p), ("softmax_mode", c_int32),
-        ("p_img", c_void_p), ("n_v_tiles", c_int32),
+        ("p_img", c_void_p), ("n_v_tiles", c_int32), ("v_dense", c_void_p),
     ]
 
 
@@ -61,7 +61,7 @@ class UnpackArgs(ctypes.Structure):
     _fields_ = [
         ("code", c_void_p), ("code_size", c_uint64), ("tiles", c_void_p), ("n_tiles", c_int32),
         ("groups", c_void_p), ("out", c_void_p), ("out_cols", c_int64), ("out_bf16", c_int32), ("status", c_void_p),
-        ("max_planes", c_int32),
+        ("max_planes", c_int32), ("out_tile_rows", c_int32),
     ]
 
 
@@ -163,6 +163,8 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = [ctypes.POINTER(AttendArgs), c_void_p]
             fn.restype = c_int32
+        handle.dkv_attend_layer_static.argtypes = [ctypes.POINTER(AttendArgs), c_int64, c_void_p]
+        handle.dkv_attend_layer_static.restype = c_int32
         handle.dkv_unpack.argtypes = [ctypes.POINTER(UnpackArgs), c_void_p]
         handle.dkv_unpack.restype = c_int32
         for name, st in (("dkv_importance", ImportanceArgs), ("dkv_topk", TopkArgs), ("dkv_refine_merge", RefineArgs),

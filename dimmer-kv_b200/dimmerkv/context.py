@@ -176,13 +176,16 @@ class CompressedBatch:
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
                  device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None,
-                 pair_keys: bool = True):
+                 pair_keys: bool = True, dense_values: bool = True):
         """``basis[kind]``: [F, F] (or [F, >= union]) float basis, columns = PCA components (the codec's
         ``stream.basis``); ``mean[kind]``: [F] shared or [n_conv, F] per conversation; ``cos/sin``:
         [positions, head_dim // 2] tables (``rope_tables``); ``union[kind]`` (optional) fixes the coefficient
         groups a stream covers (by default, the groups holding a plane for some token; a cold tier whose
         refined tokens use more groups needs them all); ``pair_keys`` runs the key kernel on CTA pairs
-        (two SMs per item, half the basis traffic each)."""
+        (two SMs per item, half the basis traffic each); ``dense_values`` decodes the value planes once per
+        decode step (at layer 0, dkv_unpack) into a tile-padded bf16 buffer of the value stream that every
+        layer's value stage streams with TMA, instead of decoding the planes again in every layer (the
+        coefficients are the same for all layers); it holds n_value_tiles * 128 * v_width bf16 values."""
         if dtype != torch.bfloat16:
             raise NotImplementedError("the sm_100a kernels of this build compute in bf16 only")
         self.lib = _lib.lib()
@@ -201,6 +204,7 @@ class CompressedBatch:
         self.keys: PackedStream = pack_streams([s[0] for s in streams], union.get("key"))
         self.values: PackedStream = pack_streams([s[1] for s in streams], union.get("value"))
         self.seq_m = torch.tensor([e - b for b, e in self.keys.seq_tokens], dtype=torch.int32, device=self.device)
+        self._seq_m_host = [e - b for b, e in self.keys.seq_tokens]  # the same lengths, kept on the host
 
         # Bases restricted to the union components, in the layouts the kernels read.
         kcols = (self.keys.union[:, None] * GROUP + torch.arange(GROUP, device=self.keys.union.device)).flatten()
@@ -233,6 +237,10 @@ class CompressedBatch:
         self._v_items_cache: dict[int, tuple] = {}
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.dense_values = dense_values
+        self._v_dense = None
+        self._v_dense_version = None
+        self._v_version = 0  # bumped whenever the value stream changes (refine, demote)
         self._poller = None
         self.poll_wait_s = 60.0  # bound of one host wait in poll_status
         self.timer = None  # optional callable(kind, fn) wrapping launches (used by the bench)
@@ -352,16 +360,49 @@ class CompressedBatch:
         self._v_items_cache[rows_pad] = out
         return out
 
+    def _dense_values(self, layer: int):
+        """The value coefficients decoded by dkv_unpack into the tile-padded bf16 buffer [n_tiles * 128,
+        v_width] (tile t's tokens at rows t * 128 .., the other rows zero): decoded at layer 0 of every decode
+        step and whenever the value stream changed since; None when disabled or without value tiles."""
+        vs = self.values
+        if not self.dense_values or vs.n_tiles == 0:
+            return None
+        rows = vs.n_tiles * 128
+        if self._v_dense is None or tuple(self._v_dense.shape) != (rows, self.v_width):
+            self._v_dense = torch.zeros(rows, self.v_width, dtype=torch.bfloat16, device=self.device)
+            self._v_dense_version = None
+        if layer == 0 or self._v_dense_version != self._v_version:
+            a = _lib.UnpackArgs(vs.code.data_ptr(), vs.code.numel(), vs.tiles.data_ptr(), vs.n_tiles,
+                                vs.groups.data_ptr(), self._v_dense.data_ptr(), self.v_width, 1,
+                                self.status.data_ptr(), vs.max_planes, 128)
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            launch = lambda: _lib.check(self.lib.dkv_unpack(a, stream), "dkv_unpack")
+            if self.timer is not None and hasattr(self.timer, "unpack"):
+                self.timer.unpack(launch)
+            else:
+                launch()
+            self._v_dense_version = self._v_version
+        return self._v_dense
+
+    def _score_offsets(self, q_len: int) -> tuple[torch.Tensor, int]:
+        """(per-conversation offsets into the score buffer on the device, total scores) for q_len rows per
+        head; computed from the host copy of the lengths."""
+        key = (q_len, tuple(self._seq_m_host))
+        if getattr(self, "_score_off", None) is None or self._score_off[0] != key:
+            counts = torch.tensor(self._seq_m_host, dtype=torch.int64) * self.q_heads * q_len
+            offsets = torch.cumsum(counts, 0) - counts
+            self._score_off = (key, offsets.to(self.device), int(counts.sum()))
+        return self._score_off[1], self._score_off[2]
+
     def _workspace(self, q_len: int, n_exact: int, rows_pad: int, n_v_items: int, item_groups: int):
         key = (q_len, n_exact, rows_pad, self.values.n_tiles)
         w = self._work.get(key)
         if w is None:
-            counts = (self.seq_m.to(torch.int64) * self.q_heads * q_len).cpu()
-            offsets = torch.cumsum(counts, 0) - counts
+            offsets, n_scores = self._score_offsets(q_len)
             rows = self.n_seq * self.q_heads * q_len
             w = {
-                "score_off": offsets.to(self.device),
-                "scores": torch.empty(max(1, int(counts.sum())), dtype=torch.float32, device=self.device),
+                "score_off": offsets,
+                "scores": torch.empty(max(1, n_scores), dtype=torch.float32, device=self.device),
                 "row_stats": torch.empty(max(1, rows * 4), dtype=torch.float32, device=self.device),
                 "p_exact": torch.empty(max(1, rows * max(1, n_exact)), dtype=torch.float32, device=self.device),
                 "partial": torch.empty(max(1, n_v_items * rows_pad * item_groups * GROUP), dtype=torch.float32,
@@ -378,12 +419,17 @@ class CompressedBatch:
 
     # ------------------------------------------------------------------ attention
     def args(self, layer: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
-             mask: torch.Tensor | None, scaling: float, out: torch.Tensor) -> _lib.AttendArgs:
+             mask: torch.Tensor | None, scaling: float, out: torch.Tensor, scratch: bool = True) -> _lib.AttendArgs:
+        """The C ABI arguments of one layer. ``scratch`` False leaves the scratch pointers null (for
+        dkv_attend_layer_static, whose scratch is the library's own array) and allocates no workspace."""
         q_len = query.shape[2]
         n_exact = key.shape[2]
         rows_pad = min(128, _round_up(self.q_heads * q_len, 16))
         v_items, v_seq, item_groups, n_v, v_spans, (v_cta, v_order) = self.value_items(rows_pad)
-        w = self._workspace(q_len, n_exact, rows_pad, n_v, item_groups)
+        if scratch:
+            w = self._workspace(q_len, n_exact, rows_pad, n_v, item_groups)
+        else:
+            w = {"score_off": self._score_offsets(q_len)[0]}
         a = _lib.AttendArgs()
         ks, vs = self.keys, self.values
         a.k_code, a.k_code_size = ks.code.data_ptr(), ks.code.numel()
@@ -403,14 +449,17 @@ class CompressedBatch:
         a.head_dim, a.q_len, a.scaling = self.head_dim, q_len, float(scaling)
         a.query, a.exact_k, a.exact_v, a.n_exact = query.data_ptr(), key.data_ptr(), value.data_ptr(), n_exact
         a.mask = mask.data_ptr() if mask is not None else None
-        a.scores, a.row_stats = w["scores"].data_ptr(), w["row_stats"].data_ptr()
-        a.p_exact, a.partial = w["p_exact"].data_ptr(), w["partial"].data_ptr()
+        ptr = lambda name: w[name].data_ptr() if name in w else None
+        a.scores, a.row_stats = ptr("scores"), ptr("row_stats")
+        a.p_exact, a.partial = ptr("p_exact"), ptr("partial")
         a.rows_pad, a.grid_k, a.grid_v = rows_pad, 0, 0
         a.out, a.out_f32, a.status = out.data_ptr(), int(out.dtype == torch.float32), self.status.data_ptr()
         a.k_max_planes, a.v_max_planes = ks.max_planes, vs.max_planes
         a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
-        a.vpart = w["vpart"].data_ptr()
-        a.p_img, a.n_v_tiles = w["p_img"].data_ptr(), vs.n_tiles
+        a.vpart = ptr("vpart")
+        a.p_img, a.n_v_tiles = ptr("p_img"), vs.n_tiles
+        dense = self._dense_values(layer) if scratch else None
+        a.v_dense = dense.data_ptr() if dense is not None else None
         a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
         a.k_pairs = self.k_pairs.data_ptr() if self.k_pairs is not None else None
         a.k_pair_groups = self.k_pair_groups.data_ptr() if self.k_pairs is not None else None
@@ -444,9 +493,34 @@ class CompressedBatch:
         self._keep = (query, key, value, mask, out, args)  # alive until the kernels have read them
         return out
 
+    def attend_layer_static(self, layer: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                            attention_mask: torch.Tensor | None, scaling: float, out: torch.Tensor) -> torch.Tensor:
+        """attend_layer through ``dkv_attend_layer_static``: the kernels' scratch is the library's fixed device
+        array, so this call allocates no workspace (for hosts whose device memory belongs to another
+        framework). ``out`` [B, q, Hq, D] (cache dtype or float32) is written; query / key / value must already
+        be contiguous in the cache dtype and the mask, if any, [B, q, E] float32. The score count the entry
+        point needs is computed from this batch's host copy of the conversation lengths."""
+        batch, q_heads, q_len, dim = query.shape
+        if batch != self.n_seq or q_heads != self.q_heads or dim != self.head_dim:
+            raise ValueError(f"query {tuple(query.shape)} does not match the batch")
+        for t in (query, key, value):
+            if t.dtype != self.dtype or not t.is_contiguous():
+                raise ValueError("query, key and value must be contiguous tensors of the cache dtype")
+        if out.shape != (batch, q_len, q_heads, dim) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous [B, q, Hq, D] tensor")
+        args = self.args(layer, query, key, value, attention_mask, scaling, out, scratch=False)
+        n_scores = self._score_offsets(q_len)[1]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self.lib.dkv_attend_layer_static(args, n_scores, stream), "dkv_attend_layer_static")
+        self._keep = (query, key, value, attention_mask, out, args)
+        return out
+
     def attend(self, module, query, key, value, attention_mask, scaling):
-        """Same contract as an HF attention function (and CompressedContext.attend): (output, None)."""
-        return self.attend_layer(module.layer_idx, query, key, value, attention_mask, scaling), None
+        """Same contract as an HF attention function (and CompressedContext.attend): (output, None). The output
+        takes the promoted type of the query and the cache dtype, as the reference's einsums give it
+        (compressed_attention.py:127-137): a float32 model gets float32 attention outputs."""
+        out_dtype = torch.promote_types(query.dtype, self.dtype)
+        return self.attend_layer(module.layer_idx, query, key, value, attention_mask, scaling, out_dtype=out_dtype), None
 
     def check_status(self) -> None:
         _lib.check_device_status(self.status)
@@ -707,11 +781,13 @@ class CompressedBatch:
                 tok += n
                 self.refined_tokens[s] += n
         self.seq_m = self.seq_m + torch.tensor(k_counts, dtype=torch.int32, device=self.device)
+        self._seq_m_host = [m + n for m, n in zip(self._seq_m_host, k_counts)]
         phases["append"] += clock() - t_mark
         t_mark = clock()
         self._rebuild_key_items()
         self._v_items_cache.clear()
         self._work = {}
+        self._v_version += 1
         phases["work_lists"] += clock() - t_mark
         self.last_refine_seconds = phases  # host wall time of the refine's phases
         self._score_cache = None
@@ -752,6 +828,7 @@ class CompressedBatch:
             self._v_items_cache.clear()
             self._work = {}
             self._score_cache = None
+            self._v_version += 1
         return before - (self.keys.code.numel() + self.values.code.numel())
 
     def _demote_stream(self, packed: PackedStream, drop_t: torch.Tensor) -> None:

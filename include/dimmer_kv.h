@@ -10,7 +10,12 @@
  *
  * The reference is Python and has no FFI of its own: each entry point below names the
  * reference function whose work it replaces. The Python host package (dimmerkv) binds
- * these symbols with ctypes; INTEGRATION.md shows the binding.
+ * these symbols with ctypes (dimmerkv/_lib.py).
+ *
+ * Kernels read `status` as they start and do no work while it is non-zero, so after a
+ * failure every later call that shares the word is inert until the caller clears it.
+ * Every wait inside a kernel is bounded (about two seconds); a wait that runs out records
+ * its code in `status` and the kernel leaves without touching the rest of its work.
  */
 #ifndef DIMMER_KV_H_
 #define DIMMER_KV_H_
@@ -131,6 +136,11 @@ typedef struct dkv_attend_args {
    * weighting kernel for every group range of the tile; NULL builds them inside the weighting kernel. */
   uint8_t* p_img;
   int32_t n_v_tiles;
+  /* Optional: the value coefficients decoded once per decode step by dkv_unpack (bf16, out_tile_rows = 128:
+   * [n_v_tiles * 128][v_width], tile t's tokens at rows t * 128 .., the other rows zero), 16-byte aligned.
+   * Given with p_img, the value stage streams them with TMA instead of decoding the planes again in every
+   * layer (the coefficients are the same for every layer); NULL decodes the planes in the value kernel. */
+  const void* v_dense;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
@@ -167,10 +177,14 @@ int dkv_finalize(const dkv_attend_args* args, void* stream);
  * cudaMalloc / cudaFree) or in latency-critical loops pass the same arguments as to
  * dkv_attend_layer except the scratch pointers (scores, row_stats, p_exact, partial, vpart, p_img), which are
  * ignored; the scratch comes from a fixed 32 MiB array declared by the library in device memory.
- * n_scores = sum over conversations of n_q_heads * q_len * seq_m[s]. Returns DKV_ERR_SCRATCH, having
- * launched nothing, when the scratch would not fit. The first call on a device looks up the array's
- * address and must come before any stream capture. Calls share the array: calls that overlap on the
- * GPU race. Allocates nothing. */
+ * n_scores = sum over conversations of n_q_heads * q_len * seq_m[s] (the score offsets seq_score_off the
+ * caller passes must lie inside it): the library cannot read seq_m without a device-to-host copy, and an
+ * n_scores below that sum lets the key kernel write past the scores region into the other scratch
+ * regions and, near the limit, past the array. The Python binding computes it from its own host copy
+ * (CompressedBatch.attend_layer_static). Returns DKV_ERR_SCRATCH, having launched nothing, when the
+ * scratch would not fit. The first call on a device (and the first after a device reset) looks up the
+ * array's address and must come before any stream capture. Calls share the array: calls that overlap on
+ * the GPU race. Allocates nothing. */
 int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_scores, void* stream);
 
 /* Ragged bit-plane unpack of a packed stream to dense coefficients (stream order).
@@ -189,6 +203,8 @@ typedef struct dkv_unpack_args {
   int32_t out_bf16;              /* 1: bf16 (the reference's .to(dtype)), 0: fp32 */
   int* status;
   int32_t max_planes;            /* largest plane count of any block (16: raw bf16 blocks); 0: unknown */
+  int32_t out_tile_rows;         /* 0: token rows in stream order; 128: tile t's tokens at rows t * 128 ..
+                                  * (rows past a tile's tokens are not written) */
 } dkv_unpack_args;
 int dkv_unpack(const dkv_unpack_args* args, void* stream);
 

@@ -2,7 +2,8 @@
 
 Usage (only where the reference checkout exists; the GPU box does not have it):
     DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py [fixture ...]
-(no names: every fixture; names such as ``encode``, ``codes``, ``storage`` or ``tiny``: only those).
+(no names: every fixture; names such as ``encode``, ``codes``, ``storage``, ``logits`` or ``tiny``: only
+those).
 
 Every array saved here is produced by the reference's own functions (scripts/progressive.py,
 scripts/kvtc.py, scripts/compressed_attention.py, scripts/dimmer.py, scripts/methods.py,
@@ -205,6 +206,36 @@ def geometry3b_fixture(out: Path) -> None:
     np.savez_compressed(out / "geometry3b.npz", **fixture)
 
 
+def logits_fixture(out: Path, methods, model, keys, values, scores, tokens: int) -> None:
+    """First-step logits and greedy replies of the reference's greedy_answer (compressed_attention.py:140-169)
+    over dkvtc@0.1:snap:floor1 codes, once in bf16 (model, cache and context, as tiny_dkvtc's greedy_direct)
+    and once in float32: the float32 run bounds the reference's own bf16 rounding for the logit tests."""
+    rng_state = torch.random.get_rng_state()  # building a model reseeds torch; later fixtures keep their draws
+    try:
+        name = "dkvtc@0.1:snap:floor1"
+        tok = types.SimpleNamespace(eos_token_id=-1, all_special_ids=[],
+                                    decode=lambda ids, skip_special_tokens=True: " ".join(map(str, ids)))
+        tail = tm.question_ids()
+        result = {"name": name, "tail": tail.numpy()}
+        with torch.inference_mode():
+            methods.apply(name, keys, values, scores)
+            codec = methods.codec("kvtc")
+            model32 = tm.build_model(torch.float32)
+            dimmer.install(model32)
+            for tag, dtype, m in (("bf16", torch.bfloat16, model), ("f32", torch.float32, model32)):
+                ctx = compressed_attention.CompressedContext(codec, [k.to(dtype) for k in keys],
+                                                             [v.to(dtype) for v in values], m, dtype=dtype)
+                exact = build_cache([l.keys.clone() for l in ctx.exact_cache.layers],
+                                    [l.values.clone() for l in ctx.exact_cache.layers], m)
+                text, logits = compressed_attention.greedy_answer(m, tok, ctx, exact, tail[None], tokens, 4,
+                                                                  stop_at_eos=False)
+                result[f"logits_{tag}"] = logits.float().numpy()
+                result[f"greedy_{tag}"] = np.array([int(x) for x in text.split()])
+        np.savez_compressed(out / "tiny_logits.npz", **result)
+    finally:
+        torch.random.set_rng_state(rng_state)
+
+
 def main() -> None:
     out = HERE
     torch.set_num_threads(min(8, os.cpu_count() or 1))
@@ -256,6 +287,8 @@ def main() -> None:
                       kvtc=tmp / "kvtc.pt", progressive=tmp / "progressive.pt")
     if not only or "storage" in only:
         storage_fixture(out, methods, keys, values, scores)
+    if not only or "logits" in only:
+        logits_fixture(out, methods, model, keys, values, scores, tokens)
     if only and "tiny" not in only:
         return
 

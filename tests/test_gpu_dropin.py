@@ -78,7 +78,16 @@ def test_prog_question_flow_on_codes(golden, tmp_path):
     top = ctx.select_top(0.05)
     count = int(fix["count"])
     assert np.array_equal(top.numpy(), np.sort(topk_lowest_index(imp[start:end], count) + start))
-    assert len(set(top.tolist()) & set(fix["top"].tolist())) >= count - 2
+    # The selection is exact on this build's importance (above: lowest-index ties). This build's importance
+    # sums fp32 scores of keys rebuilt in fp32, where the reference sums the scores of its bf16 hot cache
+    # (keys and q.k rounded to bf16, dimmer.py:52-75), so the two vectors agree to rtol 2e-3 (asserted above)
+    # and the two top sets may differ only at near-ties of the reference's own ranking: every token that one
+    # set holds and the other lacks sits within twice that tolerance of the reference's k-th value.
+    ref_imp = fix["importance"][start:end]
+    kth = float(np.sort(ref_imp)[::-1][count - 1])
+    differing = set(top.tolist()) ^ set(fix["top"].tolist())
+    for t in differing:
+        assert abs(float(ref_imp[t - start]) - kth) <= 2 * (2e-3 * abs(kth) + 1e-5), (t, ref_imp[t - start], kth)
     fetched = ctx.refine(top)
     assert fetched == codec.last_cache.fetched_bytes(top)
     torch.cuda.synchronize()

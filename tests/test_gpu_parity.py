@@ -202,10 +202,11 @@ def test_ragged_batch_matches_oracle_per_conversation():
             assert err < TOL_F32, (layer, s, err)
 
 
-def _check_3b_geometry(shapes, q, seed):
+def _check_3b_geometry(shapes, q, seed, dense=True):
     """Conversations of the given (middle tokens, groups) at the bench's attention geometry (Llama-3.2-3B:
     8 KV heads of 128, 24 query heads, GQA 3), one launch per layer, q query rows, each conversation
-    against the oracle."""
+    against the oracle. ``dense``: the value stage reads the coefficients decoded once per step
+    (value_dense.cu) or decodes the planes itself (value_weights.cu)."""
     rng = np.random.default_rng(seed)
     L, H, D, HQ = 2, 8, 128, 24
     F = L * H * D
@@ -228,7 +229,7 @@ def _check_3b_geometry(shapes, q, seed):
         convs.append(ConversationCodes(4, 4 + n_mid, toks["key"], toks["value"]))
         raw.append(c)
     batch = CompressedBatch(convs, layers=L, kv_heads=H, head_dim=D, q_heads=HQ, basis=basis, mean=mean,
-                            cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV)
+                            cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV, dense_values=dense)
     S, E = len(shapes), 40
     query = torch.randn(S, HQ, q, D, generator=g).to(torch.bfloat16)
     ek = torch.randn(S, H, E, D, generator=g).to(torch.bfloat16)
@@ -252,11 +253,12 @@ def _check_3b_geometry(shapes, q, seed):
             assert err < TOL_F32, (layer, s, err)
 
 
+@pytest.mark.parametrize("dense", [True, False], ids=["dense_values", "decoding_values"])
 @pytest.mark.parametrize("q", [1, 4])
-def test_ragged_batch_3b_geometry_matches_oracle(q):
+def test_ragged_batch_3b_geometry_matches_oracle(q, dense):
     """Four ragged conversations in one launch: up to 2100 middle tokens (an odd number of tiles, so one
-    CTA pair holds a single tile) and 16 coefficient groups."""
-    _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), q, 11 + q)
+    CTA pair holds a single tile) and 16 coefficient groups; both value kernels."""
+    _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), q, 11 + q, dense)
 
 
 @pytest.mark.parametrize("q", [1, 4])
