@@ -32,14 +32,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Basis tensor maps, cached by (address, rows, width, box rows).
+// 2-D tensor maps of 16-bit row-major matrices (bases, decoded coefficients), cached by (address, rows,
+// width, box rows, dtype).
 std::mutex g_map_mutex;
-std::map<std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t>, CUtensorMap> g_maps;
+std::map<std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, int>, CUtensorMap> g_maps;
 
-int basis_map(const void* basis, uint64_t rows, uint64_t width, uint32_t box_rows, CUtensorMap* out) {
+int basis_map(const void* basis, uint64_t rows, uint64_t width, uint32_t box_rows, CUtensorMap* out, int f16 = 0) {
   if (basis == nullptr || rows == 0 || width == 0 || width % 64 != 0) return DKV_ERR_ARGS;
   if (reinterpret_cast<uintptr_t>(basis) % 16 != 0) return DKV_ERR_ARGS;
-  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(basis), rows, width, box_rows);
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(basis), rows, width, box_rows, f16 ? 1 : 0);
   std::lock_guard<std::mutex> lock(g_map_mutex);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
@@ -53,7 +54,8 @@ int basis_map(const void* basis, uint64_t rows, uint64_t width, uint32_t box_row
   cuuint64_t gstride[1] = {width * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(basis), gdim, gstride, box, estride,
+  CUresult r = fn(&map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(basis), gdim, gstride, box, estride,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return DKV_ERR_TENSORMAP;
@@ -108,9 +110,10 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   const bool pairs = a->k_pairs != nullptr;
   if ((nb != 128 && nb != 256 && nb != 512) || n_cols % nb != 0 || nb % a->head_dim != 0) return DKV_ERR_CONFIG;
   if (pairs && nb != 512) return DKV_ERR_CONFIG;  // CTA pairs: 512 columns per item, 128-row basis boxes
+  if (a->fp16 && !pairs) return DKV_ERR_CONFIG;  // fp16 operands: the CTA-pair kernel only
   CUtensorMap map;
   rc = basis_map(a->k_basis, static_cast<uint64_t>(a->n_layers) * n_cols, static_cast<uint64_t>(a->k_width),
-                 pairs ? 128u : (nb > 256 ? 256u : static_cast<uint32_t>(nb)), &map);
+                 pairs ? 128u : (nb > 256 ? 256u : static_cast<uint32_t>(nb)), &map, a->fp16);
   if (rc != DKV_OK) return rc;
   dkv::KeyScoreParams p{};
   p.code = a->k_code;
@@ -141,6 +144,7 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   p.status = a->status;
   p.cta_begin = a->k_cta_begin;
   p.item_order = a->k_item_order;
+  p.f16 = a->fp16 ? 1 : 0;
   if ((a->k_item_order != nullptr && a->k_cta_begin == nullptr) || (a->k_cta_begin != nullptr && a->grid_k <= 0))
     return DKV_ERR_ARGS;
   p.pairs = a->k_pairs;
@@ -182,6 +186,7 @@ int dkv_softmax_stats(const dkv_attend_args* a, void* stream) {
   p.scratch_floats = a->partial != nullptr ? static_cast<int64_t>(a->n_v_items) * a->rows_pad * a->v_item_groups * 64 : 0;
   p.n_sms = sm_count();
   p.status = a->status;
+  p.f16 = a->fp16 ? 1 : 0;
   return dkv::run_softmax_stats(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -213,6 +218,7 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
   p.item_order = a->v_item_order;
   p.p_img = a->p_img;
   p.n_tiles = a->n_v_tiles;
+  p.f16 = a->fp16 ? 1 : 0;
   if ((a->v_item_order != nullptr && a->v_cta_begin == nullptr) || (a->v_cta_begin != nullptr && a->grid_v <= 0))
     return DKV_ERR_ARGS;
   const int grid = a->grid_v > 0 ? a->grid_v : (a->n_v_items < sm_count() ? a->n_v_items : sm_count());
@@ -220,7 +226,7 @@ static int value_weights_rows(const dkv_attend_args* a, int row_begin, int n_row
     // Coefficients decoded once per step: TMA boxes of 64 components x 128 token rows.
     CUtensorMap map;
     const int rc = basis_map(a->v_dense, static_cast<uint64_t>(a->n_v_tiles) * 128, static_cast<uint64_t>(a->v_width),
-                             128u, &map);
+                             128u, &map, a->fp16);
     if (rc != DKV_OK) return rc;
     return dkv::run_value_dense(map, p, grid, static_cast<cudaStream_t>(stream));
   }
@@ -255,6 +261,7 @@ static int finalize_rows(const dkv_attend_args* a, int row_begin, int n_rows, vo
   p.out_f32 = a->out_f32;
   p.vpart = a->vpart;
   p.status = a->status;
+  p.f16 = a->fp16 ? 1 : 0;
   if (a->vpart == nullptr) return DKV_ERR_ARGS;
   return dkv::run_finalize(p, static_cast<cudaStream_t>(stream));
 }
@@ -384,6 +391,7 @@ int dkv_unpack(const dkv_unpack_args* a, void* stream) {
   p.max_planes = a->max_planes;
   p.status = a->status;
   p.out_tile_rows = a->out_tile_rows;
+  p.f16 = a->f16 ? 1 : 0;
   return dkv::run_unpack(p, static_cast<cudaStream_t>(stream));
 }
 

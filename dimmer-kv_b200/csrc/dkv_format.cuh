@@ -121,6 +121,47 @@ struct ItemRange {
   }
 };
 
+// ---------------------------------------------------------------- the cache dtype (bf16 or fp16)
+// The kernels read and write 16-bit operands in the cache dtype of the call: bf16 (F16 = false) or fp16
+// (F16 = true, the reference's default CompressedContext dtype). Values are kept as raw 16-bit patterns.
+template <bool F16>
+__device__ __forceinline__ float half_to_float(uint16_t bits) {
+  if constexpr (F16) return __half2float(__ushort_as_half(bits));
+  else return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+}
+// Two packed 16-bit values (low half first) -> float2.
+template <bool F16>
+__device__ __forceinline__ float2 half2_to_float2(uint32_t bits) {
+  if constexpr (F16) {
+    const __half2 h = *reinterpret_cast<const __half2*>(&bits);
+    return __half22float2(h);
+  } else {
+    return make_float2(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u));
+  }
+}
+// Round to nearest even in the cache dtype; returns the 16-bit pattern.
+template <bool F16>
+__device__ __forceinline__ uint16_t float_to_half(float x) {
+  if constexpr (F16) return __half_as_ushort(__float2half_rn(x));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+// Two floats rounded to the cache dtype, packed (a in the low half).
+template <bool F16>
+__device__ __forceinline__ uint32_t float2_to_half2(float a, float b) {
+  if constexpr (F16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+// x rounded to the cache dtype, as a float (the reference's .to(dtype)).
+template <bool F16>
+__device__ __forceinline__ float round_half(float x) {
+  return half_to_float<F16>(float_to_half<F16>(x));
+}
+
 // Byte j (0..15, runtime) of the 'first' table.
 __device__ __forceinline__ uint32_t first_at(const GroupRegs& g, int j) {
   const uint32_t lo = (j & 4) ? g.first4[1] : g.first4[0];
@@ -205,13 +246,16 @@ __device__ __forceinline__ int gather_index(const uint8_t* blk, const GroupRegs&
 }
 
 // Decode 32 components (half h of the 64-component group) of token r from a block that starts
-// at `blk` (shared or global memory). `out` receives 16 packed bf16x2 words (components 32h..32h+31).
+// at `blk` (shared or global memory). `out` receives 16 packed words of two values in the cache dtype
+// (bf16, or fp16 with F16; components 32h..32h+31). Raw blocks (m == 16) hold the 16-bit pattern of the
+// cache dtype itself and are passed through.
 // Only the token's own planes are visited. The value is the reference's float32 arithmetic then
 // rounded to bf16 (the reference's .to(dtype), compressed_attention.py:76):
 //   progressive (idx + 0.5) * mult / 2^m + low, ladder idx * mult + low.
 // For m <= 8 the product is exact in float32 ((idx + 0.5) has at most 9 significant bits and
 // mult / 2^m at most 11, an f16 value scaled by a power of two), so one fused multiply-add rounds
 // exactly once, like the reference's separate multiply (exact) and add.
+template <bool F16 = false>
 __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs& g, int n_tokens, int r, int h,
                                             uint32_t (&out)[16]) {
   uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -245,9 +289,7 @@ __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs&
     float t[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) t[i] = __fmaf_rn(__fsub_rn(8388608.0f + i, bias), scale, low);
-    __nv_bfloat162 v01 = __floats2bfloat162_rn(t[0], t[1]);
-    __nv_bfloat162 v23 = __floats2bfloat162_rn(t[2], t[3]);
-    const uint32_t tlo = *reinterpret_cast<uint32_t*>(&v01), thi = *reinterpret_cast<uint32_t*>(&v23);
+    const uint32_t tlo = float2_to_half2<F16>(t[0], t[1]), thi = float2_to_half2<F16>(t[2], t[3]);
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
       const uint32_t sel = acc[b] * 34u + 0x10101010u;
@@ -264,14 +306,14 @@ __device__ __forceinline__ void decode_half(const uint8_t* blk, const GroupRegs&
       const float x = __uint_as_float(__byte_perm(acc[b], 0x4B000000u, 0x7440u | k));
       v[k] = __fmaf_rn(__fsub_rn(x, bias), scale, low);
     }
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
-    out[2 * b] = *reinterpret_cast<uint32_t*>(&p0);
-    out[2 * b + 1] = *reinterpret_cast<uint32_t*>(&p1);
+    out[2 * b] = float2_to_half2<F16>(v[0], v[1]);
+    out[2 * b + 1] = float2_to_half2<F16>(v[2], v[3]);
   }
 }
 
-// float32 variant of the decoder (used by the standalone unpack kernel).
+// float32 variant of the decoder (used by the standalone unpack kernel). F16: raw blocks hold fp16
+// patterns (a stream packed for an fp16 cache) instead of bf16.
+template <bool F16 = false>
 __device__ __forceinline__ void decode_half_f32(const uint8_t* blk, const GroupRegs& g, int n_tokens, int r, int h,
                                                 float (&out)[32]) {
   uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -280,12 +322,13 @@ __device__ __forceinline__ void decode_half_f32(const uint8_t* blk, const GroupR
   if (m == 0 || m == kMaxPlanes) {
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      // Raw bf16 widened to float32 (zero when there are no planes: acc and lo are zero).
+      // Raw 16-bit values widened to float32 (zero when there are no planes: acc and lo are zero).
       const uint32_t p0 = __byte_perm(lo[b], acc[b], 0x5140), p1 = __byte_perm(lo[b], acc[b], 0x7362);
-      out[4 * b] = __uint_as_float(p0 << 16);
-      out[4 * b + 1] = __uint_as_float(p0 & 0xFFFF0000u);
-      out[4 * b + 2] = __uint_as_float(p1 << 16);
-      out[4 * b + 3] = __uint_as_float(p1 & 0xFFFF0000u);
+      const float2 a = half2_to_float2<F16>(p0), c = half2_to_float2<F16>(p1);
+      out[4 * b] = a.x;
+      out[4 * b + 1] = a.y;
+      out[4 * b + 2] = c.x;
+      out[4 * b + 3] = c.y;
     }
     return;
   }

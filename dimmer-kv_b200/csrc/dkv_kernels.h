@@ -44,6 +44,7 @@ struct KeyScoreParams {
   int* status;
   const int32_t* cta_begin;       // optional static schedule (see ValueWeightParams)
   const int32_t* item_order;
+  int f16;                        // 16-bit operands (query, mean, cos / sin, basis, codes' raw values) are fp16, not bf16
   const int32_t* pairs;           // CTA-pair kernel: [n_pairs][4] = tile 0, tile 1 (-1: none), merged groups,
                                   // first pair_groups entry; items = pair * (n_cols / 512) + column block
   const int32_t* pair_groups;     // [entries][4] = union group, descriptor of tile 0, of tile 1 (-1: none), 0
@@ -68,6 +69,7 @@ struct SoftmaxParams {
   int64_t scratch_floats;
   int n_sms;                      // SMs of the device (sizes the slices)
   const int* status;              // the call's status word (read at entry: non-zero means no work)
+  int f16;                        // query and exact keys are fp16 (else bf16); probabilities round to that dtype
 };
 constexpr int kSoftmaxFull = 0;
 constexpr int kSoftmaxLocal = 1;   // row_stats <- (max, sum of exponentials) of this shard
@@ -99,6 +101,7 @@ struct ValueWeightParams {
   const int32_t* item_order;
   uint8_t* p_img;                 // optional [n_tiles][2][n_rows_pad][128 B]: P^T images (vprobs_kernel)
   int n_tiles;                    // value tiles (with p_img)
+  int f16;                        // probabilities and coefficients in fp16 (else bf16)
 };
 int run_value_weights(const ValueWeightParams& p, int grid, cudaStream_t stream);
 // P^T images of every value tile (vprobs_kernel), used by both value kernels.
@@ -126,6 +129,7 @@ struct FinalizeParams {
   int out_f32;                    // fp32 output instead of bf16
   float* vpart;                   // [finalize_chunks(r_v)][n_seq][n_rows_pad][head_dim]
   int* status;
+  int f16;                        // 16-bit operands and output in fp16 (else bf16)
 };
 int finalize_chunks(int r_v);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);
@@ -211,6 +215,7 @@ struct UnpackParams {
   int max_planes;                 // 0: unknown (slots sized for raw blocks)
   int* status;
   int out_tile_rows;              // 0: rows in stream order; 128: tile t's tokens at rows t * 128 ..
+  int f16;                        // 16-bit output (and raw blocks) in fp16 instead of bf16
 };
 int run_unpack(const UnpackParams& p, cudaStream_t stream);
 

@@ -29,17 +29,25 @@ enum DeviceError : int {
   kErrWaitDrain = 107,     // exit path waiting for outstanding async work
   kErrBadDescriptor = 110, // a tile / group descriptor failed its bounds check
 };
+// The kernel that recorded an error, added to the code (the host names it): status = site + error.
+constexpr int kSiteKeyPair = 1000;     // key_scores_pair_kernel (CTA pairs)
+constexpr int kSiteKey = 2000;         // key_scores_kernel (one CTA per item)
+constexpr int kSiteValue = 3000;       // value_weights_kernel / vprobs_kernel (planes decoded per layer)
+constexpr int kSiteValueDense = 4000;  // value_dense_kernel (coefficients decoded once per step)
+constexpr int kSiteUnpack = 5000;      // unpack_kernel
 
-// Bound on one wait. Healthy waits in these kernels last microseconds. A wait gives up only when
-// BOTH clocks say that more than the deadline has passed and it has polled at least kWaitMinPolls
-// times: %globaltimer follows the host's clock (a time step on the host moves it), and %clock64 is
-// the cycle counter of the SM the thread runs on (a context switch can resume the CTA on another
-// SM), so neither alone can end a healthy wait early. A clock seen running backwards restarts its
-// measurement. 2e9 cycles is 1.02 s at the B200's 1965 MHz maximum SM clock, longer at lower clocks.
-// Both clocks are kept in units of 1024 (ns, cycles) modulo 2^32, which wraps after 73 minutes.
+// Bound on one wait. Healthy waits in these kernels last microseconds. A wait gives up when both clocks
+// say that more than the deadline has passed: %globaltimer follows the host's clock (a time step on the
+// host moves it), and %clock64 is the cycle counter of the SM the thread runs on (a context switch can
+// resume the CTA on another SM), so neither alone can end a healthy wait early; a clock seen running
+// backwards restarts its measurement. 2e9 cycles is 1.02 s at the B200's 1965 MHz maximum SM clock.
+// Whatever %globaltimer does, a wait also ends after 6e10 cycles (about 30 s at the maximum clock).
+// The clocks are read at every poll: one mbarrier.try_wait may itself suspend the thread for a
+// hardware-defined time, so a bound counted in polls would not be a bound in time. Both clocks are kept
+// in units of 1024 (ns, cycles) modulo 2^32, which wraps after 73 minutes.
 constexpr uint32_t kWaitDeadlineNs1024 = 2000000000u / 1024u;
 constexpr uint32_t kWaitDeadlineCycles1024 = 2000000000u / 1024u;
-constexpr uint32_t kWaitMinPolls = 1u << 16;
+constexpr uint32_t kWaitHardCycles1024 = static_cast<uint32_t>(60000000000ull / 1024u);
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -55,16 +63,16 @@ __device__ __forceinline__ uint64_t sm_cycles() {
 
 // Elapsed-time bookkeeping of one bounded wait (started after its first unsuccessful poll).
 struct WaitClock {
-  uint32_t t0, c0, polls;
+  uint32_t t0, c0;
   __device__ __forceinline__ WaitClock()
-      : t0(static_cast<uint32_t>(global_ns() >> 10)), c0(static_cast<uint32_t>(sm_cycles() >> 10)), polls(0) {}
-  // Counts one poll; true once the wait has run out.
+      : t0(static_cast<uint32_t>(global_ns() >> 10)), c0(static_cast<uint32_t>(sm_cycles() >> 10)) {}
+  // True once the wait has run out.
   __device__ __forceinline__ bool expired() {
-    if ((++polls & 63u) != 0u) return false;
     const uint32_t t = static_cast<uint32_t>(global_ns() >> 10), c = static_cast<uint32_t>(sm_cycles() >> 10);
     if (static_cast<int32_t>(t - t0) < 0) t0 = t;
     if (static_cast<int32_t>(c - c0) < 0) c0 = c;
-    return polls >= kWaitMinPolls && t - t0 > kWaitDeadlineNs1024 && c - c0 > kWaitDeadlineCycles1024;
+    const uint32_t dc = c - c0;
+    return (t - t0 > kWaitDeadlineNs1024 && dc > kWaitDeadlineCycles1024) || dc > kWaitHardCycles1024;
   }
 };
 

@@ -14,6 +14,7 @@
 //             tokens, and writes the HF layout [batch, q_len, q_heads, head_dim].
 #include "dkv_kernels.h"
 #include "dkv_ptx.cuh"
+#include "dkv_format.cuh"
 
 namespace dkv {
 
@@ -45,19 +46,17 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
   const int rhi = min(head_hi, rlo + row_block);
   const int nr = rhi - rlo;
   if (nr <= 0 || n_s <= 0) return;
-  __nv_bfloat162* bs = reinterpret_cast<__nv_bfloat162*>(smem_f);  // [kRChunk][D/2]
+  uint32_t* bs = reinterpret_cast<uint32_t*>(smem_f);  // [kRChunk][D/2] pairs of 16-bit basis values
   float* ws = smem_f + kRChunk * D2;                                // [n_s][nr][kRChunk]
   const int tid = threadIdx.x;
   const int item_cols = p.item_groups * 64;
 
   // Basis slice of this KV head: rows r0 .. r0+127 of [layer][r_v][n_cols], columns kvh*D .. +D.
-  const __nv_bfloat162* bsrc =
-      reinterpret_cast<const __nv_bfloat162*>(p.basis_v + static_cast<int64_t>(p.layer) * p.r_v * p.n_cols) +
-      kvh * D2;
+  const uint32_t* bsrc =
+      reinterpret_cast<const uint32_t*>(p.basis_v + static_cast<int64_t>(p.layer) * p.r_v * p.n_cols) + kvh * D2;
   for (int i = tid; i < kRChunk * D2; i += kFinalizeThreads) {
     const int r = i / D2, dp = i % D2;
-    bs[i] = (r0 + r < p.r_v) ? bsrc[static_cast<int64_t>(r0 + r) * (p.n_cols / 2) + dp]
-                             : __floats2bfloat162_rn(0.f, 0.f);
+    bs[i] = (r0 + r < p.r_v) ? bsrc[static_cast<int64_t>(r0 + r) * (p.n_cols / 2) + dp] : 0u;  // +0.0 in both
   }
   // Weighted coefficients of the block's conversations. First the items of each conversation that cover
   // this chunk (in item order), then every element sums them with independent loads.
@@ -113,11 +112,20 @@ __global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const Finalize
   for (int j = rg; j < n_s * nr; j += n_rg) {
     const float* w = ws + j * kRChunk;
     float ax = 0.f, ay = 0.f;
+    if (p.f16) {
 #pragma unroll 8
-    for (int c = 0; c < kRChunk; ++c) {
-      const float2 b = __bfloat1622float2(bs[c * D2 + dp]);
-      ax = fmaf(w[c], b.x, ax);
-      ay = fmaf(w[c], b.y, ay);
+      for (int c = 0; c < kRChunk; ++c) {
+        const float2 b = half2_to_float2<true>(bs[c * D2 + dp]);
+        ax = fmaf(w[c], b.x, ax);
+        ay = fmaf(w[c], b.y, ay);
+      }
+    } else {
+#pragma unroll 8
+      for (int c = 0; c < kRChunk; ++c) {
+        const float2 b = half2_to_float2<false>(bs[c * D2 + dp]);
+        ax = fmaf(w[c], b.x, ax);
+        ay = fmaf(w[c], b.y, ay);
+      }
     }
     const int s = s0 + j / nr, rr = j % nr;
     float2* dst = reinterpret_cast<float2*>(
@@ -155,30 +163,39 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Finalize
     for (; ch < n_chunks; ++ch) tail += vp[ch * cstride];
     float o = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7])) + tail;
     const int64_t srow = (static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi;
-    const float mean = __bfloat162float(
-        p.mean_v[static_cast<int64_t>(s) * p.mean_seq_stride + static_cast<int64_t>(p.layer) * p.n_cols + kvh * D + d]);
+    const uint16_t mbits = reinterpret_cast<const uint16_t*>(
+        p.mean_v)[static_cast<int64_t>(s) * p.mean_seq_stride + static_cast<int64_t>(p.layer) * p.n_cols + kvh * D + d];
+    const float mean = p.f16 ? half_to_float<true>(mbits) : half_to_float<false>(mbits);
     o += mean * p.row_stats[srow * 4 + 2];
     // Exact probabilities are kept unrounded (question-time scoring sums them); the value product uses
     // them rounded to the cache dtype, as the reference does (compressed_attention.py:128, 135).
     const float* pe = p.p_exact + srow * p.n_exact;
-    const __nv_bfloat16* vex = p.exact_v + (static_cast<int64_t>(s) * n_kv + kvh) * p.n_exact * D + d;
+    const uint16_t* vex = reinterpret_cast<const uint16_t*>(p.exact_v) + (static_cast<int64_t>(s) * n_kv + kvh) * p.n_exact * D + d;
     float ex[4] = {0.f, 0.f, 0.f, 0.f};
-    int e = 0;
-    for (; e + 4 <= p.n_exact; e += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        ex[u] += __bfloat162float(__float2bfloat16_rn(pe[e + u])) *
-                 __bfloat162float(vex[static_cast<int64_t>(e + u) * D]);
-    }
     float ex_tail = 0.f;
-    for (; e < p.n_exact; ++e)
-      ex_tail += __bfloat162float(__float2bfloat16_rn(pe[e])) * __bfloat162float(vex[static_cast<int64_t>(e) * D]);
+    int e = 0;
+    if (p.f16) {
+      for (; e + 4 <= p.n_exact; e += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          ex[u] += round_half<true>(pe[e + u]) * half_to_float<true>(vex[static_cast<int64_t>(e + u) * D]);
+      }
+      for (; e < p.n_exact; ++e) ex_tail += round_half<true>(pe[e]) * half_to_float<true>(vex[static_cast<int64_t>(e) * D]);
+    } else {
+      for (; e + 4 <= p.n_exact; e += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          ex[u] += round_half<false>(pe[e + u]) * half_to_float<false>(vex[static_cast<int64_t>(e + u) * D]);
+      }
+      for (; e < p.n_exact; ++e)
+        ex_tail += round_half<false>(pe[e]) * half_to_float<false>(vex[static_cast<int64_t>(e) * D]);
+    }
     o += ((ex[0] + ex[1]) + (ex[2] + ex[3])) + ex_tail;
     const int64_t oi = ((static_cast<int64_t>(s) * p.q_len + qi) * p.n_q_heads + hq) * D + d;
     if (p.out_f32)
       static_cast<float*>(p.out)[oi] = o;
     else
-      static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
+      static_cast<uint16_t*>(p.out)[oi] = p.f16 ? float_to_half<true>(o) : float_to_half<false>(o);
   }
 }
 

@@ -59,7 +59,7 @@ struct GroupCursor {
     while (k < ir.end) {
       const int it = ir.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteKey + kErrBadDescriptor);
         k = ir.end;
         return;
       }
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const GroupRegs gr = load_group(gd);
             if (gr.code_bytes > static_cast<uint32_t>(kCodeSlot - 32) ||
                 static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size || gr.group >= p.n_union_groups) {
-              record_error(p.status, kErrBadDescriptor);
+              record_error(p.status, kSiteKey + kErrBadDescriptor);
               *abort_flag = 1;
               break;
             }
@@ -201,18 +201,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           idle = WaitClock();
           idling = true;
         } else if (idle.expired()) {
-          record_error(p.status, kErrWaitEmpty);
+          record_error(p.status, kSiteKey + kErrWaitEmpty);
           *abort_flag = 1;
         }
       }
       // Drain: every copy this producer issued has landed before the CTA can leave.
       for (int s = 0; s < kStagesC && s < static_cast<int>(c_iter); ++s) {
         const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kStagesC);
-        mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kSiteKey + kErrWaitDrain);
       }
       for (int s = 0; s < kStagesB && s < static_cast<int>(b_iter); ++s) {
         const uint32_t last = b_iter - 1 - ((b_iter - 1 - s) % kStagesB);
-        mbar_wait(&b_full[s], (last / kStagesB) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&b_full[s], (last / kStagesB) & 1, p.status, kSiteKey + kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -222,13 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteKey + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
         const int item = p.items[it];
         const TileDesc tile = p.tiles[item / nblocks];
-        if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
+        if (item_iter > 0 && !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kSiteKey + kErrWaitAccumFree, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -236,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int gi = 0; gi < tile.n_groups; ++gi) {
           const int sa = a_iter % kStagesA, sb = b_iter % kStagesB;
-          if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA, abort_flag) ||
-              !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
+          if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kSiteKey + kErrWaitA, abort_flag) ||
+              !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kSiteKey + kErrWaitBasis, abort_flag)) {
             ok = false;
             break;
           }
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Also on an early exit: no MMA may still read shared memory or TMEM past this point.
       if (a_iter > 0) {
         mma_commit(mma_done);
-        mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+        mbar_wait(mma_done, 0, p.status, kSiteKey + kErrWaitDrain);
       }
     }
   } else if (warp >= 2 && warp < 10) {
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteKey + kErrBadDescriptor);
         *abort_flag = 1;
         break;
       }
@@ -289,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int gi = 0; gi < tile.n_groups; ++gi) {
         const int cs = c_iter % kStagesC;
         const int sa = a_iter % kStagesA;
-        if (!warp_wait(&code_full[cs], (c_iter / kStagesC) & 1, p.status, kErrWaitCodes, abort_flag)) {
+        if (!warp_wait(&code_full[cs], (c_iter / kStagesC) & 1, p.status, kSiteKey + kErrWaitCodes, abort_flag)) {
           *abort_flag = 1;
           break;
         }
         if (a_iter >= kStagesA &&
-            !warp_wait(&a_empty[sa], ((a_iter / kStagesA) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+            !warp_wait(&a_empty[sa], ((a_iter / kStagesA) - 1) & 1, p.status, kSiteKey + kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int k = items.k; k < items.end && !failed && !*abort_flag; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteKey + kErrBadDescriptor);
         *abort_flag = 1;
         break;
       }
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pos = hidden ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
       const __nv_bfloat16* cosrow = p.cos_t + static_cast<int64_t>(pos) * (D / 2);
       const __nv_bfloat16* sinrow = p.sin_t + static_cast<int64_t>(pos) * (D / 2);
-      if (!warp_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum, abort_flag)) {
+      if (!warp_wait(accum_full, item_iter & 1, p.status, kSiteKey + kErrWaitAccum, abort_flag)) {
         *abort_flag = 1;
         break;
       }
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* out_base = p.scores + p.seq_score_off[s];
       const int kv0 = nblk * kHeads;
       for (int qi = 0; qi < p.q_len; ++qi) {
-        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+        if (!group_sync(ep_sync, n_sync, p.status, kSiteKey + kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           failed = true;
           break;
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       static_cast<int64_t>(p.layer) * p.n_cols + nblk * NB;
           for (int i = et; i < NB; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
         }
-        if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+        if (!group_sync(ep_sync, n_sync, p.status, kSiteKey + kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           failed = true;
           break;

@@ -87,7 +87,7 @@ struct PairCursor {
     while (k < ir.end) {
       const int it = ir.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteKeyPair + kErrBadDescriptor);
         k = ir.end;
         break;
       }
@@ -126,12 +126,12 @@ constexpr uint32_t kStashEnd = 1u;  // no more groups for this CTA
 
 }  // namespace
 
-template <int D, int G, bool RAW>
+template <int D, int G, bool RAW, bool F16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     key_scores_pair_kernel(const __grid_constant__ CUtensorMap bmap, const KeyScoreParams p) {
   constexpr int kHeads = kPairCols / D;     // KV heads per item
   constexpr int kHalfHeads = kHeads / 2;    // heads per epilogue half
-  constexpr uint32_t kIdesc = idesc_f16(256, kMmaN, true, false, false);
+  constexpr uint32_t kIdesc = idesc_f16(256, kMmaN, /*is_bf16=*/!F16, false, false);
   using L = PairSmem<RAW>;
   constexpr int kStagesA = L::kStagesA;
   constexpr int kStagesB = L::kStagesB;
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       while (!c_ended && !*abort_flag) {
         const int cs = c_iter % kStagesC;
         if (c_iter >= kStagesC &&
-            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kSiteKeyPair + kErrWaitEmpty, abort_flag)) {
           give_up();
           break;
         }
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (gr.code_bytes > static_cast<uint32_t>(kCodeSlot - 32) ||
               static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size ||
               gr.group >= p.n_union_groups) {
-            record_error(p.status, kErrBadDescriptor);
+            record_error(p.status, kSiteKeyPair + kErrBadDescriptor);
             give_up();
             break;
           }
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int e = 0; e < 2; ++e) {
         const int cs = c_iter % kStagesC;
         if (c_iter >= kStagesC &&
-            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kErrWaitDrain, abort_flag))
+            !mbar_wait(&code_empty[cs], ((c_iter / kStagesC) - 1) & 1, p.status, kSiteKeyPair + kErrWaitDrain, abort_flag))
           break;
         uint4* stash = reinterpret_cast<uint4*>(c_slots + (cs + 1) * kCodeSlot - 32);
         stash[0] = make_uint4(0u, 0u, 0u, kStashEnd << 24);
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // Drain: every plane-block copy this CTA issued has landed before the CTA can leave.
       for (int s = 0; s < kStagesC && s < static_cast<int>(c_iter); ++s) {
         const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kStagesC);
-        mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&code_full[s], (last / kStagesC) & 1, p.status, kSiteKeyPair + kErrWaitDrain);
       }
     }
   } else if (warp == 2) {
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       while (!cb.done() && !*abort_flag) {
         const int sb = b_iter % kStagesB;
         if (b_iter >= kStagesB &&
-            !mbar_wait(&b_empty[sb], ((b_iter / kStagesB) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+            !mbar_wait(&b_empty[sb], ((b_iter / kStagesB) - 1) & 1, p.status, kSiteKeyPair + kErrWaitEmpty, abort_flag)) {
           give_up();
           break;
         }
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // Drain: every basis copy this CTA issued has landed before the CTA can leave.
       for (int s = 0; s < kStagesB && s < static_cast<int>(b_iter); ++s) {
         const uint32_t last = b_iter - 1 - ((b_iter - 1 - s) % kStagesB);
-        mbar_wait(&b_full[s], (last / kStagesB) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&b_full[s], (last / kStagesB) & 1, p.status, kSiteKeyPair + kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -320,14 +320,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
           const int it = items.at(k);
           if (it < 0) {
-            record_error(p.status, kErrBadDescriptor);
+            record_error(p.status, kSiteKeyPair + kErrBadDescriptor);
             give_up();
             break;
           }
           const int n_merged = p.pairs[4 * (p.items[it] / nblocks) + 2];
           if (n_merged <= 0) continue;  // nothing accumulated; the epilogue writes the mean-only keys
           if (item_iter >= 1 &&
-              !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
+              !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kSiteKeyPair + kErrWaitAccumFree, abort_flag)) {
             give_up();
             break;
           }
@@ -335,9 +335,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           bool ok = true;
           for (int gi = 0; gi < n_merged; ++gi) {
             const int sa = a_iter % kStagesA, sb = b_iter % kStagesB;
-            if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kErrWaitA, abort_flag) ||
-                !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag) ||
-                !mbar_wait(&b_peer[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
+            if (!mbar_wait(&a_full[sa], (a_iter / kStagesA) & 1, p.status, kSiteKeyPair + kErrWaitA, abort_flag) ||
+                !mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kSiteKeyPair + kErrWaitBasis, abort_flag) ||
+                !mbar_wait(&b_peer[sb], (b_iter / kStagesB) & 1, p.status, kSiteKeyPair + kErrWaitBasis, abort_flag)) {
               ok = false;
               break;
             }
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // Also on an early exit: no pair MMA may still read shared memory or TMEM past this point.
         if (a_iter > 0) {
           mma_commit_pair(mma_done, 0x1);
-          mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+          mbar_wait(mma_done, 0, p.status, kSiteKeyPair + kErrWaitDrain);
         }
       }
     } else {
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         uint32_t b_iter = 0;
         while (!cf.done() && !*abort_flag) {
           const int sb = b_iter % kStagesB;
-          if (!mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kErrWaitBasis, abort_flag)) {
+          if (!mbar_wait(&b_full[sb], (b_iter / kStagesB) & 1, p.status, kSiteKeyPair + kErrWaitBasis, abort_flag)) {
             give_up();
             break;
           }
@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int h = u >> 7;
     for (uint32_t i = set;; i += 2) {  // position in the sequence: code slot i % kStagesC, A stage i % kStagesA
       const int cs = i % kStagesC;
-      if (!warp_wait(&code_full[cs], (i / kStagesC) & 1, p.status, kErrWaitCodes, abort_flag)) {
+      if (!warp_wait(&code_full[cs], (i / kStagesC) & 1, p.status, kSiteKeyPair + kErrWaitCodes, abort_flag)) {
         give_up();
         break;
       }
@@ -410,14 +410,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       if ((w0.w >> 24) & kStashEnd) break;
       const int sa = i % kStagesA;
       if (i >= static_cast<uint32_t>(kStagesA) &&
-          !warp_wait(&a_empty[sa], ((i / kStagesA) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          !warp_wait(&a_empty[sa], ((i / kStagesA) - 1) & 1, p.status, kSiteKeyPair + kErrWaitEmpty, abort_flag)) {
         give_up();
         break;
       }
       const GroupRegs gr = group_from_words(w0, *reinterpret_cast<const uint4*>(slot + kCodeSlot - 16));
       const int n_tok = static_cast<int>((w0.w >> 16) & 0xFFu);
       uint32_t out[16];
-      decode_half(slot, gr, n_tok, r, h, out);
+      decode_half<F16>(slot, gr, n_tok, r, h, out);
       uint8_t* a = a_tiles + sa * kATilePair;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int k = items.k; k < items.end && !*abort_flag && !failed; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteKeyPair + kErrBadDescriptor);
         give_up();
         break;
       }
@@ -458,10 +458,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int pos = valid ? p.tok_pos[tile.token_base + r] : 0;
       const bool hidden = pos < 0;  // refined or evicted token: excluded from the softmax
       pos = hidden ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
-      const __nv_bfloat16* cosrow = p.cos_t + static_cast<int64_t>(pos) * (D / 2);
-      const __nv_bfloat16* sinrow = p.sin_t + static_cast<int64_t>(pos) * (D / 2);
+      const uint16_t* cosrow = reinterpret_cast<const uint16_t*>(p.cos_t) + static_cast<int64_t>(pos) * (D / 2);
+      const uint16_t* sinrow = reinterpret_cast<const uint16_t*>(p.sin_t) + static_cast<int64_t>(pos) * (D / 2);
       if (accumulated) {
-        if (!warp_wait(accum_full, item_iter & 1, p.status, kErrWaitAccum, abort_flag)) {
+        if (!warp_wait(accum_full, item_iter & 1, p.status, kSiteKeyPair + kErrWaitAccum, abort_flag)) {
           give_up();
           break;
         }
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int kv0 = nblk * kHeads;
         const int h0 = head_half * kHalfHeads;  // first head of this half
         for (int qi = 0; qi < p.q_len; ++qi) {
-          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+          if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyPair + kErrWaitAccum, abort_flag)) {
             give_up();
             failed = true;
             break;
@@ -482,14 +482,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           for (int i = et; i < kHeads * G * D; i += 256) {
             const int hq = kv0 * G + i / D;
             const int d = i % D;
-            q_s[i] = __bfloat162float(p.query[((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D + d]);
+            q_s[i] = half_to_float<F16>(reinterpret_cast<const uint16_t*>(
+                p.query)[((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D + d]);
           }
           if (qi == 0) {
-            const __nv_bfloat16* mrow = p.mean + static_cast<int64_t>(s) * p.mean_seq_stride +
-                                        static_cast<int64_t>(p.layer) * p.n_cols + nblk * kPairCols;
-            for (int i = et; i < kPairCols; i += 256) mean_s[i] = __bfloat162float(mrow[i]);
+            const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.mean) + static_cast<int64_t>(s) * p.mean_seq_stride +
+                                   static_cast<int64_t>(p.layer) * p.n_cols + nblk * kPairCols;
+            for (int i = et; i < kPairCols; i += 256) mean_s[i] = half_to_float<F16>(mrow[i]);
           }
-          if (!group_sync(ep_sync, n_sync, p.status, kErrWaitAccum, abort_flag)) {
+          if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyPair + kErrWaitAccum, abort_flag)) {
             give_up();
             failed = true;
             break;
@@ -506,8 +507,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
             const uint4 cv[2] = {__ldg(cp), __ldg(cp + 1)};
             const uint4 sv[2] = {__ldg(sp), __ldg(sp + 1)};
-            const __nv_bfloat162* cbv = reinterpret_cast<const __nv_bfloat162*>(cv);
-            const __nv_bfloat162* sbv = reinterpret_cast<const __nv_bfloat162*>(sv);
+            const uint32_t* cbv = reinterpret_cast<const uint32_t*>(cv);  // 8 pairs of 16-bit values
+            const uint32_t* sbv = reinterpret_cast<const uint32_t*>(sv);
 #pragma unroll
             for (int hp = 0; hp < kHalfHeads; hp += 2) {
               uint32_t x1[2][16], x2[2][16];
@@ -530,8 +531,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                 const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                  const float2 cf = __bfloat1622float2(cbv[i / 2]);
-                  const float2 sf = __bfloat1622float2(sbv[i / 2]);
+                  const float2 cf = half2_to_float2<F16>(cbv[i / 2]);
+                  const float2 sf = half2_to_float2<F16>(sbv[i / 2]);
                   const float4 ma = m1[i / 4], mb = m2[i / 4];
                   const float k1a = __uint_as_float(x1[e][i]) + ((i & 2) ? ma.z : ma.x);
                   const float k1b = __uint_as_float(x1[e][i + 1]) + ((i & 2) ? ma.w : ma.y);
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   cluster_sync_all();
 }
 
-template <int D, int G, bool RAW>
+template <int D, int G, bool RAW, bool F16>
 static int launch_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   using L = PairSmem<RAW>;
   const int smem = 1024 + L::kQ + (kPairCols / D) * G * D * 4 + kPairCols * 4 + 48 * 8 + 32;
@@ -596,10 +597,10 @@ static int launch_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int gri
   // The warpgroup register split assumes exactly kLaunchRegs per thread at launch; with any other
   // count setmaxnreg.inc could wait for registers that never come, so refuse to launch.
   cudaFuncAttributes fattr{};
-  if (cudaFuncGetAttributes(&fattr, key_scores_pair_kernel<D, G, RAW>) != cudaSuccess) return kDkvErrCuda;
+  if (cudaFuncGetAttributes(&fattr, key_scores_pair_kernel<D, G, RAW, F16>) != cudaSuccess) return kDkvErrCuda;
   if (fattr.numRegs != kLaunchRegs) return kDkvErrConfig;
   cudaError_t e =
-      cudaFuncSetAttribute(key_scores_pair_kernel<D, G, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaFuncSetAttribute(key_scores_pair_kernel<D, G, RAW, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return kDkvErrCuda;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
@@ -613,18 +614,18 @@ static int launch_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int gri
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, key_scores_pair_kernel<D, G, RAW>, bmap, p);
+  e = cudaLaunchKernelEx(&cfg, key_scores_pair_kernel<D, G, RAW, F16>, bmap, p);
   return e == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 
-template <int D>
+template <int D, bool F16>
 static int pair_dispatch_g(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   const bool raw = p.max_planes > 8;
   switch (p.q_per_kv) {
-    case 1: return raw ? launch_pair<D, 1, true>(bmap, p, grid, stream) : launch_pair<D, 1, false>(bmap, p, grid, stream);
-    case 2: return raw ? launch_pair<D, 2, true>(bmap, p, grid, stream) : launch_pair<D, 2, false>(bmap, p, grid, stream);
-    case 3: return raw ? launch_pair<D, 3, true>(bmap, p, grid, stream) : launch_pair<D, 3, false>(bmap, p, grid, stream);
-    case 4: return raw ? launch_pair<D, 4, true>(bmap, p, grid, stream) : launch_pair<D, 4, false>(bmap, p, grid, stream);
+    case 1: return raw ? launch_pair<D, 1, true, F16>(bmap, p, grid, stream) : launch_pair<D, 1, false, F16>(bmap, p, grid, stream);
+    case 2: return raw ? launch_pair<D, 2, true, F16>(bmap, p, grid, stream) : launch_pair<D, 2, false, F16>(bmap, p, grid, stream);
+    case 3: return raw ? launch_pair<D, 3, true, F16>(bmap, p, grid, stream) : launch_pair<D, 3, false, F16>(bmap, p, grid, stream);
+    case 4: return raw ? launch_pair<D, 4, true, F16>(bmap, p, grid, stream) : launch_pair<D, 4, false, F16>(bmap, p, grid, stream);
     default: return kDkvErrConfig;
   }
 }
@@ -633,8 +634,8 @@ static int pair_dispatch_g(const CUtensorMap& bmap, const KeyScoreParams& p, int
 int run_key_scores_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream) {
   if (grid < 2 || grid % 2 != 0 || p.n_cols % kPairCols != 0 || p.pairs == nullptr || kPairCols % p.head_dim != 0)
     return kDkvErrConfig;
-  if (p.head_dim == 128) return pair_dispatch_g<128>(bmap, p, grid, stream);
-  if (p.head_dim == 64) return pair_dispatch_g<64>(bmap, p, grid, stream);
+  if (p.head_dim == 128) return p.f16 ? pair_dispatch_g<128, true>(bmap, p, grid, stream) : pair_dispatch_g<128, false>(bmap, p, grid, stream);
+  if (p.head_dim == 64) return p.f16 ? pair_dispatch_g<64, true>(bmap, p, grid, stream) : pair_dispatch_g<64, false>(bmap, p, grid, stream);
   return kDkvErrConfig;
 }
 

@@ -12,6 +12,7 @@
 #include <cfloat>
 #include <cmath>
 #include "dkv_ptx.cuh"
+#include "dkv_format.cuh"
 #include "dkv_kernels.h"
 
 namespace dkv {
@@ -19,7 +20,12 @@ namespace dkv {
 namespace {
 constexpr int kSoftmaxThreads = 256;
 
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// x rounded to the cache dtype (the reference's p.to(dtype)), bf16 or fp16 by the call's flag.
+__device__ __forceinline__ float dtype_round(float x, int f16) { return f16 ? round_half<true>(x) : round_half<false>(x); }
+__device__ __forceinline__ float load_half(const __nv_bfloat16* ptr, int64_t i, int f16) {
+  const uint16_t bits = reinterpret_cast<const uint16_t*>(ptr)[i];
+  return f16 ? half_to_float<true>(bits) : half_to_float<false>(bits);
+}
 
 __device__ __forceinline__ void merge_ml(float& m, float& l, float m2, float l2) {
   if (m2 == -INFINITY) return;
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_mass_kernel(const Sof
   float mass = 0.f;
   for (int64_t n = r.lo + threadIdx.x; n < r.hi; n += blockDim.x) {
     const float x = r.sc[n];
-    if (x != -INFINITY) mass += bf16_round(expf(x - mx) * inv);
+    if (x != -INFINITY) mass += dtype_round(expf(x - mx) * inv, p.f16);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mass += __shfl_xor_sync(0xffffffffu, mass, o);
@@ -155,17 +161,16 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const So
   const int kvh = hq / p.q_per_kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  const __nv_bfloat16* q = p.query + ((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D;
-  for (int d = tid; d < D; d += blockDim.x) qv[d] = __bfloat162float(q[d]);
+  const int64_t q0 = ((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D;
+  for (int d = tid; d < D; d += blockDim.x) qv[d] = load_half(p.query, q0 + d, p.f16);
   __syncthreads();
 
   // Exact-token scores, one warp per token.
-  const __nv_bfloat16* kbase = p.exact_k + (static_cast<int64_t>(s) * (p.n_q_heads / p.q_per_kv) + kvh) *
-                                               static_cast<int64_t>(p.n_exact) * D;
+  const int64_t kbase = (static_cast<int64_t>(s) * (p.n_q_heads / p.q_per_kv) + kvh) * static_cast<int64_t>(p.n_exact) * D;
   for (int e = warp; e < p.n_exact; e += blockDim.x / 32) {
-    const __nv_bfloat16* k = kbase + static_cast<int64_t>(e) * D;
+    const int64_t k = kbase + static_cast<int64_t>(e) * D;
     float dot = 0.f;
-    for (int d = lane; d < D; d += 32) dot += qv[d] * __bfloat162float(k[d]);
+    for (int d = lane; d < D; d += 32) dot += qv[d] * load_half(p.exact_k, k + d, p.f16);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
     if (lane == 0) {
@@ -234,7 +239,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_stats_kernel(const So
   float mass = 0.f;
   for (int64_t n = tid; n < m_s; n += blockDim.x) {
     const float x = sc[n];
-    if (x != -INFINITY) mass += bf16_round(expf(x - mx) * inv);
+    if (x != -INFINITY) mass += dtype_round(expf(x - mx) * inv, p.f16);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mass += __shfl_xor_sync(0xffffffffu, mass, o);

@@ -75,7 +75,7 @@ __device__ __forceinline__ void store_zero_rows(uint8_t* out_row0, int64_t row_s
 
 }  // namespace
 
-template <bool BF16, bool RAW>
+template <bool BF16, bool RAW, bool F16>
 __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(const UnpackParams p) {
   using S = UnpackSmem<BF16, RAW>;
   constexpr int kUnpackSlotBytes = S::kSlotBytes;
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   const TileDesc tile = p.tiles[blockIdx.x];
   const int n_union = static_cast<int>(p.out_cols / kGroup);
   if (tile.n_tokens < 1 || tile.n_tokens > kTileTokens || tile.n_groups < 0 || tile.n_groups > n_union) {
-    if (tid == 0) record_error(p.status, kErrBadDescriptor);
+    if (tid == 0) record_error(p.status, kSiteUnpack + kErrBadDescriptor);
     return;  // uniform over the CTA: nothing initialised yet
   }
   if (tid == 0) {
@@ -114,13 +114,13 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
         const GroupRegs gr = load_group(&p.groups[tile.group_base + gi]);
         if (gr.code_bytes == 0 || gr.code_bytes > static_cast<uint32_t>(kUnpackSlotBytes) || (gr.code_bytes & 15u) ||
             (gr.code_offset & 15u) || static_cast<uint64_t>(gr.code_offset) + gr.code_bytes > p.code_size) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteUnpack + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
         const int s = issued % kUnpackSlots;
         if (issued >= kUnpackSlots &&
-            !mbar_wait(&empty[s], ((issued / kUnpackSlots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+            !mbar_wait(&empty[s], ((issued / kUnpackSlots) - 1) & 1, p.status, kSiteUnpack + kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
       // Drain: the CTA must not exit with a copy into its shared memory in flight.
       const int first = issued > kUnpackSlots ? issued - kUnpackSlots : 0;
       for (int i = first; i < issued; ++i)
-        mbar_wait(&full[i % kUnpackSlots], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes);
+        mbar_wait(&full[i % kUnpackSlots], (i / kUnpackSlots) & 1, p.status, kSiteUnpack + kErrWaitCodes);
     }
     return;
   }
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
   for (int i = 0; i < tile.n_groups; ++i) {
     const int s = i % kUnpackSlots;
     // The warp leaves together (its stores end in __syncwarp): one lane giving up ends the warp.
-    const bool landed = mbar_wait(&full[s], (i / kUnpackSlots) & 1, p.status, kErrWaitCodes, abort_flag);
+    const bool landed = mbar_wait(&full[s], (i / kUnpackSlots) & 1, p.status, kSiteUnpack + kErrWaitCodes, abort_flag);
     if (!__all_sync(0xffffffffu, landed)) {
       *abort_flag = 1;
       return;
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
     const GroupRegs gr = group_from_words(stash[0], stash[1]);
     const int g = static_cast<int>(gr.group);
     if (g < g_done || g >= n_union) {  // descriptors out of union order, or a group past out_cols / 64
-      record_error(p.status, kErrBadDescriptor);
+      record_error(p.status, kSiteUnpack + kErrBadDescriptor);
       *abort_flag = 1;
       return;
     }
@@ -180,12 +180,12 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
     uint4 chunks[kC];
     if (BF16) {
       uint32_t out[16];
-      decode_half(blk, gr, tile.n_tokens, r, h, out);
+      decode_half<F16>(blk, gr, tile.n_tokens, r, h, out);
 #pragma unroll
       for (int k = 0; k < 4; ++k) chunks[k] = make_uint4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
     } else {
       float out[32];
-      decode_half_f32(blk, gr, tile.n_tokens, r, h, out);
+      decode_half_f32<F16>(blk, gr, tile.n_tokens, r, h, out);
 #pragma unroll
       for (int k = 0; k < kC; ++k)
         chunks[k] = make_uint4(__float_as_uint(out[4 * k]), __float_as_uint(out[4 * k + 1]),
@@ -202,14 +202,21 @@ __global__ void __launch_bounds__(kUnpackThreads, BF16 ? 4 : 1) unpack_kernel(co
       store_zero_rows<BF16>(out_base + static_cast<int64_t>(g_done) * kGroup * (BF16 ? 2 : 4), stride, lane, n_valid);
 }
 
-template <bool BF16, bool RAW>
-static int launch_unpack(const UnpackParams& p, cudaStream_t stream) {
+template <bool BF16, bool RAW, bool F16>
+static int launch_unpack3(const UnpackParams& p, cudaStream_t stream) {
   const int smem = UnpackSmem<BF16, RAW>::kBytes + 128;
-  if (cudaFuncSetAttribute(unpack_kernel<BF16, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+  if (cudaFuncSetAttribute(unpack_kernel<BF16, RAW, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return kDkvErrCuda;
-  unpack_kernel<BF16, RAW><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
+  unpack_kernel<BF16, RAW, F16><<<p.n_tiles, kUnpackThreads, smem, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
+// BF16: 16-bit output (in fp16 with p.f16, else bf16); otherwise float32. p.f16 also says that raw blocks hold
+// fp16 patterns.
+template <bool BF16, bool RAW>
+static int launch_unpack(const UnpackParams& p, cudaStream_t stream) {
+  return p.f16 ? launch_unpack3<BF16, RAW, true>(p, stream) : launch_unpack3<BF16, RAW, false>(p, stream);
 }
 
 int run_unpack(const UnpackParams& p, cudaStream_t stream) {

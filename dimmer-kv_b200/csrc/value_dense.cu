@@ -51,6 +51,7 @@ __device__ __forceinline__ int dense_next_pair(const GroupDesc* d, int n, int g0
 
 }  // namespace
 
+template <bool F16>
 __global__ void __launch_bounds__(kDThreads, 1)
     value_dense_kernel(const __grid_constant__ CUtensorMap vmap, const ValueWeightParams p, int a_stages) {
   extern __shared__ uint8_t smem_raw[];
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t idesc = idesc_f16(128, NR, true, /*a_mn=*/true, /*b_mn=*/false);
+  const uint32_t idesc = idesc_f16(128, NR, /*is_bf16=*/!F16, /*a_mn=*/true, /*b_mn=*/false);
   const int item_cols = p.item_groups * 64;
   const int n_pairs = p.item_groups / 2;
   const ItemRange items(p.cta_begin, p.item_order, p.n_items);
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteValueDense + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
@@ -125,19 +126,19 @@ __global__ void __launch_bounds__(kDThreads, 1)
           tile_range(it, t, tb, d0, d1);
           const int n = d1 - d0;
           if (n < 0 || n > kDMaxRangeGroups || t < 0 || t >= p.n_tiles) {
-            record_error(p.status, kErrBadDescriptor);
+            record_error(p.status, kSiteValueDense + kErrBadDescriptor);
             *abort_flag = 1;
             break;
           }
           const int pb = p_iter & 1, db = d_iter & 1;
-          if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kSiteValueDense + kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
           mbar_arrive_expect_tx(&p_full[pb], p_tile);
           bulk_load(p_tiles + pb * p_tile, p.p_img + static_cast<int64_t>(t) * p_tile, p_tile, &p_full[pb]);
           ++p_iter;
-          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kSiteValueDense + kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -153,11 +154,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
       // Drain: every copy this producer issued has landed before the CTA can leave.
       for (int s = 0; s < 2 && s < static_cast<int>(d_iter); ++s) {
         const uint32_t last = d_iter - 1 - ((d_iter - 1 - s) % 2);
-        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kSiteValueDense + kErrWaitDrain);
       }
       for (int s = 0; s < 2 && s < static_cast<int>(p_iter); ++s) {
         const uint32_t last = p_iter - 1 - ((p_iter - 1 - s) % 2);
-        mbar_wait(&p_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&p_full[s], (last / 2) & 1, p.status, kSiteValueDense + kErrWaitDrain);
       }
     }
   } else if (warp == 2) {
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
           tile_range(it, t, tb, d0, d1);
           const int n = d1 - d0;
           const int db = d_iter & 1;
-          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
+          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kSiteValueDense + kErrWaitCodes, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -183,13 +184,13 @@ __global__ void __launch_bounds__(kDThreads, 1)
           bool ok = n >= 0 && n <= kDMaxRangeGroups;
           while (ok && (pair = dense_next_pair(d, n, g0, i)) >= 0) {
             if (pair >= n_pairs || d[i - 1].group < static_cast<uint32_t>(g0)) {  // outside the item's groups
-              record_error(p.status, kErrBadDescriptor);
+              record_error(p.status, kSiteValueDense + kErrBadDescriptor);
               ok = false;
               break;
             }
             const int st = a_iter % a_stages;
             if (a_iter >= static_cast<uint32_t>(a_stages) &&
-                !mbar_wait(&a_empty[st], ((a_iter / a_stages) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+                !mbar_wait(&a_empty[st], ((a_iter / a_stages) - 1) & 1, p.status, kSiteValueDense + kErrWaitEmpty, abort_flag)) {
               ok = false;
               break;
             }
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
       // Drain: every TMA box this producer issued has landed before the CTA can leave.
       for (int s = 0; s < a_stages && s < static_cast<int>(a_iter); ++s) {
         const uint32_t last = a_iter - 1 - ((a_iter - 1 - s) % a_stages);
-        mbar_wait(&a_full[s], (last / a_stages) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&a_full[s], (last / a_stages) & 1, p.status, kSiteValueDense + kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
         const int tb = p.items[4 * it + 1], te = p.items[4 * it + 2], g0 = p.items[4 * it + 3];
         const uint32_t acc_base = tmem + (item_iter & 1) * kDAccumCols;
         if (item_iter >= 2 &&
-            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kErrWaitAccumFree,
+            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kSiteValueDense + kErrWaitAccumFree,
                        abort_flag)) {
           *abort_flag = 1;
           break;
@@ -239,8 +240,8 @@ __global__ void __launch_bounds__(kDThreads, 1)
           tile_range(it, t, tb, d0, d1);
           const int n = d1 - d0;
           const int pb = p_iter & 1, db = d_iter & 1;
-          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA, abort_flag) ||
-              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
+          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kSiteValueDense + kErrWaitA, abort_flag) ||
+              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kSiteValueDense + kErrWaitCodes, abort_flag)) {
             ok = false;
             break;
           }
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
               break;
             }
             const int st = a_iter % a_stages;
-            if (!mbar_wait(&a_full[st], (a_iter / a_stages) & 1, p.status, kErrWaitA, abort_flag)) {
+            if (!mbar_wait(&a_full[st], (a_iter / a_stages) & 1, p.status, kSiteValueDense + kErrWaitA, abort_flag)) {
               ok = false;
               break;
             }
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
       if (issued) {
         // Every exit: no MMA may still read shared memory or TMEM past this point.
         mma_commit(mma_done);
-        mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+        mbar_wait(mma_done, 0, p.status, kSiteValueDense + kErrWaitDrain);
       }
     }
   } else if (warp >= 4) {
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
         tile_range(it, t, tb, d0, d1);
         for (int i2 = d0; i2 < d1; ++i2) live_mask |= 1u << ((static_cast<int>(__ldg(&p.groups[i2].group)) - g0) >> 1);
       }
-      if (!warp_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kErrWaitAccum, abort_flag)) {
+      if (!warp_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kSiteValueDense + kErrWaitAccum, abort_flag)) {
         *abort_flag = 1;
         break;
       }
@@ -358,9 +359,15 @@ int run_value_dense(const CUtensorMap& vmap, const ValueWeightParams& p, int gri
   const int smem = 1024 + stages * kDPairTile + 2 * p.n_rows_pad * 256 + 2 * kDMaxRangeGroups * 32 + 32 * 8 + 16;
   const int rc = run_vprobs(p, stream);  // P^T images of every value tile for this call's rows
   if (rc != kDkvOk) return rc;
-  if (cudaFuncSetAttribute(value_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return kDkvErrCuda;
-  value_dense_kernel<<<grid, kDThreads, smem, stream>>>(vmap, p, stages);
+  if (p.f16) {
+    if (cudaFuncSetAttribute(value_dense_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kDkvErrCuda;
+    value_dense_kernel<true><<<grid, kDThreads, smem, stream>>>(vmap, p, stages);
+  } else {
+    if (cudaFuncSetAttribute(value_dense_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kDkvErrCuda;
+    value_dense_kernel<false><<<grid, kDThreads, smem, stream>>>(vmap, p, stages);
+  }
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) vprobs_kernel(const ValueWeightParams p) 
   const int t = blockIdx.x;
   const TileDesc tile = p.tiles[t];
   const bool tile_ok = tile.n_tokens >= 1 && tile.n_tokens <= kTileTokens;
-  if (!tile_ok && threadIdx.x == 0) record_error(p.status, kErrBadDescriptor);
+  if (!tile_ok && threadIdx.x == 0) record_error(p.status, kSiteValue + kErrBadDescriptor);
   const int s = tile.seq;
   const int r = threadIdx.x & 127;
   const bool tok_ok = tile_ok && r < tile.n_tokens;
@@ -86,15 +86,15 @@ __global__ void __launch_bounds__(256) vprobs_kernel(const ValueWeightParams p) 
       const float* st = p.row_stats + (static_cast<int64_t>(s) * p.n_q_heads * p.q_len + p.row_begin + n) * 4;
       prob = (x == -INFINITY) ? 0.f : expf(x - st[0]) * st[1];
     }
-    *reinterpret_cast<__nv_bfloat16*>(img + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
-        __float2bfloat16_rn(prob);
+    *reinterpret_cast<uint16_t*>(img + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
+        p.f16 ? float_to_half<true>(prob) : float_to_half<false>(prob);
   }
   __syncthreads();
   uint4* dst = reinterpret_cast<uint4*>(p.p_img + static_cast<int64_t>(t) * NR * 256);
   for (int i = threadIdx.x; i < NR * 16; i += blockDim.x) dst[i] = reinterpret_cast<const uint4*>(img)[i];
 }
 
-template <bool RAW, bool PIMG>
+template <bool RAW, bool PIMG, bool F16>
 __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const ValueWeightParams p, int a_slots) {
   using L = ValueSmem<RAW>;
   constexpr int kCodeSlots = L::kCodeSlots;
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t idesc = idesc_f16(128, NR, true, /*a_mn=*/true, /*b_mn=*/false);
+  const uint32_t idesc = idesc_f16(128, NR, /*is_bf16=*/!F16, /*a_mn=*/true, /*b_mn=*/false);
   const int item_cols = p.item_groups * 64;
   const int n_pairs = p.item_groups / 2;
   const ItemRange items(p.cta_begin, p.item_order, p.n_items);
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteValue + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
@@ -179,18 +179,18 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int n = d1 - d0;
           const int db = d_iter & 1;
           if (n < 0 || n > kMaxRangeGroups) {
-            record_error(p.status, kErrBadDescriptor);
+            record_error(p.status, kSiteValue + kErrBadDescriptor);
             *abort_flag = 1;
             break;
           }
           if (PIMG) {
             if (t < 0 || t >= p.n_tiles) {
-              record_error(p.status, kErrBadDescriptor);
+              record_error(p.status, kSiteValue + kErrBadDescriptor);
               *abort_flag = 1;
               break;
             }
             const int pb = p_iter & 1;
-            if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+            if (p_iter >= 2 && !mbar_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kSiteValue + kErrWaitEmpty, abort_flag)) {
               *abort_flag = 1;
               break;
             }
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             bulk_load(p_tiles + pb * p_tile, p.p_img + static_cast<int64_t>(t) * p_tile, p_tile, &p_full[pb]);
             ++p_iter;
           }
-          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+          if (d_iter >= 2 && !mbar_wait(&d_empty[db], ((d_iter >> 1) - 1) & 1, p.status, kSiteValue + kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -214,11 +214,11 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       // Drain: every copy this producer issued has landed before the CTA can leave.
       for (int s = 0; s < 2 && s < static_cast<int>(d_iter); ++s) {
         const uint32_t last = d_iter - 1 - ((d_iter - 1 - s) % 2);
-        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&d_full[s], (last / 2) & 1, p.status, kSiteValue + kErrWaitDrain);
       }
       for (int s = 0; PIMG && s < 2 && s < static_cast<int>(p_iter); ++s) {
         const uint32_t last = p_iter - 1 - ((p_iter - 1 - s) % 2);
-        mbar_wait(&p_full[s], (last / 2) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&p_full[s], (last / 2) & 1, p.status, kSiteValue + kErrWaitDrain);
       }
     }
   } else if (warp == 0 || warp == 18) {
@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteValue + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                         p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
           const int db = d_iter & 1;
-          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
+          if (!mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kSiteValue + kErrWaitCodes, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -257,13 +257,13 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
               if (gi < 0) continue;
               const uint32_t off = d[gi].code_offset, bytes = d[gi].code_bytes;
               if (bytes > static_cast<uint32_t>(kCodeSlot) || static_cast<uint64_t>(off) + bytes > p.code_size) {
-                record_error(p.status, kErrBadDescriptor);
+                record_error(p.status, kSiteValue + kErrBadDescriptor);
                 ok = false;
                 break;
               }
               const int cs = c_iter % kCodeSlots;
               if (c_iter >= kCodeSlots &&
-                  !mbar_wait(&r_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+                  !mbar_wait(&r_empty[cs], ((c_iter / kCodeSlots) - 1) & 1, p.status, kSiteValue + kErrWaitEmpty, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       // Drain: every copy this producer issued has landed before the CTA can leave.
       for (int s = 0; s < kCodeSlots && s < static_cast<int>(c_iter); ++s) {
         const uint32_t last = c_iter - 1 - ((c_iter - 1 - s) % kCodeSlots);
-        mbar_wait(&r_full[s], (last / kCodeSlots) & 1, p.status, kErrWaitDrain);
+        mbar_wait(&r_full[s], (last / kCodeSlots) & 1, p.status, kSiteValue + kErrWaitDrain);
       }
     }
   } else if (warp == 1) {
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         const int it = items.at(k);
         if (it < 0) {
-          record_error(p.status, kErrBadDescriptor);
+          record_error(p.status, kSiteValue + kErrBadDescriptor);
           *abort_flag = 1;
           break;
         }
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         // drains one half while the next item accumulates into the other.
         const uint32_t acc_base = tmem + (item_iter & 1) * kAccumCols;
         if (item_iter >= 2 &&
-            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kErrWaitAccumFree, abort_flag)) {
+            !mbar_wait(&accum_empty[item_iter & 1], ((item_iter >> 1) - 1) & 1, p.status, kSiteValue + kErrWaitAccumFree, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -315,8 +315,8 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           const int pb = p_iter & 1, db = d_iter & 1;
           const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                         p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
-          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kErrWaitA, abort_flag) ||
-              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
+          if (!mbar_wait(&p_full[pb], (p_iter >> 1) & 1, p.status, kSiteValue + kErrWaitA, abort_flag) ||
+              !mbar_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kSiteValue + kErrWaitCodes, abort_flag)) {
             ok = false;
             break;
           }
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           while ((pair = next_pair(d, n, g0, i, lo, hi)) >= 0) {
             const int set = ord & 1;
             const int slot = a_iter[set] % a_slots;
-            if (!mbar_wait(&a_full[set * 2 + slot], (a_iter[set] / a_slots) & 1, p.status, kErrWaitA, abort_flag)) {
+            if (!mbar_wait(&a_full[set * 2 + slot], (a_iter[set] / a_slots) & 1, p.status, kSiteValue + kErrWaitA, abort_flag)) {
               ok = false;
               break;
             }
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         // Every exit (also one where the epilogue gave up): no MMA may still read shared memory or TMEM
         // past this point.
         mma_commit(mma_done);
-        mbar_wait(mma_done, 0, p.status, kErrWaitDrain);
+        mbar_wait(mma_done, 0, p.status, kSiteValue + kErrWaitDrain);
       }
     }
   } else {
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
     for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
       const int it = items.at(k);
       if (it < 0) {
-        record_error(p.status, kErrBadDescriptor);
+        record_error(p.status, kSiteValue + kErrBadDescriptor);
         *abort_flag = 1;
         break;
       }
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         st_s[2 * w + 1] = inv;
       }
       mbar_arrive(&stats_ready[item_iter % 3]);
-      if (!warp_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kErrWaitA, abort_flag)) {
+      if (!warp_wait(&stats_ready[item_iter % 3], (item_iter / 3) & 1, p.status, kSiteValue + kErrWaitA, abort_flag)) {
         *abort_flag = 1;
         break;
       }
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         // ---- P^T tile: rows x 128 tokens, bf16 (the reference rounds p to the cache dtype); set s builds
         //      rows [s*NR/2, (s+1)*NR/2), thread half h a quarter of them.
         const int pb = p_iter & 1;
-        if (!PIMG && p_iter >= 2 && !warp_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+        if (!PIMG && p_iter >= 2 && !warp_wait(&p_empty[pb], ((p_iter >> 1) - 1) & 1, p.status, kSiteValue + kErrWaitEmpty, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -431,8 +431,8 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             for (int kk = 0; kk < 4; ++kk) {
               const int n = n0 + kk;
               const float prob = (x[kk] == -INFINITY) ? 0.f : expf(x[kk] - st_s[2 * n]) * st_s[2 * n + 1];
-              *reinterpret_cast<__nv_bfloat16*>(pt + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
-                  __float2bfloat16_rn(prob);
+              *reinterpret_cast<uint16_t*>(pt + atom * (NR * 128) + sw128_offset(n, chunk) + within) =
+                  float_to_half<F16>(prob);
             }
           }
           fence_async_shared();
@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
         const int db = d_iter & 1;
         const int n = p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2 + 1] -
                       p.item_ranges[(static_cast<int64_t>(it) * p.tile_chunk + (t - tb)) * 2];
-        if (!warp_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kErrWaitCodes, abort_flag)) {
+        if (!warp_wait(&d_full[db], (d_iter >> 1) & 1, p.status, kSiteValue + kErrWaitCodes, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
           }
           const int slot = a_iter % a_slots;
           if (a_iter >= static_cast<uint32_t>(a_slots) &&
-              !warp_wait(&a_empty[set * 2 + slot], ((a_iter / a_slots) - 1) & 1, p.status, kErrWaitEmpty, abort_flag)) {
+              !warp_wait(&a_empty[set * 2 + slot], ((a_iter / a_slots) - 1) & 1, p.status, kSiteValue + kErrWaitEmpty, abort_flag)) {
             *abort_flag = 1;
             break;
           }
@@ -467,13 +467,13 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
             uint32_t out[16];
             if (gi >= 0) {
               const int cs = set * kCodeSlots + c_iter % kCodeSlots;  // this set's ring
-              if (!warp_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kErrWaitCodes, abort_flag)) {
+              if (!warp_wait(&code_full[cs], (c_iter / kCodeSlots) & 1, p.status, kSiteValue + kErrWaitCodes, abort_flag)) {
                 *abort_flag = 1;
                 break;
               }
               const uint4* dw = reinterpret_cast<const uint4*>(d + gi);
               const GroupRegs gr = group_from_words(dw[0], dw[1]);
-              decode_half(c_slots + cs * kCodeSlot, gr, tile.n_tokens, r, h, out);
+              decode_half<F16>(c_slots + cs * kCodeSlot, gr, tile.n_tokens, r, h, out);
               mbar_arrive(&code_empty[cs]);
               ++c_iter;
             } else {
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
       if (*abort_flag) break;
       // ---- epilogue (warps 4..7, one per TMEM lane quarter): TMEM -> partial sums
       if (warp == 4 || warp == 5 || warp == 14 || warp == 15) {
-        if (!warp_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kErrWaitAccum, abort_flag)) {
+        if (!warp_wait(&accum_full[item_iter & 1], (item_iter >> 1) & 1, p.status, kSiteValue + kErrWaitAccum, abort_flag)) {
           *abort_flag = 1;
           break;
         }
@@ -539,13 +539,19 @@ __global__ void __launch_bounds__(kVThreads, 1) value_weights_kernel(const Value
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-template <bool RAW, bool PIMG>
-static int launch_vw(const ValueWeightParams& p, int grid, int smem, int a_slots, cudaStream_t stream) {
-  if (cudaFuncSetAttribute(value_weights_kernel<RAW, PIMG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+template <bool RAW, bool PIMG, bool F16>
+static int launch_vw3(const ValueWeightParams& p, int grid, int smem, int a_slots, cudaStream_t stream) {
+  if (cudaFuncSetAttribute(value_weights_kernel<RAW, PIMG, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return kDkvErrCuda;
-  value_weights_kernel<RAW, PIMG><<<grid, kVThreads, smem, stream>>>(p, a_slots);
+  value_weights_kernel<RAW, PIMG, F16><<<grid, kVThreads, smem, stream>>>(p, a_slots);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
+
+template <bool RAW, bool PIMG>
+static int launch_vw(const ValueWeightParams& p, int grid, int smem, int a_slots, cudaStream_t stream) {
+  return p.f16 ? launch_vw3<RAW, PIMG, true>(p, grid, smem, a_slots, stream)
+               : launch_vw3<RAW, PIMG, false>(p, grid, smem, a_slots, stream);
 }
 
 int run_vprobs(const ValueWeightParams& p, cudaStream_t stream) {

@@ -51,7 +51,7 @@ class AttendArgs(ctypes.Structure):
         ("vpart", c_void_p),
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
         ("k_pairs", c_void_p), ("k_pair_groups", c_void_p), ("softmax_mode", c_int32),
-        ("p_img", c_void_p), ("n_v_tiles", c_int32), ("v_dense", c_void_p),
+        ("p_img", c_void_p), ("n_v_tiles", c_int32), ("v_dense", c_void_p), ("fp16", c_int32),
     ]
 
 
@@ -61,7 +61,7 @@ class UnpackArgs(ctypes.Structure):
     _fields_ = [
         ("code", c_void_p), ("code_size", c_uint64), ("tiles", c_void_p), ("n_tiles", c_int32),
         ("groups", c_void_p), ("out", c_void_p), ("out_cols", c_int64), ("out_bf16", c_int32), ("status", c_void_p),
-        ("max_planes", c_int32), ("out_tile_rows", c_int32),
+        ("max_planes", c_int32), ("out_tile_rows", c_int32), ("f16", c_int32),
     ]
 
 
@@ -190,11 +190,21 @@ def check(rc: int, what: str) -> None:
         raise DimmerKVError(f"{what}: {STATUS_TEXT.get(rc, rc)}")
 
 
+DEVICE_SITES = {1: "key_scores_pair", 2: "key_scores", 3: "value_weights", 4: "value_dense", 5: "unpack"}
+
+
+def describe_device_error(code: int) -> str:
+    """'device error <code>: <what> (<kernel>)' for a status word (kernel site * 1000 + error)."""
+    site, err = divmod(code, 1000)
+    where = f" in {DEVICE_SITES[site]}" if site in DEVICE_SITES else ""
+    return f"device error {code}: {DEVICE_ERRORS.get(err, 'unknown')}{where}"
+
+
 def check_device_status(status) -> None:
     """Raise if a kernel recorded a device-side error in ``status`` (a 1-element int32 cuda tensor)."""
     code = int(status.item())
     if code != 0:
-        raise DimmerKVError(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown')}")
+        raise DimmerKVError(describe_device_error(code))
 
 
 class StatusPoller:
@@ -241,7 +251,7 @@ class StatusPoller:
                 time.sleep(0.0005)
             code = int(self._host[slot])
             if code != 0:
-                raise DimmerKVError(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown')}")
+                raise DimmerKVError(describe_device_error(code))
 
     def drain(self) -> None:
         """Wait (bounded) for every poll still queued and check it."""

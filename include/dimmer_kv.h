@@ -141,6 +141,11 @@ typedef struct dkv_attend_args {
    * Given with p_img, the value stage streams them with TMA instead of decoding the planes again in every
    * layer (the coefficients are the same for every layer); NULL decodes the planes in the value kernel. */
   const void* v_dense;
+  /* The cache dtype of every 16-bit operand (query, exact keys / values, bases, means, RoPE tables, v_dense,
+   * the raw 16-bit planes of the streams) and of a 16-bit output: 0 bf16, 1 fp16 (the reference's default
+   * CompressedContext dtype). Probabilities are rounded to it where the reference rounds them. fp16 needs the
+   * CTA-pair key kernel (k_pairs). */
+  int32_t fp16;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */
@@ -205,6 +210,7 @@ typedef struct dkv_unpack_args {
   int32_t max_planes;            /* largest plane count of any block (16: raw bf16 blocks); 0: unknown */
   int32_t out_tile_rows;         /* 0: token rows in stream order; 128: tile t's tokens at rows t * 128 ..
                                   * (rows past a tile's tokens are not written) */
+  int32_t f16;                   /* 1: a 16-bit output is fp16 (not bf16), and raw blocks hold fp16 patterns */
 } dkv_unpack_args;
 int dkv_unpack(const dkv_unpack_args* args, void* stream);
 
