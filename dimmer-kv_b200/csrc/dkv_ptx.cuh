@@ -36,18 +36,14 @@ constexpr int kSiteValue = 3000;       // value_weights_kernel / vprobs_kernel (
 constexpr int kSiteValueDense = 4000;  // value_dense_kernel (coefficients decoded once per step)
 constexpr int kSiteUnpack = 5000;      // unpack_kernel
 
-// Bound on one wait. Healthy waits in these kernels last microseconds. A wait gives up when both clocks
-// say that more than the deadline has passed: %globaltimer follows the host's clock (a time step on the
-// host moves it), and %clock64 is the cycle counter of the SM the thread runs on (a context switch can
-// resume the CTA on another SM), so neither alone can end a healthy wait early; a clock seen running
-// backwards restarts its measurement. 2e9 cycles is 1.02 s at the B200's 1965 MHz maximum SM clock.
-// Whatever %globaltimer does, a wait also ends after 6e10 cycles (about 30 s at the maximum clock).
-// The clocks are read at every poll: one mbarrier.try_wait may itself suspend the thread for a
-// hardware-defined time, so a bound counted in polls would not be a bound in time. Both clocks are kept
-// in units of 1024 (ns, cycles) modulo 2^32, which wraps after 73 minutes.
-constexpr uint32_t kWaitDeadlineNs1024 = 2000000000u / 1024u;
-constexpr uint32_t kWaitDeadlineCycles1024 = 2000000000u / 1024u;
-constexpr uint32_t kWaitHardCycles1024 = static_cast<uint32_t>(60000000000ull / 1024u);
+// Bound on one wait. Healthy waits in these kernels last microseconds; a wait gives up after 2 s of
+// %globaltimer time. The time is summed over polls in steps clamped to 100 ms (a step backwards counts as
+// nothing), so that a jump of the timer (it follows the host's clock) cannot end a healthy wait early.
+// Every poll sleeps for a bounded time (mbar_try_wait's suspend hint), so the clock is read at least every
+// 20 microseconds whatever the barrier does. Times are kept in units of 1.024 us (ns >> 10).
+constexpr uint32_t kWaitDeadline1024 = 2000000000u / 1024u;
+constexpr uint32_t kWaitStepCap1024 = 100000000u / 1024u;
+constexpr uint32_t kPollSuspendNs = 20000u;
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -55,29 +51,29 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-__device__ __forceinline__ uint64_t sm_cycles() {
-  uint64_t c;
-  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
-  return c;
-}
-
 // Elapsed-time bookkeeping of one bounded wait (started after its first unsuccessful poll).
 struct WaitClock {
-  uint32_t t0, c0;
-  __device__ __forceinline__ WaitClock()
-      : t0(static_cast<uint32_t>(global_ns() >> 10)), c0(static_cast<uint32_t>(sm_cycles() >> 10)) {}
+  uint32_t last, elapsed;
+  __device__ __forceinline__ WaitClock() : last(static_cast<uint32_t>(global_ns() >> 10)), elapsed(0) {}
   // True once the wait has run out.
   __device__ __forceinline__ bool expired() {
-    const uint32_t t = static_cast<uint32_t>(global_ns() >> 10), c = static_cast<uint32_t>(sm_cycles() >> 10);
-    if (static_cast<int32_t>(t - t0) < 0) t0 = t;
-    if (static_cast<int32_t>(c - c0) < 0) c0 = c;
-    const uint32_t dc = c - c0;
-    return (t - t0 > kWaitDeadlineNs1024 && dc > kWaitDeadlineCycles1024) || dc > kWaitHardCycles1024;
+    const uint32_t t = static_cast<uint32_t>(global_ns() >> 10);
+    const int32_t step = static_cast<int32_t>(t - last);
+    last = t;
+    if (step > 0) elapsed += static_cast<uint32_t>(step) < kWaitStepCap1024 ? static_cast<uint32_t>(step) : kWaitStepCap1024;
+    return elapsed > kWaitDeadline1024;
   }
 };
 
 __device__ __forceinline__ void record_error(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+// A wait that ran out: its code (kernel site + error, below 10^4) and, in the decimal digits above, the
+// barrier that did not complete (its shared-memory address / 8, modulo 10^5): status = barrier * 10^4 +
+// code. The host prints both.
+__device__ __forceinline__ void record_wait_error(int* status, int code, uint32_t bar_saddr) {
+  record_error(status, static_cast<int>((bar_saddr >> 3) % 100000u) * 10000 + code);
 }
 
 // The call's status word as the kernel starts: non-zero when an earlier kernel of the call (or of an
@@ -113,14 +109,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Test of the phase with the given parity that may suspend the thread until the phase completes, for at
+// most kPollSuspendNs (the suspend-time hint bounds the sleep; without it the hardware limit applies).
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kPollSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -150,7 +148,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     if (mbar_try_wait(bar, parity)) return true;
     if (abort != nullptr && *abort != 0) return false;
     if (clock.expired()) {
-      record_error(status, code);
+      record_wait_error(status, code, smem_u32(bar));
       return false;
     }
   }

@@ -194,10 +194,13 @@ DEVICE_SITES = {1: "key_scores_pair", 2: "key_scores", 3: "value_weights", 4: "v
 
 
 def describe_device_error(code: int) -> str:
-    """'device error <code>: <what> (<kernel>)' for a status word (kernel site * 1000 + error)."""
-    site, err = divmod(code, 1000)
+    """'device error <code>: <what> in <kernel>' for a status word: barrier * 10^4 + kernel site * 1000 +
+    error, the barrier (its shared-memory address / 8) recorded by a wait that ran out."""
+    barrier, rest = divmod(code, 10000)
+    site, err = divmod(rest, 1000)
     where = f" in {DEVICE_SITES[site]}" if site in DEVICE_SITES else ""
-    return f"device error {code}: {DEVICE_ERRORS.get(err, 'unknown')}{where}"
+    bar = f" (barrier at shared address {barrier * 8:#x})" if barrier else ""
+    return f"device error {code}: {DEVICE_ERRORS.get(err, 'unknown')}{where}{bar}"
 
 
 def check_device_status(status) -> None:
