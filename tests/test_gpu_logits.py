@@ -49,6 +49,20 @@ class OracleAttention:
         return torch.from_numpy(np.ascontiguousarray(out)).to(query.device, query.dtype), None
 
 
+def _oracle_with_tables(fix, inputs, model, tokens):
+    """The oracle of the dkvtc fixture with the RoPE tables of ``model`` (as CompressedContext takes them)."""
+    from dimmerkv.synthetic import rope_full
+    from oracle.codes import round_dtype
+
+    ctx = oracle_context(fix, inputs, "bf16", False)
+    cos, sin = rope_full(model, tokens, DEV)
+    start, end = (int(v) for v in fix["span"])
+    ctx.cos = round_dtype(cos.cpu().numpy()[start:end], "bf16").astype(ctx.f)
+    ctx.sin = round_dtype(sin.cpu().numpy()[start:end], "bf16").astype(ctx.f)
+    ctx.order_cos, ctx.order_sin = ctx.cos[ctx.order], ctx.sin[ctx.order]
+    return ctx
+
+
 def _fresh(cache, model):
     return build_cache([l.keys.clone() for l in cache.layers], [l.values.clone() for l in cache.layers], model)
 
@@ -70,7 +84,9 @@ def test_first_step_logits_match_oracle_fp32(golden, tmp_path):
     with torch.inference_mode():
         ours, logits = _greedy(model, ctx, _fresh(ctx.exact_cache, model), tail, tokens)
         ctx.batch.check_status()
-        oracle = OracleAttention(oracle_context(fix, inputs, "bf16", False))
+        # The oracle's RoPE tables come from this float32 model (a bf16 model's rotary frequencies are themselves
+        # rounded to bf16, so the fixture's tables belong to another model).
+        oracle = OracleAttention(_oracle_with_tables(fix, inputs, model, tokens))
         want_tokens, want = _greedy(model, oracle, _fresh(ctx.exact_cache, model), tail, tokens)
     err = float(np.abs(logits - want).max())
     assert np.isfinite(err) and err < 1e-4, err
