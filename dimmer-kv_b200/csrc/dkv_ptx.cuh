@@ -356,6 +356,12 @@ __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Named barrier `id` over `threads` threads (a multiple of 32): every warp of the participating set
+// executes it once, from whatever code location its role is at.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }
 
 __device__ __forceinline__ int warp_id() { return static_cast<int>(threadIdx.x >> 5); }

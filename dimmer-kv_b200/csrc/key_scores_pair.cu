@@ -40,6 +40,13 @@ constexpr int kPairThreads = 896;
 // Register split per warpgroup (setmaxnreg): the launch gives every thread kLaunchRegs; the control
 // warpgroup drops to 40, the four decode warpgroups to 48, the two epilogue warpgroups take 136:
 // 128*40 + 512*48 + 256*136 = 64512 <= 896*72 = 64512. The launch checks the compiled count first.
+// Registers move between warps of the same SM sub-partition only (warp w runs on sub-partition w % 4), and
+// each sub-partition holds one control warp, four decode warps and two epilogue warps: 32*(72-40) +
+// 4*32*(72-48) = 4096 registers released there, exactly the 2*32*(136-72) its two epilogue warps take.
+// The balance is exact, so no warp may take registers back (its setmaxnreg.inc at the bottom of its
+// branch) before both epilogue warps of its sub-partition hold their 136: the idle control warp 3 would
+// otherwise reach its inc at once and could starve an epilogue warp of sub-partition 3 for good. Every
+// warp therefore meets the others on named barrier kRegBarrier right after its first setmaxnreg.
 constexpr int kLaunchRegs = 72;
 #ifndef DKV_REGS_CONTROL
 #define DKV_REGS_CONTROL 40
@@ -49,6 +56,7 @@ constexpr int kLaunchRegs = 72;
 constexpr int kRegsControl = DKV_REGS_CONTROL, kRegsDecode = DKV_REGS_DECODE, kRegsEpilogue = DKV_REGS_EPILOGUE;
 static_assert(128 * kRegsControl + 512 * kRegsDecode + 256 * kRegsEpilogue <= kPairThreads * kLaunchRegs,
               "register split exceeds the launch allocation");
+constexpr int kRegBarrier = 1;              // named barrier of the register hand-over (0 is __syncthreads)
 constexpr int kPairCols = 512;              // key columns per item
 constexpr int kMmaN = 256;                  // N of one pair MMA (two per K step)
 constexpr int kHalfCols = 128;              // basis columns of one pair MMA loaded by each CTA
@@ -211,9 +219,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   // Each role's register budget is set at the top of its warpgroup's branch (so that it governs the
   // role's code) and the launch budget restored at the bottom, before the common exit path; the
-  // epilogue warpgroups release their extra registers there, which the others then take back.
+  // epilogue warpgroups release their extra registers there, which the others then take back. Between
+  // the two, every warp passes the register hand-over barrier once all epilogue warps hold their budget.
   if (warp < 4) {
   setmaxnreg_dec<kRegsControl>();
+  named_barrier_sync(kRegBarrier, kPairThreads);
   if (warp == 0) {
     // ------------------------------------------------------------ code producer
     if (lane == 0) {
@@ -393,6 +403,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   setmaxnreg_inc<kLaunchRegs>();
   } else if (warp < 20) {
     setmaxnreg_dec<kRegsDecode>();
+    named_barrier_sync(kRegBarrier, kPairThreads);
     // ------------------------------------------------------------ decode warps (follow the slots)
     // Set 0 (warps 4-11) takes the even positions of the group sequence, set 1 (warps 12-19) the odd.
     const int set = (warp - 4) >> 3;
@@ -431,6 +442,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     setmaxnreg_inc<kLaunchRegs>();
   } else {
     setmaxnreg_inc<kRegsEpilogue>();
+    named_barrier_sync(kRegBarrier, kPairThreads);
     // ------------------------------------------------------------ epilogue warps
     // A warp reads the TMEM lane quarter (warp % 4); warps 20..23 and 24..27 each cover quarters
     // 0..3, the first four taking the first half of the item's KV heads, the others the second.
