@@ -732,9 +732,9 @@ def run_kernels(args, cfg, device) -> dict:
             "code_read_gbs": round(code_bytes_step / (elapsed / args.steps) / 1e9, 2),
             "stage_ms_per_step": timer.stage_ms(args.steps), "roofline": roofline(flops_layer, timer.key_ms()),
             "gpu_launches": len(timer.events) * KERNELS_PER_LAYER + len(timer.unpack_events),
-            "unpack": unpack_rate(batch, device),
-            "encode": encode_rate(device), "storage": storage_rate(device),
-            "allocate": allocate_rate(device), "demote": demote_rate(batch, device)}
+            **({} if args.no_extras else {
+                "unpack": unpack_rate(batch, device), "encode": encode_rate(device), "storage": storage_rate(device),
+                "allocate": allocate_rate(device), "demote": demote_rate(batch, device)})}
 
 
 def _one_conversation(cfg: dict, seed: int, device, keep_full: bool = False, fixed_planes=None, model=None):

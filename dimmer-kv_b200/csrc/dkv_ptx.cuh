@@ -39,13 +39,12 @@ constexpr int kSiteUnpack = 5000;      // unpack_kernel
 // Bound on one wait. Healthy waits in these kernels last microseconds; a wait gives up after 2 s of
 // %globaltimer time. The time is summed over polls in steps clamped to 100 ms (a step backwards counts as
 // nothing), so that a jump of the timer (it follows the host's clock) cannot end a healthy wait early.
-// Polls use mbarrier.test_wait, which never suspends the thread, with a short __nanosleep back-off between
-// them: mbarrier.try_wait may suspend the thread for a hardware-defined time (its suspend time is only a
-// hint), so a loop of try_wait is not bounded in time. Times are kept in units of 1.024 us (ns >> 10).
+// Polls are mbarrier.try_wait, which suspends the thread until the phase completes (the efficient wait of
+// a pipeline) or for at most the suspend-time hint, kPollSuspendNs; the deadline is checked between polls.
+// Times are kept in units of 1.024 us (ns >> 10).
 constexpr uint32_t kWaitDeadline1024 = 2000000000u / 1024u;
 constexpr uint32_t kWaitStepCap1024 = 100000000u / 1024u;
-constexpr uint32_t kPollSpins = 8;         // polls without sleeping before the back-off starts
-constexpr uint32_t kPollSleepMaxNs = 256;  // longest sleep between two polls
+constexpr uint32_t kPollSuspendNs = 1000000u;
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -112,6 +111,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 
 // Non-blocking test of the phase with the given parity (for a thread that polls several barriers).
+// Test of the phase with the given parity that may suspend the thread until the phase completes, for at
+// most kPollSuspendNs.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kPollSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -130,19 +143,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // that drain the thread's own copies or MMAs in flight pass no abort flag: those always complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
                                           const volatile int* abort = nullptr) {
-  if (mbar_test_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   WaitClock clock;
-  uint32_t polls = 0, sleep_ns = 16;
   while (true) {
-    if (mbar_test_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (abort != nullptr && *abort != 0) return false;
     if (clock.expired()) {
       record_wait_error(status, code, smem_u32(bar));
       return false;
-    }
-    if (++polls > kPollSpins) {
-      __nanosleep(sleep_ns);
-      sleep_ns = sleep_ns < kPollSleepMaxNs ? 2 * sleep_ns : kPollSleepMaxNs;
     }
   }
 }
