@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 
 from . import dimmer
-from .codes import from_coefficients
+from .codes import from_coefficients, retype_raw
 from .common import build_cache
 from .context import CompressedBatch, ConversationCodes, TokenCodes, rope_tables
 
@@ -35,9 +35,11 @@ class CompressedContext:
             given = getattr(codec, "last_codes", None)
             if given is not None and kind in given:
                 codes[kind] = given[kind]
+                if dtype != torch.bfloat16:  # raw planes were packed for a bf16 cache: re-encode them in dtype
+                    codes[kind] = retype_raw(codes[kind], codec.last_coefficients[kind], dtype)
             else:
                 codes[kind] = from_coefficients(codec.last_coefficients[kind].to(device),
-                                                codec.last_choice[kind].to(device))
+                                                codec.last_choice[kind].to(device), dtype)
         conv = ConversationCodes(start, end, _to(codes["key"], device), _to(codes["value"], device))
         cos, sin = rope_tables(model, max(tokens, end) + 1, device, dtype)
         # A progressive codec's cold tier can refine any group: cover them all.

@@ -186,8 +186,10 @@ class CompressedBatch:
         decode step (at layer 0, dkv_unpack) into a tile-padded bf16 buffer of the value stream that every
         layer's value stage streams with TMA, instead of decoding the planes again in every layer (the
         coefficients are the same for all layers); it holds n_value_tiles * 128 * v_width bf16 values."""
-        if dtype != torch.bfloat16:
-            raise NotImplementedError("the sm_100a kernels of this build compute in bf16 only")
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise NotImplementedError(f"the sm_100a kernels take bf16 or fp16 operands, not {dtype}")
+        if dtype == torch.float16 and not pair_keys:
+            raise NotImplementedError("fp16 operands need the CTA-pair key kernel (pair_keys=True)")
         self.lib = _lib.lib()
         self.layers, self.kv_heads, self.head_dim, self.q_heads = layers, kv_heads, head_dim, q_heads
         self.n_cols = kv_heads * head_dim
@@ -229,6 +231,8 @@ class CompressedBatch:
         # Key work items: every tile x column block, scheduled over the SMs.
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.pair_keys = pair_keys and self.n_cols % 512 == 0
+        if dtype == torch.float16 and not self.pair_keys:
+            raise NotImplementedError("fp16 operands need the CTA-pair key kernel (kv_heads * head_dim a multiple of 512)")
         if self.pair_keys:
             self.k_block = 512
         else:
@@ -369,12 +373,12 @@ class CompressedBatch:
             return None
         rows = vs.n_tiles * 128
         if self._v_dense is None or tuple(self._v_dense.shape) != (rows, self.v_width):
-            self._v_dense = torch.zeros(rows, self.v_width, dtype=torch.bfloat16, device=self.device)
+            self._v_dense = torch.zeros(rows, self.v_width, dtype=self.dtype, device=self.device)
             self._v_dense_version = None
         if layer == 0 or self._v_dense_version != self._v_version:
             a = _lib.UnpackArgs(vs.code.data_ptr(), vs.code.numel(), vs.tiles.data_ptr(), vs.n_tiles,
                                 vs.groups.data_ptr(), self._v_dense.data_ptr(), self.v_width, 1,
-                                self.status.data_ptr(), vs.max_planes, 128)
+                                self.status.data_ptr(), vs.max_planes, 128, int(self.dtype == torch.float16))
             stream = torch.cuda.current_stream(self.device).cuda_stream
             launch = lambda: _lib.check(self.lib.dkv_unpack(a, stream), "dkv_unpack")
             if self.timer is not None and hasattr(self.timer, "unpack"):
@@ -460,6 +464,7 @@ class CompressedBatch:
         a.p_img, a.n_v_tiles = ptr("p_img"), vs.n_tiles
         dense = self._dense_values(layer) if scratch else None
         a.v_dense = dense.data_ptr() if dense is not None else None
+        a.fp16 = int(self.dtype == torch.float16)
         a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
         a.k_pairs = self.k_pairs.data_ptr() if self.k_pairs is not None else None
         a.k_pair_groups = self.k_pair_groups.data_ptr() if self.k_pairs is not None else None

@@ -2,8 +2,8 @@
 
 Usage (only where the reference checkout exists; the GPU box does not have it):
     DIMMERKV_REFERENCE=/path/to/Dimmer-KV python tests/golden/make_golden.py [fixture ...]
-(no names: every fixture; names such as ``encode``, ``codes``, ``storage``, ``logits`` or ``tiny``: only
-those).
+(no names: every fixture; names such as ``encode``, ``codes``, ``storage``, ``logits``, ``f16`` or ``tiny``:
+only those).
 
 Every array saved here is produced by the reference's own functions (scripts/progressive.py,
 scripts/kvtc.py, scripts/compressed_attention.py, scripts/dimmer.py, scripts/methods.py,
@@ -236,6 +236,80 @@ def logits_fixture(out: Path, methods, model, keys, values, scores, tokens: int)
         torch.random.set_rng_state(rng_state)
 
 
+def f16_fixture(out: Path, methods, model, keys, values, scores, tokens: int) -> None:
+    """The reference's CompressedContext in float16 (its default dtype, compressed_attention.py:34-35) on the
+    two entry points' codes: attention outputs of both layers at q = 1 and 4 (the same queries, new tokens and
+    masks as tiny_dkvtc / tiny_prog), and greedy_answer's first-step logits and reply with the model in
+    float16 over the dkvtc codes."""
+    rng_state = torch.random.get_rng_state()
+    try:
+        cfg = model.config
+        layers, heads, dim = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+        g = torch.Generator().manual_seed(21)  # the draws of main(): same queries and new tokens
+        module = types.SimpleNamespace(num_key_value_groups=cfg.num_attention_heads // heads)
+        queries = {q: torch.randn(1, cfg.num_attention_heads, q, dim, generator=g) for q in (1, 4)}
+        news = {q: (torch.randn(1, heads, q, dim, generator=g), torch.randn(1, heads, q, dim, generator=g))
+                for q in (1, 4)}
+        dtype = torch.float16
+        result = {}
+
+        def attend_all(ctx, tag):
+            for layer in range(layers):
+                module.layer_idx = layer
+                ex = ctx.exact_cache.layers[layer]
+                for q in (1, 4):
+                    k = torch.cat([ex.keys, news[q][0].to(dtype)], dim=2)
+                    v = torch.cat([ex.values, news[q][1].to(dtype)], dim=2)
+                    mask = None
+                    if q > 1:
+                        e = k.shape[2]
+                        mask = torch.zeros(1, 1, q, e, dtype=dtype)
+                        causal = torch.triu(torch.ones(q, q, dtype=torch.bool), 1)
+                        mask[0, 0, :, e - q:][causal] = torch.finfo(dtype).min
+                    out_, _ = ctx.attend(module, queries[q].to(dtype), k, v, mask, dim ** -0.5)
+                    result[f"{tag}_f16_attend_l{layer}_q{q}"] = out_.float().numpy()
+
+        with torch.inference_mode():
+            methods.apply("dkvtc@0.1:snap:floor1", keys, values, scores)
+            codec = methods.codec("kvtc")
+            ctx = compressed_attention.CompressedContext(codec, [k.to(dtype) for k in keys],
+                                                         [v.to(dtype) for v in values], model)
+            assert ctx.dtype == dtype  # the reference's default
+            attend_all(ctx, "dkvtc")
+            pcodec = methods.codec("prog")
+            stored = pcodec.encode(keys, values, 0.1, tm.RECENT, None)
+            shim = types.SimpleNamespace(layers=layers, heads=heads, head_dim=dim, device=torch.device("cpu"),
+                                         last_span=(stored.start, stored.end), streams={}, last_choice={},
+                                         last_coefficients={})
+            for kind in ("key", "value"):
+                s = stored.stores[kind]
+                planes = pcodec.orders[kind].planes[s.hot_pieces]
+                shim.streams[kind] = pcodec.base.streams[kind]
+                shim.last_choice[kind] = s.hot_pieces
+                shim.last_coefficients[kind] = progressive.dequantize(s.codes, s.low, s.span, planes)
+            ctx = compressed_attention.CompressedContext(shim, [k.to(dtype) for k in keys],
+                                                         [v.to(dtype) for v in values], model)
+            attend_all(ctx, "prog")
+            # greedy_answer with the model in float16 over the dkvtc codes
+            methods.apply("dkvtc@0.1:snap:floor1", keys, values, scores)
+            model16 = tm.build_model(dtype)
+            dimmer.install(model16)
+            ctx = compressed_attention.CompressedContext(codec, [k.to(dtype) for k in keys],
+                                                         [v.to(dtype) for v in values], model16)
+            exact = build_cache([l.keys.clone() for l in ctx.exact_cache.layers],
+                                [l.values.clone() for l in ctx.exact_cache.layers], model16)
+            tok = types.SimpleNamespace(eos_token_id=-1, all_special_ids=[],
+                                        decode=lambda ids, skip_special_tokens=True: " ".join(map(str, ids)))
+            tail = tm.question_ids()
+            text, logits = compressed_attention.greedy_answer(model16, tok, ctx, exact, tail[None], tokens, 4,
+                                                              stop_at_eos=False)
+            result.update(tail=tail.numpy(), logits_f16=logits.float().numpy(),
+                          greedy_f16=np.array([int(x) for x in text.split()]))
+        np.savez_compressed(out / "tiny_f16.npz", **result)
+    finally:
+        torch.random.set_rng_state(rng_state)
+
+
 def main() -> None:
     out = HERE
     torch.set_num_threads(min(8, os.cpu_count() or 1))
@@ -289,6 +363,8 @@ def main() -> None:
         storage_fixture(out, methods, keys, values, scores)
     if not only or "logits" in only:
         logits_fixture(out, methods, model, keys, values, scores, tokens)
+    if not only or "f16" in only:
+        f16_fixture(out, methods, model, keys, values, scores, tokens)
     if only and "tiny" not in only:
         return
 

@@ -34,29 +34,30 @@ def _to(t):
     return t
 
 
-def _batch(golden, prog: bool) -> CompressedBatch:
+def _batch(golden, prog: bool, dtype=torch.bfloat16) -> CompressedBatch:
     inputs = golden("tiny_inputs")
     fix = golden("tiny_prog" if prog else "tiny_dkvtc")
     start, end = (int(v) for v in fix["span"])
     if prog:
         key, value = _prog_tokens(fix, inputs, "key"), _prog_tokens(fix, inputs, "value")
     else:
-        key = _to(from_coefficients(torch.from_numpy(fix["coeff_key"]), torch.from_numpy(fix["choice_key"])))
-        value = _to(from_coefficients(torch.from_numpy(fix["coeff_value"]), torch.from_numpy(fix["choice_value"])))
+        key = _to(from_coefficients(torch.from_numpy(fix["coeff_key"]), torch.from_numpy(fix["choice_key"]), dtype))
+        value = _to(from_coefficients(torch.from_numpy(fix["coeff_value"]), torch.from_numpy(fix["choice_value"]), dtype))
     bases = {k: torch.from_numpy(v) for k, v in tiny_bases(inputs).items()}
     mean = {"key": torch.from_numpy(inputs["mean_key"]), "value": torch.from_numpy(inputs["mean_value"])}
     half = inputs["cos"].shape[1] // 2
     cos = torch.from_numpy(inputs["cos"][:, :half].copy())
     sin = torch.from_numpy(inputs["sin"][:, :half].copy())
     return CompressedBatch([ConversationCodes(start, end, key, value)], layers=2, kv_heads=8, head_dim=64,
-                           q_heads=32, basis=bases, mean=mean, cos=cos, sin=sin, device=DEV)
+                           q_heads=32, basis=bases, mean=mean, cos=cos, sin=sin, device=DEV, dtype=dtype)
 
 
 def _call(batch, fix, inputs, layer, q, out_dtype):
-    k, v, mask = exact_kv(fix, inputs, layer, q, "bf16")
-    query = torch.from_numpy(fix[f"query_q{q}"]).to(DEV, torch.bfloat16)
-    kt = torch.from_numpy(k).to(DEV, torch.bfloat16)
-    vt = torch.from_numpy(v).to(DEV, torch.bfloat16)
+    tag = "f16" if batch.dtype == torch.float16 else "bf16"
+    k, v, mask = exact_kv(fix, inputs, layer, q, tag)
+    query = torch.from_numpy(fix[f"query_q{q}"]).to(DEV, batch.dtype)
+    kt = torch.from_numpy(k).to(DEV, batch.dtype)
+    vt = torch.from_numpy(v).to(DEV, batch.dtype)
     mt = torch.from_numpy(mask).to(DEV) if mask is not None else None
     out = batch.attend_layer(layer, query, kt, vt, mt, 64 ** -0.5, out_dtype=out_dtype)
     torch.cuda.synchronize()
@@ -79,6 +80,30 @@ def test_attend_matches_oracle_and_reference(golden, prog, q):
         out16, _ = _call(batch, fix, inputs, layer, q, torch.bfloat16)
         ref = fix[f"bf16_attend_l{layer}_q{q}"]
         assert np.abs(out16 - ref).max() < bf16_bound(fix, layer, q)
+
+
+@pytest.mark.parametrize("prog", [True, False], ids=["prog", "dkvtc_raw"])
+@pytest.mark.parametrize("q", [1, 4])
+def test_attend_fp16_matches_oracle_and_reference(golden, prog, q):
+    """The cache dtype of the reference's default CompressedContext (float16, compressed_attention.py:34-35):
+    fp32 output against the oracle rounding every stored operand to fp16 at 1e-4, fp16 output against the
+    reference's own float16 run (tests/golden/tiny_f16.npz) within max(2e-3, 1.25 x the reference's own
+    float16-vs-float32 deviation)."""
+    inputs = golden("tiny_inputs")
+    fix = golden("tiny_prog" if prog else "tiny_dkvtc")
+    f16 = golden("tiny_f16")
+    tag = "prog" if prog else "dkvtc"
+    batch = _batch(golden, prog, torch.float16)
+    ctx = oracle_context(fix, inputs, "f16", prog)
+    for layer in range(2):
+        out32, (k, v, mask) = _call(batch, fix, inputs, layer, q, torch.float32)
+        want = ctx.attend(layer, fix[f"query_q{q}"], k, v, mask, 64 ** -0.5)
+        err = np.abs(out32 - want).max()
+        assert err < TOL_F32, (layer, q, err)
+        out16, _ = _call(batch, fix, inputs, layer, q, torch.float16)
+        ref = f16[f"{tag}_f16_attend_l{layer}_q{q}"]
+        bound = max(2e-3, 1.25 * float(np.abs(ref - fix[f"f32_attend_l{layer}_q{q}"]).max()))
+        assert np.abs(out16 - ref).max() < bound, (layer, q, float(np.abs(out16 - ref).max()), bound)
 
 
 def test_unpack_bit_exact(golden):
@@ -202,7 +227,7 @@ def test_ragged_batch_matches_oracle_per_conversation():
             assert err < TOL_F32, (layer, s, err)
 
 
-def _check_3b_geometry(shapes, q, seed, dense=True):
+def _check_3b_geometry(shapes, q, seed, dense=True, dtype=torch.bfloat16):
     """Conversations of the given (middle tokens, groups) at the bench's attention geometry (Llama-3.2-3B:
     8 KV heads of 128, 24 query heads, GQA 3), one launch per layer, q query rows, each conversation
     against the oracle. ``dense``: the value stage reads the coefficients decoded once per step
@@ -229,11 +254,12 @@ def _check_3b_geometry(shapes, q, seed, dense=True):
         convs.append(ConversationCodes(4, 4 + n_mid, toks["key"], toks["value"]))
         raw.append(c)
     batch = CompressedBatch(convs, layers=L, kv_heads=H, head_dim=D, q_heads=HQ, basis=basis, mean=mean,
-                            cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV, dense_values=dense)
+                            cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV, dense_values=dense,
+                            dtype=dtype)
     S, E = len(shapes), 40
-    query = torch.randn(S, HQ, q, D, generator=g).to(torch.bfloat16)
-    ek = torch.randn(S, H, E, D, generator=g).to(torch.bfloat16)
-    ev = torch.randn(S, H, E, D, generator=g).to(torch.bfloat16)
+    query = torch.randn(S, HQ, q, D, generator=g).to(dtype)
+    ek = torch.randn(S, H, E, D, generator=g).to(dtype)
+    ev = torch.randn(S, H, E, D, generator=g).to(dtype)
     for layer in range(L):
         out = batch.attend_layer(layer, query.to(DEV), ek.to(DEV), ev.to(DEV), None, D ** -0.5, out_dtype=torch.float32)
         torch.cuda.synchronize()
@@ -245,7 +271,8 @@ def _check_3b_geometry(shapes, q, seed, dense=True):
                                 choice={k: c[k][4] for k in ("key", "value")}, decoded=decoded,
                                 basis={k: v.numpy() for k, v in basis.items()},
                                 mean={k: v.numpy() for k, v in mean.items()},
-                                cos=cos_full.numpy(), sin=sin_full.numpy(), dtype="bf16")
+                                cos=cos_full.numpy(), sin=sin_full.numpy(),
+                                dtype="f16" if dtype == torch.float16 else "bf16")
             want = ctx.attend(layer, query[s : s + 1].float().numpy(), ek[s : s + 1].float().numpy(),
                               ev[s : s + 1].float().numpy(), None, D ** -0.5)
             assert out[s : s + 1].shape == want.shape
@@ -259,6 +286,12 @@ def test_ragged_batch_3b_geometry_matches_oracle(q, dense):
     """Four ragged conversations in one launch: up to 2100 middle tokens (an odd number of tiles, so one
     CTA pair holds a single tile) and 16 coefficient groups; both value kernels."""
     _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), q, 11 + q, dense)
+
+
+@pytest.mark.parametrize("dense", [True, False], ids=["dense_values", "decoding_values"])
+def test_ragged_batch_3b_geometry_fp16_matches_oracle(dense):
+    """The same ragged launch with fp16 operands (the reference's default cache dtype), both value kernels."""
+    _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), 1, 71, dense, torch.float16)
 
 
 @pytest.mark.parametrize("q", [1, 4])
