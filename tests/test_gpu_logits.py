@@ -108,3 +108,24 @@ def test_greedy_answer_matches_reference_bf16(golden, tmp_path):
     assert ours == ref["greedy_bf16"].tolist()
     # The reference's own direct reply from the dkvtc fixture is the same reply.
     assert ours == fix["greedy_direct"].tolist()
+
+
+def test_greedy_answer_default_dtype_matches_reference_fp16(golden, tmp_path):
+    """The reference's stock call sequence: CompressedContext(codec, keys, values, model) with its default
+    dtype (float16, compressed_attention.py:34-35) next to a float16 model (scripts/common.py:39 on CUDA);
+    first-step logits against the reference's own float16 run (tests/golden/tiny_f16.npz) within
+    max(2e-3, 1.25 x the reference's float16-vs-float32 logit deviation), the same reply."""
+    inputs, fix, methods, _, _, keys, values = _setup(golden, tmp_path, "tiny_dkvtc")
+    f16, f32 = golden("tiny_f16"), golden("tiny_logits")
+    model = tm.build_model(torch.float16, DEV)
+    dimmer.install(model)
+    ctx = CompressedContext(methods.codec("kvtc"), [k.half() for k in keys], [v.half() for v in values], model)
+    assert ctx.dtype == torch.float16 and ctx.batch.dtype == torch.float16
+    tail = torch.from_numpy(f16["tail"]).to(DEV)
+    with torch.inference_mode():
+        ours, logits = _greedy(model, ctx, _fresh(ctx.exact_cache, model), tail, ctx.context_tokens)
+    ctx.batch.check_status()
+    bound = max(2e-3, 1.25 * float(np.abs(f16["logits_f16"] - f32["logits_f32"]).max()))
+    err = float(np.abs(logits - f16["logits_f16"]).max())
+    assert err < bound, (err, bound)
+    assert ours == f16["greedy_f16"].tolist()
