@@ -1,16 +1,18 @@
 """Decode throughput over a compressed KV cache (BASELINE metric, config 3).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg3|cfg1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg3|cfg1|cfg2|cfg4|cfg5] [--kernels-only]
 
-Workload: Llama-3.2-3B architecture, random-init bf16 weights; a batch of
-64 compressed conversations per GPU with lengths uniform in [4096, 16384] (seeded), 3% hot budget,
-per-token plane counts {0,1,2,4,6,8} @ {.05,.35,.25,.2,.1,.05} on the first G coefficient groups
+Workload: Llama-3.2-3B architecture, random-init bf16 weights; one seeded
+batch of 64 compressed conversations with lengths uniform in [4096, 16384], 3% hot budget, per-token
+plane counts {0,1,2,4,6,8} @ {.05,.35,.25,.2,.1,.05} on the first G coefficient groups
 (dimmerkv.synthetic documents the rules). A step = one decode step of every conversation of the
 batch: the HF model forward with every attention layer running over the packed codes
-(dkv_attend_layer: tcgen05 key rebuild + RoPE + QK, softmax statistics, tcgen05 value weighting,
-value basis + exact tokens). Conversation-parallel across GPUs: each rank decodes its own 64
-conversations, no data-path collective ("scaling": "weak"); the timed region is bracketed by a
-barrier and synchronize on every rank and the maximum over ranks is reported.
+(dkv_attend_layer: tcgen05 key rebuild + RoPE + QK, softmax statistics, value stage, value basis +
+exact tokens). Across GPUs the batch is partitioned by hot code bytes (longest-first bin packing), no
+data-path collective ("scaling": "strong"); the timed region is bracketed by a barrier and synchronize
+on every rank and the maximum over ranks is reported. Multi-GPU runs add a split-K leg (cfg5, one
+131072-token conversation sharded over the ranks); 1-GPU runs add cfg1, cfg2 and cfg4 under "configs".
 
 --impl reference times the reference algorithm on the host CPU (the numpy restatement under
 oracle/, float32, all host threads) on a bounded sample of the same workload.
@@ -34,8 +36,12 @@ sys.path.insert(0, str(ROOT))
 CONFIGS = {
     "cfg3": dict(arch="3b", seqs=64, tmin=4096, tmax=16384, budget=0.03, max_groups=64,
                  workload="3B random-init, 64 ragged conversations T~U[4096,16384], 3% hot budget, bs64 decode"),
-    "cfg1": dict(arch="1b", seqs=1, tmin=1536, tmax=1536, budget=0.03, max_groups=16,
+    "cfg1": dict(arch="1b", seqs=1, tmin=1536, tmax=1536, budget=0.03, max_groups=16, decode=32,
                  workload="1B random-init, 1 conversation T=1536, 3% hot budget, bs1 decode"),
+    "cfg2": dict(arch="1b", mode="ladder", seqs=1, tmin=8192, tmax=8192, budget=0.02, max_groups=16, decode=128,
+                 method="dkvtc@0.02:snap:floor1",
+                 workload="1B random-init, 1 conversation T=8192, dkvtc@0.02:snap:floor1 ladder codes through "
+                          "KVTCCodec.compress (synthetic rank-1024 basis and rung ladder), bs1 decode"),
     "cfg4": dict(arch="3b", mode="question", seqs=1, tmin=32768, tmax=32768, budget=0.03, max_groups=64,
                  hot_planes=2, question=64, fraction=0.01, decode=32,
                  workload="3B random-init, one 32768-token conversation; hot tier planes 1-2 on the budget's "
@@ -64,6 +70,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the one-layer oracle check after the timing")
     p.add_argument("--no-splitk", action="store_true", help="multi-GPU runs: skip the split-K (cfg5) leg")
+    p.add_argument("--no-configs", action="store_true",
+                   help="1-GPU runs: skip cfg1 / cfg2 / cfg4 after the headline (extra keys of the line)")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the unpack / encode / storage / allocator / demote rates after the timing")
     p.add_argument("--layers", type=int, default=None,
@@ -407,7 +415,9 @@ def key_kernel_source_hash() -> str:
     return h.hexdigest()[:16]
 
 
-def roofline(flops_layer: int, key_ms: list) -> dict:
+def roofline(flops_layer: int, key_ms: list, profiled_workload: bool = True) -> dict:
+    """The key kernel against the sustained bf16 peak. ``profiled_workload``: the launches are of the workload
+    that profiles/key_scores_traffic.json was captured on (cfg3's geometry), so its DRAM bytes scale to them."""
     peaks = measured_peaks()
     peak_tf = peaks["bf16_tflops_sustained"]
     peak_name = peaks["source"] + " (bf16_tflops_sustained)"
@@ -415,7 +425,9 @@ def roofline(flops_layer: int, key_ms: list) -> dict:
     achieved = flops_layer / (key_avg_ms / 1e3) / 1e12
     traffic, traffic_note = None, "no ncu capture of this build"
     prof = ROOT / "profiles" / "key_scores_traffic.json"
-    if prof.exists():
+    if not profiled_workload:
+        traffic_note = "no ncu capture of this geometry (the capture in profiles/ is of the 3B workload)"
+    elif prof.exists():
         rec = json.loads(prof.read_text())
         if rec.get("source_sha16") == key_kernel_source_hash():
             # The capture's DRAM bytes per launch, scaled to this launch by the algorithmic FLOPs (traffic grows
@@ -836,16 +848,278 @@ def run_question(args, cfg, device) -> dict:
     phases = {"importance": ev[0].elapsed_time(ev[1]), "select": ev[1].elapsed_time(ev[2]),
               "refine_fetch_merge": ev[2].elapsed_time(ev[3])}
     total = sum(phases.values())
+    # The scoring forward's attention against its binding roofline: per layer the key rebuild of the busy
+    # tokens, QK of the question's rows, the value weighting and the value basis; the hot codes read per layer.
+    q, r, layers = cfg["question"], conv.groups * 64, c.num_hidden_layers
+    n_cols = c.num_key_value_heads * c.head_dim
+    hq, hd = c.num_attention_heads, c.head_dim
+    imp_flops = layers * (2 * conv.busy_key * r * n_cols + 2 * conv.middle * hq * q * hd + 2 * conv.middle * hq * q * r
+                          + 2 * hq * q * r * hd)
+    imp_roof = step_roofline(imp_flops, conv.hot_bytes * layers, phases["importance"] / 1e3)
     return {"metric": "question-time refinement latency (score + top-1% select + cold-plane merge)",
             "value": round(total, 3), "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": 1,
             "warmup": args.warmup, "dtype": "bf16", "data": "synthetic (seeded random-init weights, random ids)",
             "config": {"workload": cfg["workload"], "context": tokens, "groups": conv.groups, "refined": count},
             "phases_ms": {k: round(v, 3) for k, v in phases.items()}, "fetched_bytes": fetched,
             "refine_host_ms": {k: round(v * 1e3, 3) for k, v in getattr(batch, "last_refine_seconds", {}).items()},
-            "topk_matches_lowest_index_rule": exact,
+            "topk_matches_lowest_index_rule": exact, "importance_roofline": imp_roof,
             "answer_after_refine": {"question_tokens": cfg["question"], "decode_steps": cfg["decode"],
                                     "seconds": round(answer_s, 3), "decode_tok_s": round(cfg["decode"] / answer_s, 2),
                                     **stats}}
+
+
+def time_decode(model, batch, cache, ids, positions, steps: int, warmup: int, device) -> dict:
+    """Greedy decode steps with attention over ``batch``, timed on the device with CUDA events between two
+    synchronizes (every kernel launch of the timed steps bracketed by StageTimer events, the status word
+    polled every step). Returns the elapsed seconds, the key kernel's launch times, the stage times per step,
+    the launch count and the clock samples."""
+    import torch
+
+    from dimmerkv import dimmer
+
+    stream = torch.cuda.current_stream(device)
+    timer = StageTimer(batch, stream)
+    dimmer.STATE.compressed = batch
+
+    def step(ids_, pos_):
+        out = model(input_ids=ids_, past_key_values=cache, position_ids=pos_, use_cache=True)
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        batch.poll_status()
+        return nxt
+
+    try:
+        with torch.inference_mode():
+            for _ in range(warmup):
+                ids = step(ids, positions)
+                positions = positions + 1
+            batch.poll_status(depth=0)
+            torch.cuda.synchronize(device)
+            batch.timer = timer
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(device.index if device.index is not None else 0) as clocks:
+                start.record(stream)
+                for _ in range(steps):
+                    ids = step(ids, positions)
+                    positions = positions + 1
+                end.record(stream)
+                batch.poll_status(depth=0)
+                torch.cuda.synchronize(device)
+            batch.timer = None
+            batch.check_status()
+    finally:
+        batch.timer = None
+        dimmer.STATE.compressed = None
+    return {"elapsed": start.elapsed_time(end) / 1e3, "key_ms": timer.key_ms(), "stage_ms": timer.stage_ms(steps),
+            "launches": len(timer.events) * KERNELS_PER_LAYER + len(timer.unpack_events), "clocks": clocks.summary()}
+
+
+def bs1_line(name: str, cfg: dict, steps: int, warmup: int, run: dict, work: tuple, parity: dict | None,
+             config: dict) -> dict:
+    """The JSON object of one batch-1 configuration measured after the headline (an extra key of its line)."""
+    flops_layer, code_bytes_step, step_flops = work
+    t = run["elapsed"]
+    line = {"metric": f"decode tok/s over compressed KV ({name}, bs1)", "value": round(steps / t, 3), "unit": "tok/s",
+            "steps": steps, "warmup": warmup, "ms_per_step": round(t / steps * 1e3, 3), "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic (seeded random-init weights, random token ids, synthetic PCA basis)",
+            "config": {"workload": cfg["workload"], **config},
+            "stage_ms_per_step": run["stage_ms"],
+            "roofline": roofline(flops_layer, run["key_ms"], profiled_workload=False),
+            "step_roofline": step_roofline(step_flops, code_bytes_step, t / steps),
+            "gpu_launches": run["launches"], "clocks": run["clocks"]}
+    if parity is not None:
+        line["parity_max_abs"] = parity["max_abs"]
+        line["parity"] = parity
+    return line
+
+
+def measure_cfg1(args, device) -> dict:
+    """Config 1: 1B random-init, one 1536-token conversation compressed at 3% with
+    progressive codes, 32 batch-1 decode steps over the codes; one layer checked against the oracle."""
+    import torch
+
+    cfg = CONFIGS["cfg1"]
+    model, batch, convs, lengths, bases = build_workload(cfg, 1, args.seed, device)
+    work = step_work(batch, convs, model.config.num_hidden_layers)
+    parity = bench_parity(model, batch, convs, bases)
+    cache = exact_cache(model, convs)
+    ids = torch.randint(0, model.config.vocab_size, (1, 1), generator=torch.Generator().manual_seed(args.seed + 1))
+    warmup = max(3, args.warmup)
+    run = time_decode(model, batch, cache, ids.to(device), torch.tensor(lengths, device=device)[:, None],
+                      cfg["decode"], warmup, device)
+    cv = convs[0]
+    return bs1_line("cfg1", cfg, cfg["decode"], warmup, run, work, parity,
+                    {"context": cv.tokens, "groups": cv.groups, "budget": cfg["budget"], "codes": "progressive"})
+
+
+def build_ladder_context(cfg: dict, seed: int, device):
+    """Config 2's workload through the drop-in API: a 1B random-init model prefills a seeded random context
+    with the reference's score recording (dimmer.prefill_with_scores), a synthetic kvtc checkpoint (seeded
+    rank-1024 orthonormal bases, this context's middle-token means, a rung ladder from ladder_rungs) is
+    written and loaded by KVTCCodec, Methods.apply runs the method (dkvtc@0.02:snap:floor1: per-token rungs,
+    uniform floor, greedy upgrades weighted by the SnapKV scores) and CompressedContext packs the ladder's
+    integer codes. Returns (model, context, codec, Compressed, keys, values)."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    from dimmerkv import dimmer, synthetic
+    from dimmerkv.compressed_attention import CompressedContext
+    from dimmerkv.kvtc import rope_tables as kvtc_rope
+    from dimmerkv.methods import Methods
+
+    model = synthetic.build_model(synthetic.LLAMA_1B, device=device, seed=seed)
+    dimmer.install(model)
+    c = model.config
+    layers, heads, dim = c.num_hidden_layers, c.num_key_value_heads, c.head_dim
+    features = layers * heads * dim
+    tokens = cfg["tmin"]
+    g = torch.Generator().manual_seed(30_000 + seed)
+    ids = torch.randint(0, c.vocab_size, (1, tokens), generator=g).to(device)
+    with torch.inference_mode():
+        cache, scores = dimmer.prefill_with_scores(model, ids)
+    keys = [l.keys.clone() for l in cache.layers]
+    values = [l.values.clone() for l in cache.layers]
+    del cache
+    cos, sin = kvtc_rope(model, tokens, device)
+    start, end = synthetic.SINKS, tokens - synthetic.RECENT
+    streams = {}
+    with torch.inference_mode():
+        for i, (kind, tensors) in enumerate((("key", keys), ("value", values))):
+            basis = synthetic.seeded_basis(features, cfg["max_groups"] * synthetic.GROUP, 2000 + 2 * seed + i, device)
+            matrix = synthetic.token_matrix(tensors, cos, sin) if kind == "key" else synthetic.token_matrix(tensors)
+            mean = matrix[start:end].mean(0)
+            rungs, sizes = synthetic.ladder_rungs((matrix[start:end] - mean) @ basis)
+            streams[kind] = (mean, basis, rungs, sizes)
+            del matrix
+    tmp = Path(tempfile.mkdtemp(prefix="dkv_cfg2_"))
+    try:
+        synthetic.kvtc_checkpoint(tmp / "kvtc.pt", "synthetic-llama-1b", layers, heads, dim, streams)
+        methods = Methods("synthetic-llama-1b", tmp / "none", tmp / "none", device, synthetic.RECENT, model=model,
+                          kvtc=tmp / "kvtc.pt")
+        with torch.inference_mode():
+            compressed = methods.apply(cfg["method"], keys, values, scores)
+        codec = methods.codec("kvtc")
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    with torch.inference_mode():
+        ctx = CompressedContext(codec, keys, values, model, dtype=torch.bfloat16)
+    return model, ctx, codec, compressed, keys, values
+
+
+def ladder_work(codec, ctx, compressed, tokens: int) -> tuple[int, int, int]:
+    """step_work for ladder codes: a token of rung k costs the groups its rung codes (every group of the basis
+    at the exact rung, none when evicted); code bytes under the reference's accounting (Compressed.used_bytes
+    less the exact tokens), re-read every layer."""
+    import torch
+
+    widths = {}
+    for kind in ("key", "value"):
+        stream = codec.streams[kind]
+        coded = (stream.rungs > 0).sum(dim=1).tolist() + [stream.basis.shape[1] // codec.group]
+        choice = codec.last_choice[kind].cpu()
+        per_token = torch.tensor(coded)[choice.clamp_min(0)] * (choice >= 0)
+        widths[kind] = int(per_token.sum()) * codec.group
+    start, end = codec.last_span
+    middle = end - start
+    b = ctx.batch
+    layers = codec.layers
+    key = 2 * widths["key"] * b.n_cols + 2 * middle * b.q_heads * b.head_dim
+    step_flops = layers * (key + 2 * b.q_heads * widths["value"] + 2 * b.q_heads * b.v_width * b.head_dim)
+    code_bytes = compressed.used_bytes - (tokens - middle) * 2 * codec.exact_bytes
+    return key, code_bytes * layers, step_flops
+
+
+def ladder_parity(model, ctx, codec, keys, values, layer: int | None = None) -> dict:
+    """One attention layer of the ladder-coded context on a random query against the oracle (the codec's
+    dequantised coefficients and rung choices, the reference's operand rounding, float64 sums)."""
+    import numpy as np
+    import torch
+
+    from dimmerkv.synthetic import rope_full
+    from oracle.attention import OracleContext
+
+    c = model.config
+    L, H, D, HQ = c.num_hidden_layers, c.num_key_value_heads, c.head_dim, c.num_attention_heads
+    layer = L - 1 if layer is None else layer
+    start, end = codec.last_span
+    dev = ctx.batch.device
+    q = torch.randn(1, HQ, 1, D, generator=torch.Generator().manual_seed(78)).to(torch.bfloat16)
+    ek = torch.cat([keys[layer][..., :start, :], keys[layer][..., end:, :]], dim=2)
+    ev = torch.cat([values[layer][..., :start, :], values[layer][..., end:, :]], dim=2)
+    with torch.inference_mode():
+        got = ctx.batch.attend_layer(layer, q.to(dev), ek, ev, None, D ** -0.5, out_dtype=torch.float32)
+        torch.cuda.synchronize(dev)
+    ctx.batch.check_status()
+    cos, sin = rope_full(model, keys[0].shape[2], dev)
+    oracle = OracleContext(start=start, end=end, layers=L, heads=H, head_dim=D,
+                           choice={k: codec.last_choice[k].cpu().numpy() for k in ("key", "value")},
+                           decoded={k: codec.last_coefficients[k].float().cpu().numpy() for k in ("key", "value")},
+                           basis={k: codec.streams[k].basis.float().cpu().numpy() for k in ("key", "value")},
+                           mean={k: codec.streams[k].mean.float().cpu().numpy() for k in ("key", "value")},
+                           cos=cos.cpu().numpy(), sin=sin.cpu().numpy(), dtype="bf16")
+    want = oracle.attend(layer, q.float().numpy(), ek.float().cpu().numpy(), ev.float().cpu().numpy(), None,
+                         D ** -0.5)
+    err = float(np.abs(got.cpu().numpy() - want).max())
+    return {"max_abs": err, "tolerance": 1e-4, "layer": layer, "conversation_tokens": int(keys[0].shape[2]),
+            "oracle": "oracle/attention.py (float64 sums)", "pass": bool(err < 1e-4)}
+
+
+def measure_cfg2(args, device) -> dict:
+    """Config 2: 1B random-init, one 8192-token conversation compressed with
+    dkvtc@0.02:snap:floor1 through Methods.apply / KVTCCodec.compress (ladder codes), 128 batch-1 decode steps
+    over the codes; one layer checked against the oracle."""
+    import torch
+
+    from dimmerkv.common import build_cache
+
+    cfg = CONFIGS["cfg2"]
+    model, ctx, codec, compressed, keys, values = build_ladder_context(cfg, args.seed, device)
+    tokens = keys[0].shape[2]
+    work = ladder_work(codec, ctx, compressed, tokens)
+    parity = ladder_parity(model, ctx, codec, keys, values)
+    start, end = codec.last_span
+    cache = build_cache([torch.cat([k[..., :start, :], k[..., end:, :]], dim=2) for k in keys],
+                        [torch.cat([v[..., :start, :], v[..., end:, :]], dim=2) for v in values], model)
+    del keys, values
+    ids = torch.randint(0, model.config.vocab_size, (1, 1), generator=torch.Generator().manual_seed(args.seed + 2))
+    warmup = max(3, args.warmup)
+    run = time_decode(model, ctx.batch, cache, ids.to(device), torch.tensor([[tokens]], device=device),
+                      cfg["decode"], warmup, device)
+    budget_bytes = int(cfg["budget"] * tokens * 2 * codec.exact_bytes)
+    hist = {k: round(v, 4) for k, v in sorted(compressed.histogram.items())}
+    return bs1_line("cfg2", cfg, cfg["decode"], warmup, run, work, parity,
+                    {"context": tokens, "method": cfg["method"], "rungs": len(codec.streams["key"].rung_bytes),
+                     "used_bytes": compressed.used_bytes, "budget_bytes": budget_bytes,
+                     "compress_s": round(compressed.seconds, 3), "rung_histogram": hist})
+
+
+def measure_cfg4(args, device) -> dict:
+    """Config 4: question-time refinement of one 32K conversation (run_question)."""
+    return run_question(args, CONFIGS["cfg4"], device)
+
+
+def secondary_configs(args, device) -> dict:
+    """cfg1, cfg2 and cfg4, measured after the headline in the same process so that the default run carries
+    them (extra keys of its line). Each builds its own model and codes; a failure is recorded under its key
+    (with the traceback on stderr) and the next one runs."""
+    import gc
+    import traceback
+
+    import torch
+
+    out = {}
+    for name, fn in (("cfg1", measure_cfg1), ("cfg2", measure_cfg2), ("cfg4", measure_cfg4)):
+        t0 = time.time()
+        try:
+            out[name] = fn(args, device)
+        except Exception as exc:  # noqa: BLE001 - reported in the line, the headline stands
+            traceback.print_exc(file=sys.stderr)
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+        out[name]["wall_s"] = round(time.time() - t0, 1)
+        gc.collect()
+        torch.cuda.empty_cache()
+    return out
 
 
 class _LocalComm:
@@ -1108,6 +1382,13 @@ def run_ours(args, cfg, rank, world, device):
             result["splitk"] = splitk
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_sample(model, convs, bases, lengths, layers=2)
+        if world == 1 and not args.no_configs and args.config == "cfg3":
+            del model, batch, convs, cache
+            import gc
+
+            gc.collect()
+            torch.cuda.empty_cache()
+            result["configs"] = secondary_configs(args, device)
     return result
 
 
@@ -1249,6 +1530,10 @@ def main():
             result = run_question(args, cfg, device)
         elif mode == "splitk":
             result = run_splitk(args, cfg, rank, world, device)
+        elif mode == "ladder":
+            if world > 1:
+                raise SystemExit("cfg2 runs on one GPU")
+            result = measure_cfg2(args, device)
         else:
             result = run_ours(args, cfg, rank, world, device)
         if result is not None:

@@ -193,6 +193,59 @@ def compress_conversation(keys: list[torch.Tensor], values: list[torch.Tensor], 
                                  full if keep_full else None)
 
 
+# kvtc bit widths per group (scripts/kvtc.py:24) as upgrade steps, and the bytes one (token, group) costs at
+# each width (b * group / 8, plus 4 bytes of f16 low / scale once a group is coded, kvtc.py:23).
+_UPGRADES = ((0, 2), (2, 4), (4, 8))
+
+
+def _group_bytes(bits: int, group: int) -> int:
+    return bits * group // 8 + (4 if bits else 0)
+
+
+def ladder_rungs(coefficients: torch.Tensor, group: int = GROUP, max_rungs: int = 48) -> tuple[torch.Tensor, list]:
+    """A synthetic kvtc rung ladder for ``coefficients`` [tokens, groups * group] (the fit a kvtc checkpoint
+    holds, which the reference calibrates offline): rung k is rung k-1 plus one upgrade of one group's
+    width (0 -> 2 -> 4 -> 8 bits), the upgrade with the largest estimated squared-error drop per byte,
+    the error of a group at b bits taken as its energy * 4^-b (its whole energy at 0 bits). Returns
+    (rungs [n, groups] int64 bits, bytes per token of each rung), bytes strictly increasing."""
+    groups = coefficients.shape[1] // group
+    energy = coefficients.float().view(-1, groups, group).square().sum(dim=(0, 2)).double().cpu().tolist()
+    bits = [0] * groups
+    rungs, sizes = [], []
+
+    def err(e: float, b: int) -> float:
+        return e if b == 0 else e * 4.0 ** -b
+
+    while len(rungs) < max_rungs:
+        best, pick = -1.0, None
+        for g in range(groups):
+            step = next((u for u in _UPGRADES if u[0] == bits[g]), None)
+            if step is None:
+                continue
+            gain = (err(energy[g], step[0]) - err(energy[g], step[1])) / (
+                _group_bytes(step[1], group) - _group_bytes(step[0], group))
+            if gain > best:
+                best, pick = gain, (g, step[1])
+        if pick is None:
+            break
+        bits[pick[0]] = pick[1]
+        rungs.append(list(bits))
+        sizes.append(sum(_group_bytes(b, group) for b in bits))
+    return torch.tensor(rungs, dtype=torch.int64), sizes
+
+
+def kvtc_checkpoint(path, model_id: str, layers: int, heads: int, head_dim: int, streams: dict,
+                    group: int = GROUP, sinks: int = SINKS) -> None:
+    """Write a kvtc checkpoint in the layout KVTCCodec loads (model, geometry, group, sinks and per stream
+    mean [F], basis [F, R], rungs, rung_bytes) from ``streams[kind] = (mean, basis, rungs, rung_bytes)``."""
+    saved = {"model": model_id, "layers": layers, "heads": heads, "head_dim": head_dim, "group": group,
+             "sinks": sinks}
+    for kind, (mean, basis, rungs, sizes) in streams.items():
+        saved[kind] = {"mean": mean.float().cpu(), "basis": basis.float().cpu(), "rungs": rungs.cpu(),
+                       "rung_bytes": [int(x) for x in sizes]}
+    torch.save(saved, path)
+
+
 def prefill(model, ids: torch.Tensor, chunk: int = 4096):
     """Prefill [1, T] with the model's own (sdpa) attention, chunked; returns per-layer keys, values."""
     from transformers import DynamicCache

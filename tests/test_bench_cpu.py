@@ -57,3 +57,48 @@ def test_step_roofline_picks_the_binding_side():
     assert 0 < line["frac"] < 1
     peaks = bench.measured_peaks()
     assert abs(line["min_ms"] - 137e12 / (peaks["bf16_tflops_sustained"] * 1e12) * 1e3) < 1e-2
+
+
+def test_synthetic_ladder_feeds_the_drop_in_codec(tmp_path):
+    """cfg2's producer on the host: ladder_rungs gives strictly growing rungs of one upgrade each (kvtc widths
+    0/2/4/8), kvtc_checkpoint writes a file KVTCCodec loads, and Methods.apply("dkvtc@0.02:snap:floor1")
+    compresses a cache with it within the budget, keeping the ladder's integer codes."""
+    import torch
+
+    import tinymodel as tm
+    from dimmerkv import dimmer
+    from dimmerkv.kvtc import rope_tables, rung_bytes
+    from dimmerkv.methods import Methods
+
+    model = tm.build_model(torch.float32, "cpu")
+    dimmer.install(model)
+    c = model.config
+    layers, heads, dim = c.num_hidden_layers, c.num_key_value_heads, c.head_dim
+    features, tokens = layers * heads * dim, 4000  # 2% must cover the 36 exact tokens and the coarsest rungs
+    g = torch.Generator().manual_seed(5)
+    keys = [torch.randn(1, heads, tokens, dim, generator=g) for _ in range(layers)]
+    values = [torch.randn(1, heads, tokens, dim, generator=g) for _ in range(layers)]
+    cos, sin = rope_tables(model, tokens, "cpu")
+    start, end = synthetic.SINKS, tokens - synthetic.RECENT
+    streams = {}
+    for i, (kind, tensors) in enumerate((("key", keys), ("value", values))):
+        basis = synthetic.seeded_basis(features, 4 * 64, 40 + i, "cpu")
+        matrix = synthetic.token_matrix(tensors, cos, sin) if kind == "key" else synthetic.token_matrix(tensors)
+        mean = matrix[start:end].mean(0)
+        rungs, sizes = synthetic.ladder_rungs((matrix[start:end] - mean) @ basis)
+        assert rungs.shape == (12, 4)  # 4 groups x 3 upgrades
+        assert all(a < b for a, b in zip(sizes, sizes[1:]))
+        assert sizes == [rung_bytes(r, 64) for r in rungs]
+        steps = (rungs[1:] != rungs[:-1]).sum(dim=1)
+        assert bool((steps == 1).all()) and set(rungs.unique().tolist()) <= {0, 2, 4, 8}
+        streams[kind] = (mean, basis, rungs, sizes)
+    synthetic.kvtc_checkpoint(tmp_path / "kvtc.pt", "tiny-synthetic", layers, heads, dim, streams)
+    scores = {"snap": [torch.rand(heads, tokens, generator=g) for _ in range(layers)]}
+    methods = Methods("tiny-synthetic", tmp_path / "none", tmp_path / "none", torch.device("cpu"), synthetic.RECENT,
+                      model=model, kvtc=tmp_path / "kvtc.pt")
+    with torch.inference_mode():
+        out = methods.apply("dkvtc@0.02:snap:floor1", keys, values, scores)
+    codec = methods.codec("kvtc")
+    assert out.used_bytes <= int(0.02 * tokens * 2 * codec.exact_bytes)
+    assert codec.last_codes is not None and codec.last_codes["key"].kind == 1
+    assert int((codec.last_choice["key"] >= 0).sum()) == end - start

@@ -108,3 +108,20 @@ def test_bench_geometry_60_to_63_groups_matches_oracle():
             assert np.isfinite(err) and err < TOL_F32, (shapes[s], layer, err)
         del ctx
     assert len(errors) == S * len(layers)
+
+
+def test_cfg2_ladder_workload_matches_oracle():
+    """BASELINE configs[1]'s producer and codes on a 4096-token context: the 1B random-init model's prefill,
+    a synthetic kvtc checkpoint, Methods.apply("dkvtc@0.02:snap:floor1") (KVTCCodec.compress with SnapKV
+    weights and the uniform floor) and CompressedContext over the ladder's integer codes; the first and last
+    layers against the oracle on the codec's own coefficients and choices at 1e-4 (the bench's cfg2 leg runs
+    the same check on its 8192-token context)."""
+    import bench
+
+    cfg = dict(bench.CONFIGS["cfg2"], tmin=4096, tmax=4096)
+    model, ctx, codec, compressed, keys, values = bench.build_ladder_context(cfg, 0, DEV)
+    assert codec.last_codes["key"].kind == 1 and ctx.batch.pair_keys
+    assert compressed.used_bytes <= int(cfg["budget"] * 4096 * 2 * codec.exact_bytes)
+    for layer in (0, model.config.num_hidden_layers - 1):
+        res = bench.ladder_parity(model, ctx, codec, keys, values, layer)
+        assert res["pass"], res
