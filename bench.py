@@ -52,8 +52,8 @@ CONFIGS = {
                           "(split-K, log-sum-exp merge over NCCL), bs1 decode"),
 }
 METRIC = "decode tok/s over compressed KV (3B,16K,bs64)"
-# Kernels of one attention layer (one row chunk): key_scores_pair, softmax_stats, vprobs, value_dense (or
-# value_weights), vbasis, combine; plus, once per step, the unpack of the value planes.
+# Kernels of one attention layer (one row chunk): key_scores_dense (or key_scores_pair), softmax_stats, vprobs,
+# value_dense (or value_weights), vbasis, combine; plus, once per step, the unpack of the key and value planes.
 KERNELS_PER_LAYER = 6
 
 
@@ -357,7 +357,7 @@ class StageTimer:
         self.batch, self.stream, self.events, self.unpack_events = batch, stream, [], []
 
     def unpack(self, launch):
-        """Events around the once-per-step decode of the value planes (CompressedBatch._dense_values)."""
+        """Events around a once-per-step decode of the key or value planes (CompressedBatch._dense_stream)."""
         import torch
 
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -387,7 +387,7 @@ class StageTimer:
     def stage_ms(self, steps: int):
         out = {name: round(sum(ev[i].elapsed_time(ev[i + 1]) for ev in self.events) / steps, 3)
                for i, name in enumerate(self.NAMES)}
-        out["value_unpack"] = round(sum(a.elapsed_time(b) for a, b in self.unpack_events) / steps, 3)
+        out["unpack"] = round(sum(a.elapsed_time(b) for a, b in self.unpack_events) / steps, 3)
         return out
 
 
@@ -819,8 +819,11 @@ def run_question(args, cfg, device) -> dict:
         imp = question_importance_direct(model, batch, cache, tail, [tokens])[0]
         ev[1].record(stream)
         selected = batch.select_top([count])
+        side = torch.cuda.Stream(device)
         ev[2].record(stream)
-        fetched = batch.refine(selected, [cold], torch.cuda.Stream(device))
+        t_call = time.perf_counter()
+        fetched = batch.refine(selected, [cold], side)
+        refine_call_s = time.perf_counter() - t_call
         ev[3].record(stream)
         torch.cuda.synchronize(device)
         gc.enable()
@@ -862,6 +865,7 @@ def run_question(args, cfg, device) -> dict:
             "config": {"workload": cfg["workload"], "context": tokens, "groups": conv.groups, "refined": count},
             "phases_ms": {k: round(v, 3) for k, v in phases.items()}, "fetched_bytes": fetched,
             "refine_host_ms": {k: round(v * 1e3, 3) for k, v in getattr(batch, "last_refine_seconds", {}).items()},
+            "refine_call_host_ms": round(refine_call_s * 1e3, 3),
             "topk_matches_lowest_index_rule": exact, "importance_roofline": imp_roof,
             "answer_after_refine": {"question_tokens": cfg["question"], "decode_steps": cfg["decode"],
                                     "seconds": round(answer_s, 3), "decode_tok_s": round(cfg["decode"] / answer_s, 2),

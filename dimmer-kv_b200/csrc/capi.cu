@@ -153,6 +153,16 @@ int dkv_key_scores(const dkv_attend_args* a, void* stream) {
   if (pairs) {
     // Two CTAs per cluster; grid_k counts the schedule's lists (one per cluster).
     const int clusters = a->grid_k > 0 ? a->grid_k : sm_count() / 2;
+    if (a->k_dense != nullptr) {
+      // Key coefficients decoded once per step: both operands by TMA (64 x 128 boxes of the decoded buffer).
+      if (a->n_k_tiles <= 0 || (reinterpret_cast<uintptr_t>(a->k_dense) & 15u) != 0) return DKV_ERR_ARGS;
+      CUtensorMap amap;
+      rc = basis_map(a->k_dense, static_cast<uint64_t>(a->n_k_tiles) * 128, static_cast<uint64_t>(a->k_width), 128u,
+                     &amap, a->fp16);
+      if (rc != DKV_OK) return rc;
+      p.n_tiles = a->n_k_tiles;
+      return dkv::run_key_scores_dense(map, amap, p, 2 * clusters, static_cast<cudaStream_t>(stream));
+    }
     return dkv::run_key_scores_pair(map, p, 2 * clusters, static_cast<cudaStream_t>(stream));
   }
   const int grid = a->grid_k > 0 ? a->grid_k : (a->n_k_items < sm_count() ? a->n_k_items : sm_count());

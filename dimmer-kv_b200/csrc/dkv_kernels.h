@@ -48,9 +48,13 @@ struct KeyScoreParams {
   const int32_t* pairs;           // CTA-pair kernel: [n_pairs][4] = tile 0, tile 1 (-1: none), merged groups,
                                   // first pair_groups entry; items = pair * (n_cols / 512) + column block
   const int32_t* pair_groups;     // [entries][4] = union group, descriptor of tile 0, of tile 1 (-1: none), 0
+  int n_tiles;                    // key tiles (rows of the decoded key buffer / 128, for the dense kernel)
 };
 int run_key_scores(const CUtensorMap& bmap, const KeyScoreParams& p, int nb, int grid, cudaStream_t stream);
 int run_key_scores_pair(const CUtensorMap& bmap, const KeyScoreParams& p, int grid, cudaStream_t stream);
+// The CTA-pair key kernel over key coefficients decoded once per step (key_scores_dense.cu).
+int run_key_scores_dense(const CUtensorMap& bmap, const CUtensorMap& amap, const KeyScoreParams& p, int grid,
+                         cudaStream_t stream);
 
 // Softmax statistics over compressed + exact tokens (softmax.cu).
 struct SoftmaxParams {

@@ -35,6 +35,7 @@ constexpr int kSiteKey = 2000;         // key_scores_kernel (one CTA per item)
 constexpr int kSiteValue = 3000;       // value_weights_kernel / vprobs_kernel (planes decoded per layer)
 constexpr int kSiteValueDense = 4000;  // value_dense_kernel (coefficients decoded once per step)
 constexpr int kSiteUnpack = 5000;      // unpack_kernel
+constexpr int kSiteKeyDense = 6000;    // key_scores_dense_kernel (coefficients decoded once per step)
 
 // Bound on one wait. Healthy waits in these kernels last microseconds; a wait gives up after 2 s of
 // %globaltimer time. The time is summed over polls in steps clamped to 100 ms (a step backwards counts as

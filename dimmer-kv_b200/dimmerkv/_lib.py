@@ -52,6 +52,7 @@ class AttendArgs(ctypes.Structure):
         ("k_cta_begin", c_void_p), ("k_item_order", c_void_p), ("v_cta_begin", c_void_p), ("v_item_order", c_void_p),
         ("k_pairs", c_void_p), ("k_pair_groups", c_void_p), ("softmax_mode", c_int32),
         ("p_img", c_void_p), ("n_v_tiles", c_int32), ("v_dense", c_void_p), ("fp16", c_int32),
+        ("k_dense", c_void_p), ("n_k_tiles", c_int32),
     ]
 
 
@@ -190,7 +191,8 @@ def check(rc: int, what: str) -> None:
         raise DimmerKVError(f"{what}: {STATUS_TEXT.get(rc, rc)}")
 
 
-DEVICE_SITES = {1: "key_scores_pair", 2: "key_scores", 3: "value_weights", 4: "value_dense", 5: "unpack"}
+DEVICE_SITES = {1: "key_scores_pair", 2: "key_scores", 3: "value_weights", 4: "value_dense", 5: "unpack",
+                6: "key_scores_dense"}
 
 
 def describe_device_error(code: int) -> str:

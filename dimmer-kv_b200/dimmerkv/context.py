@@ -176,7 +176,7 @@ class CompressedBatch:
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
                  device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None,
-                 pair_keys: bool = True, dense_values: bool = True):
+                 pair_keys: bool = True, dense_values: bool = True, dense_keys: bool = True):
         """``basis[kind]``: [F, F] (or [F, >= union]) float basis, columns = PCA components (the codec's
         ``stream.basis``); ``mean[kind]``: [F] shared or [n_conv, F] per conversation; ``cos/sin``:
         [positions, head_dim // 2] tables (``rope_tables``); ``union[kind]`` (optional) fixes the coefficient
@@ -185,7 +185,9 @@ class CompressedBatch:
         (two SMs per item, half the basis traffic each); ``dense_values`` decodes the value planes once per
         decode step (at layer 0, dkv_unpack) into a tile-padded bf16 buffer of the value stream that every
         layer's value stage streams with TMA, instead of decoding the planes again in every layer (the
-        coefficients are the same for all layers); it holds n_value_tiles * 128 * v_width bf16 values."""
+        coefficients are the same for all layers); it holds n_value_tiles * 128 * v_width bf16 values;
+        ``dense_keys`` does the same for the key planes when the CTA-pair key kernel runs (n_key_tiles * 128 *
+        k_width values), so that every layer's key rebuild streams its coefficients with TMA."""
         if dtype not in (torch.bfloat16, torch.float16):
             raise NotImplementedError(f"the sm_100a kernels take bf16 or fp16 operands, not {dtype}")
         if dtype == torch.float16 and not pair_keys:
@@ -242,9 +244,10 @@ class CompressedBatch:
         self._work: dict = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.dense_values = dense_values
-        self._v_dense = None
-        self._v_dense_version = None
-        self._v_version = 0  # bumped whenever the value stream changes (refine, demote)
+        self.dense_keys = dense_keys
+        self._dense = {"key": None, "value": None}            # decoded coefficients per stream
+        self._dense_version = {"key": None, "value": None}    # the stream version they were decoded from
+        self._v_version = 0  # bumped whenever the key or value stream changes (refine, demote)
         self._poller = None
         self.poll_wait_s = 60.0  # bound of one host wait in poll_status
         self.timer = None  # optional callable(kind, fn) wrapping launches (used by the bench)
@@ -364,29 +367,34 @@ class CompressedBatch:
         self._v_items_cache[rows_pad] = out
         return out
 
-    def _dense_values(self, layer: int):
-        """The value coefficients decoded by dkv_unpack into the tile-padded bf16 buffer [n_tiles * 128,
-        v_width] (tile t's tokens at rows t * 128 .., the other rows zero): decoded at layer 0 of every decode
-        step and whenever the value stream changed since; None when disabled or without value tiles."""
-        vs = self.values
-        if not self.dense_values or vs.n_tiles == 0:
+    def _dense_stream(self, kind: str, layer: int):
+        """The coefficients of one stream decoded by dkv_unpack into a tile-padded 16-bit buffer [n_tiles *
+        128, width] (tile t's tokens at rows t * 128 .., zeros for the groups a tile does not hold, the other
+        rows zero): decoded at layer 0 of every decode step and whenever the streams changed since; None when
+        disabled, without tiles, or (keys) without the CTA-pair key kernel."""
+        packed = self.keys if kind == "key" else self.values
+        width = self.k_width if kind == "key" else self.v_width
+        on = self.dense_keys and self.k_pairs is not None if kind == "key" else self.dense_values
+        if not on or packed.n_tiles == 0:
             return None
-        rows = vs.n_tiles * 128
-        if self._v_dense is None or tuple(self._v_dense.shape) != (rows, self.v_width):
-            self._v_dense = torch.zeros(rows, self.v_width, dtype=self.dtype, device=self.device)
-            self._v_dense_version = None
-        if layer == 0 or self._v_dense_version != self._v_version:
-            a = _lib.UnpackArgs(vs.code.data_ptr(), vs.code.numel(), vs.tiles.data_ptr(), vs.n_tiles,
-                                vs.groups.data_ptr(), self._v_dense.data_ptr(), self.v_width, 1,
-                                self.status.data_ptr(), vs.max_planes, 128, int(self.dtype == torch.float16))
+        rows = packed.n_tiles * 128
+        buf = self._dense[kind]
+        if buf is None or tuple(buf.shape) != (rows, width):
+            buf = self._dense[kind] = None  # free the old buffer before the new one is allocated
+            buf = self._dense[kind] = torch.zeros(rows, width, dtype=self.dtype, device=self.device)
+            self._dense_version[kind] = None
+        if layer == 0 or self._dense_version[kind] != self._v_version:
+            a = _lib.UnpackArgs(packed.code.data_ptr(), packed.code.numel(), packed.tiles.data_ptr(), packed.n_tiles,
+                                packed.groups.data_ptr(), buf.data_ptr(), width, 1, self.status.data_ptr(),
+                                packed.max_planes, 128, int(self.dtype == torch.float16))
             stream = torch.cuda.current_stream(self.device).cuda_stream
             launch = lambda: _lib.check(self.lib.dkv_unpack(a, stream), "dkv_unpack")
             if self.timer is not None and hasattr(self.timer, "unpack"):
                 self.timer.unpack(launch)
             else:
                 launch()
-            self._v_dense_version = self._v_version
-        return self._v_dense
+            self._dense_version[kind] = self._v_version
+        return buf
 
     def _score_offsets(self, q_len: int) -> tuple[torch.Tensor, int]:
         """(per-conversation offsets into the score buffer on the device, total scores) for q_len rows per
@@ -462,8 +470,11 @@ class CompressedBatch:
         a.v_item_ranges, a.v_tile_chunk = v_spans.data_ptr(), self.tile_chunk
         a.vpart = ptr("vpart")
         a.p_img, a.n_v_tiles = ptr("p_img"), vs.n_tiles
-        dense = self._dense_values(layer) if scratch else None
+        dense = self._dense_stream("value", layer) if scratch else None
         a.v_dense = dense.data_ptr() if dense is not None else None
+        dense_k = self._dense_stream("key", layer) if scratch else None
+        a.k_dense = dense_k.data_ptr() if dense_k is not None else None
+        a.n_k_tiles = ks.n_tiles
         a.fp16 = int(self.dtype == torch.float16)
         a.k_cta_begin, a.k_item_order, a.grid_k = self.k_cta_begin.data_ptr(), None, int(self.k_cta_begin.numel()) - 1
         a.k_pairs = self.k_pairs.data_ptr() if self.k_pairs is not None else None

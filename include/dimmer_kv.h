@@ -146,6 +146,13 @@ typedef struct dkv_attend_args {
    * CompressedContext dtype). Probabilities are rounded to it where the reference rounds them. fp16 needs the
    * CTA-pair key kernel (k_pairs). */
   int32_t fp16;
+  /* Optional: the key coefficients decoded once per decode step by dkv_unpack of the key stream (16-bit in
+   * the cache dtype, out_tile_rows = 128: [n_k_tiles * 128][k_width], key tile t's tokens at rows t * 128 ..,
+   * zeros for groups a tile does not hold), 16-byte aligned. Given with k_pairs, the key stage streams them
+   * with TMA instead of decoding the planes again in every layer (the coefficients are the same for every
+   * layer); NULL decodes the planes in the key kernel. */
+  const void* k_dense;
+  int32_t n_k_tiles;
 } dkv_attend_args;
 
 /* Floats of dkv_attend_args.vpart for a value basis of v_width components. */

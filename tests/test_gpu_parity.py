@@ -230,8 +230,9 @@ def test_ragged_batch_matches_oracle_per_conversation():
 def _check_3b_geometry(shapes, q, seed, dense=True, dtype=torch.bfloat16):
     """Conversations of the given (middle tokens, groups) at the bench's attention geometry (Llama-3.2-3B:
     8 KV heads of 128, 24 query heads, GQA 3), one launch per layer, q query rows, each conversation
-    against the oracle. ``dense``: the value stage reads the coefficients decoded once per step
-    (value_dense.cu) or decodes the planes itself (value_weights.cu)."""
+    against the oracle. ``dense``: the key and value stages read the coefficients decoded once per step
+    (key_scores_dense.cu, value_dense.cu) or decode the planes themselves (key_scores_pair.cu,
+    value_weights.cu)."""
     rng = np.random.default_rng(seed)
     L, H, D, HQ = 2, 8, 128, 24
     F = L * H * D
@@ -255,7 +256,7 @@ def _check_3b_geometry(shapes, q, seed, dense=True, dtype=torch.bfloat16):
         raw.append(c)
     batch = CompressedBatch(convs, layers=L, kv_heads=H, head_dim=D, q_heads=HQ, basis=basis, mean=mean,
                             cos=cos_full[:, : D // 2], sin=sin_full[:, : D // 2], device=DEV, dense_values=dense,
-                            dtype=dtype)
+                            dense_keys=dense, dtype=dtype)
     S, E = len(shapes), 40
     query = torch.randn(S, HQ, q, D, generator=g).to(dtype)
     ek = torch.randn(S, H, E, D, generator=g).to(dtype)
@@ -280,17 +281,18 @@ def _check_3b_geometry(shapes, q, seed, dense=True, dtype=torch.bfloat16):
             assert err < TOL_F32, (layer, s, err)
 
 
-@pytest.mark.parametrize("dense", [True, False], ids=["dense_values", "decoding_values"])
+@pytest.mark.parametrize("dense", [True, False], ids=["dense", "decoding"])
 @pytest.mark.parametrize("q", [1, 4])
 def test_ragged_batch_3b_geometry_matches_oracle(q, dense):
     """Four ragged conversations in one launch: up to 2100 middle tokens (an odd number of tiles, so one
-    CTA pair holds a single tile) and 16 coefficient groups; both value kernels."""
+    CTA pair holds a single tile) and 16 coefficient groups; both key kernels and both value kernels."""
     _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), q, 11 + q, dense)
 
 
-@pytest.mark.parametrize("dense", [True, False], ids=["dense_values", "decoding_values"])
+@pytest.mark.parametrize("dense", [True, False], ids=["dense", "decoding"])
 def test_ragged_batch_3b_geometry_fp16_matches_oracle(dense):
-    """The same ragged launch with fp16 operands (the reference's default cache dtype), both value kernels."""
+    """The same ragged launch with fp16 operands (the reference's default cache dtype), both key and value
+    kernels."""
     _check_3b_geometry(((2100, 16), (130, 3), (1000, 9), (257, 1)), 1, 71, dense, torch.float16)
 
 
