@@ -401,12 +401,12 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "of fallback"}
 
 
-KEY_KERNEL_SOURCES = ("key_scores_pair.cu", "dkv_ptx.cuh", "dkv_format.cuh", "dkv_kernels.h")
+KEY_KERNEL_SOURCES = ("key_scores_dense.cu", "dkv_ptx.cuh", "dkv_format.cuh", "dkv_kernels.h")
 
 
 def key_kernel_source_hash() -> str:
-    """sha256 (first 16 hex digits) of the sources the CTA-pair key kernel is compiled from: a profile of the
-    kernel is used for the line's traffic only while it was captured from these exact sources."""
+    """sha256 (first 16 hex digits) of the sources the bench's key kernel (key_scores_dense) is compiled from: a
+    profile of the kernel is used for the line's traffic only while it was captured from these exact sources."""
     import hashlib
 
     h = hashlib.sha256()
