@@ -40,10 +40,6 @@ constexpr int kKdA = 16384;                  // 128 token rows x 64 components x
 constexpr int kKdBHalf = kKdHalfCols * 128;  // 128 basis rows x 64 components x 16 bit
 constexpr int kKdStage = kKdA + 2 * kKdBHalf;
 constexpr int kKdStages = 4;
-#ifndef DKV_KD_PREFETCH
-#define DKV_KD_PREFETCH 16
-#endif
-constexpr int kKdPrefetch = DKV_KD_PREFETCH;  // A boxes brought into L2 ahead of their stage load
 
 }  // namespace
 
@@ -128,33 +124,6 @@ __global__ void __launch_bounds__(kKdThreads, 1)
       prefetch_tensormap(&bmap);
       prefetch_tensormap(&amap);
       uint32_t s_iter = 0;
-      // L2 prefetch cursor over the same (item, merged group) sequence, kept kKdPrefetch boxes ahead of the
-      // stage loads: the A boxes come from HBM (the decoded buffer is far larger than L2), the basis boxes
-      // are shared by every CTA and stay in L2.
-      int pk = items.k, pn = -1, pgi = 0, pfirst = 0, pti = -1;
-      uint32_t pf_pos = 0;
-      auto pf_step = [&]() -> bool {
-        for (;;) {
-          if (pk >= items.end) return false;
-          if (pn < 0) {
-            int pair, nblk;
-            if (!item_at(pk, pair, nblk, pn, pfirst)) {
-              pk = items.end;
-              return false;
-            }
-            pti = p.pairs[4 * pair + rank];
-            pgi = 0;
-          }
-          if (pgi < pn) break;
-          pk += items.step;
-          pn = -1;
-        }
-        const uint32_t g = static_cast<uint32_t>(__ldg(p.pair_groups + 4 * (pfirst + pgi)));
-        if (pti >= 0 && pti < p.n_tiles && g < p.n_union_groups)
-          tma_prefetch_l2_2d(&amap, static_cast<int>(g) * kGroup, pti * kTileTokens);
-        ++pgi;
-        return true;
-      };
       for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
         int pair, nblk, n_merged, first;
         if (!item_at(k, pair, nblk, n_merged, first)) {
@@ -177,7 +146,6 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             ok = false;
             break;
           }
-          while (pf_pos < s_iter + kKdPrefetch && pf_step()) ++pf_pos;
           const int s = s_iter % kKdStages;
           if (s_iter >= kKdStages &&
               !mbar_wait(&empty[s], ((s_iter / kKdStages) - 1) & 1, p.status, kSiteKeyDense + kErrWaitEmpty, abort_flag)) {
