@@ -197,6 +197,11 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Bring the line holding addr into L1 (no data returned, nothing to wait for).
+__device__ __forceinline__ void prefetch_l1(const void* addr) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(addr)));
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -275,14 +275,20 @@ __global__ void __launch_bounds__(kKdThreads, 1)
       pos = hidden ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
       const uint16_t* cosrow = reinterpret_cast<const uint16_t*>(p.cos_t) + static_cast<int64_t>(pos) * (D / 2);
       const uint16_t* sinrow = reinterpret_cast<const uint16_t*>(p.sin_t) + static_cast<int64_t>(pos) * (D / 2);
-      if (accumulated) {
-        if (!warp_wait(accum_full, item_iter & 1, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
-          give_up();
-          break;
-        }
+      // The accumulator is waited for as late as possible: the first query row's q and mean loads (and the
+      // RoPE rows' way into L1) happen while the item's MMAs still run.
+      auto wait_accum = [&]() -> bool {
+        if (!warp_wait(accum_full, item_iter & 1, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) return false;
         tc_fence_after();
+        return true;
+      };
+      if (accumulated && !has_tile && !wait_accum()) {
+        give_up();
+        break;
       }
       if (has_tile) {
+        prefetch_l1(cosrow);
+        prefetch_l1(sinrow);
         const int s = tile.seq;
         const int64_t m_s = p.seq_m[s];
         float* out_base = p.scores + p.seq_score_off[s];
@@ -304,7 +310,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
                                    static_cast<int64_t>(p.layer) * p.n_cols + nblk * kKdCols;
             for (int i = et; i < kKdCols; i += kKdEpilogueThreads) mean_s[i] = half_to_float<F16>(mrow[i]);
           }
-          if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
+          if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag) ||
+              (qi == 0 && accumulated && !wait_accum())) {
             give_up();
             failed = true;
             break;
