@@ -15,15 +15,11 @@
 // two) x 512 key columns, its groups the sorted union of the two tiles' groups. Per merged group each CTA
 // loads one stage: its tile's 128 x 64 coefficient box (A, 16 KB) and 128 of each pair MMA's 256 basis
 // rows (B, 2 x 16 KB). The even CTA issues M = 256 (128 rows of each CTA) x N = 256 pair MMAs, two per
-// K step, into a 512-column fp32 accumulator per CTA. The epilogue reads the accumulator's two 256-column
-// halves one after the other and frees each as soon as it is read: the next item's MMAs into the first half
-// start while the epilogue still reads the second (up to a ring of stages ahead, their second-half MMAs
-// held back until that half is free). Roles (640 threads, no register reallocation):
+// K step, into a 512-column fp32 accumulator per CTA. Roles (640 threads, no register reallocation):
 //   warp 0      producer: A and B boxes of every merged group into a ring of stages (TMA, no multicast)
 //   warp 1      even CTA: pair MMA issuer; odd CTA: forwards its stage completions to the even CTA
-//   warps 4-19  epilogue, four warps per TMEM lane quarter (warp % 4): per half, TMEM -> + mean -> RoPE ->
-//               q.k for each head's query group -> fp32 scores; with head_dim 128 (two heads per half) two
-//               warps share a head (one half of its RoPE pairs each) and add their partial products
+//   warps 4-19  epilogue, four warps per TMEM lane quarter (warp % 4), each one KV head of the item (two
+//               for head_dim 64): TMEM -> + mean -> RoPE -> q.k for the head's query group -> fp32 scores
 // Every wait is bounded and abort-aware (dkv_ptx.cuh); the abort flag is cluster-wide; the kernel does
 // no work when the call's status word is already set.
 #include "dkv_ptx.cuh"
@@ -51,26 +47,22 @@ template <int D, int G, bool F16>
 __global__ void __launch_bounds__(kKdThreads, 1)
     key_scores_dense_kernel(const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap amap,
                             const KeyScoreParams p) {
-  constexpr int kHeads = kKdCols / D;          // KV heads per item
-  constexpr int kHalfHeads = kHeads / 2;       // KV heads per accumulator half (2 or 4)
-  constexpr int kSplit = 4 / kHalfHeads;       // epilogue warps per head and quarter (2 or 1)
-  constexpr int kChunks = (D / 2) / kSplit;    // RoPE pair dims of a warp's share of its head
+  constexpr int kHeads = kKdCols / D;        // KV heads per item
+  constexpr int kSetHeads = kHeads / 4;      // heads per epilogue warp
   constexpr uint32_t kIdesc = idesc_f16(256, kKdMmaN, /*is_bf16=*/!F16, false, false);
-  static_assert(kHalfHeads * kSplit == 4 && kChunks % 16 == 0, "epilogue split");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;                                                // [kKdStages][A | B half 0 | B half 1]
   float* q_s = reinterpret_cast<float*>(smem + kKdStages * kKdStage);   // [kHeads * G][D]
   float* mean_s = q_s + kHeads * G * D;                                  // [kKdCols]
-  float* red_s = mean_s + kKdCols;                                       // [kHalfHeads][G][128] partial q.k
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red_s + kHalfHeads * G * 128);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(mean_s + kKdCols);
   uint64_t* full = bars;                       // [kKdStages] this CTA's A and B boxes (TMA)
   uint64_t* peer_full = full + kKdStages;      // [kKdStages] even CTA: the odd CTA's forward
   uint64_t* empty = peer_full + kKdStages;     // [kKdStages] pair-MMA commit (both CTAs)
   uint64_t* accum_full = empty + kKdStages;    // pair-MMA commit at the end of an item
-  uint64_t* accum_empty = accum_full + 1;      // [2] per half, even CTA: 2 x 16 epilogue warp arrivals
-  uint64_t* mma_done = accum_empty + 2;        // even CTA: every issued pair MMA has completed
+  uint64_t* accum_empty = accum_full + 1;      // even CTA: 2 x 16 epilogue warp arrivals
+  uint64_t* mma_done = accum_empty + 1;        // even CTA: every issued pair MMA has completed
   uint64_t* ep_sync = mma_done + 1;            // [2] epilogue rendezvous (512 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_sync + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -90,8 +82,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
       mbar_init(&empty[i], 1);
     }
     mbar_init(accum_full, 1);
-    mbar_init(&accum_empty[0], 2 * kKdEpilogueWarps);
-    mbar_init(&accum_empty[1], 2 * kKdEpilogueWarps);
+    mbar_init(accum_empty, 2 * kKdEpilogueWarps);
     mbar_init(mma_done, 1);
     mbar_init(&ep_sync[0], kKdEpilogueThreads);
     mbar_init(&ep_sync[1], kKdEpilogueThreads);
@@ -189,67 +180,47 @@ __global__ void __launch_bounds__(kKdThreads, 1)
       // ---------------------------------------------------------- pair MMA issuer (even CTA)
       if (lane == 0) {
         uint32_t s_iter = 0, item_iter = 0;
-        // MMAs of one stage into accumulator half hf (four K steps of 16).
-        auto issue = [&](int st, int hf, bool first_group) {
-          const uint32_t a_base = smem_u32(stages + st * kKdStage);
-          const uint32_t b_base = a_base + kKdA + hf * kKdBHalf;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_pair(tmem + hf * kKdMmaN, smem_desc_sw128(a_base + 32 * kk, 16, 1024),
-                         smem_desc_sw128(b_base + 32 * kk, 16, 1024), kIdesc, (!first_group || kk > 0) ? 1u : 0u);
-        };
-        bool ok = true;
-        for (int k = items.k; k < items.end && ok && !*abort_flag; k += items.step) {
+        for (int k = items.k; k < items.end && !*abort_flag; k += items.step) {
           int pair, nblk, n_merged, first;
           if (!item_at(k, pair, nblk, n_merged, first)) break;  // reported by the producer
           if (n_merged <= 0) continue;
-          const uint32_t prev = (item_iter - 1) & 1;  // phase of the previous item's release
-          // The first half is free once the epilogue has read the previous item's first half.
           if (item_iter >= 1 &&
-              !mbar_wait(&accum_empty[0], prev, p.status, kSiteKeyDense + kErrWaitAccumFree, abort_flag)) {
-            ok = false;
+              !mbar_wait(accum_empty, (item_iter - 1) & 1, p.status, kSiteKeyDense + kErrWaitAccumFree, abort_flag)) {
+            give_up();
             break;
           }
           tc_fence_after();
-          // Second-half MMAs wait for the second half; until then they are held back, their stages kept.
-          bool hi_free = item_iter == 0;
-          uint32_t held = s_iter;  // first stage whose second-half MMAs are held back
+          bool ok = true;
           for (int gi = 0; gi < n_merged; ++gi) {
-            const int st = s_iter % kKdStages;
+            const int s = s_iter % kKdStages;
             const uint32_t par = (s_iter / kKdStages) & 1;
-            if (!mbar_wait(&full[st], par, p.status, kSiteKeyDense + kErrWaitA, abort_flag) ||
-                !mbar_wait(&peer_full[st], par, p.status, kSiteKeyDense + kErrWaitBasis, abort_flag)) {
+            if (!mbar_wait(&full[s], par, p.status, kSiteKeyDense + kErrWaitA, abort_flag) ||
+                !mbar_wait(&peer_full[s], par, p.status, kSiteKeyDense + kErrWaitBasis, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue(st, 0, gi == 0);
-            if (hi_free) {
-              issue(st, 1, gi == 0);
-              mma_commit_pair(&empty[st], 0x3);
+            const uint32_t a_base = smem_u32(stages + s * kKdStage);
+            const uint32_t b_base = a_base + kKdA;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t adesc = smem_desc_sw128(a_base + 32 * kk, 16, 1024);
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const uint64_t bdesc = smem_desc_sw128(b_base + hf * kKdBHalf + 32 * kk, 16, 1024);
+                mma_f16_pair(tmem + hf * kKdMmaN, adesc, bdesc, kIdesc, (gi > 0 || kk > 0) ? 1u : 0u);
+              }
             }
+            mma_commit_pair(&empty[s], 0x3);
             ++s_iter;
-            if (!hi_free && (s_iter - held == static_cast<uint32_t>(kKdStages) || gi == n_merged - 1 ||
-                             mbar_test_wait(&accum_empty[1], prev))) {
-              if (!mbar_wait(&accum_empty[1], prev, p.status, kSiteKeyDense + kErrWaitAccumFree, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const int g_held = gi - static_cast<int>(s_iter - 1 - held);  // group of the first held stage
-              for (uint32_t u = held; u < s_iter; ++u) {
-                const int su = u % kKdStages;
-                issue(su, 1, g_held + static_cast<int>(u - held) == 0);
-                mma_commit_pair(&empty[su], 0x3);
-              }
-              hi_free = true;
-            }
           }
-          if (!ok) break;
+          if (!ok) {
+            give_up();
+            break;
+          }
           mma_commit_pair(accum_full, 0x3);
           ++item_iter;
         }
-        if (!ok) give_up();
         // Also on an early exit: no pair MMA may still read shared memory or TMEM past this point.
         if (s_iter > 0) {
           mma_commit_pair(mma_done, 0x1);
@@ -282,21 +253,14 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warps
-    // Warp w reads TMEM lane quarter w % 4 (the tile rows 32 (w % 4) ..). Set s = (w - 4) / 4 takes, in
-    // accumulator half h, head h * kHalfHeads + s / kSplit and the RoPE pair dims [part * kChunks,
-    // (part + 1) * kChunks) of it, part = s % kSplit; each half is released as soon as it has been read.
+    // Warp w reads TMEM lane quarter w % 4 (the tile rows 32 (w % 4) ..); warps 4..7, 8..11, 12..15 and
+    // 16..19 each cover the four quarters for their own kSetHeads of the item's KV heads.
     const int r = (warp & 3) * 32 + lane;  // TMEM lane == tile token row
     const int et = tid - 128;              // 0..511 within the epilogue group
-    const int set = (warp - 4) >> 2;
-    const int part = set % kSplit;
+    const int h0 = ((warp - 4) >> 2) * kSetHeads;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t item_iter = 0, n_sync = 0;
     bool failed = false;
-    auto release = [&](int h) {
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(accum_empty_lead + h * 8);
-    };
     for (int k = items.k; k < items.end && !*abort_flag && !failed; k += items.step) {
       int pair, nblk, n_merged, first;
       if (!item_at(k, pair, nblk, n_merged, first)) break;  // reported by the producer
@@ -318,26 +282,17 @@ __global__ void __launch_bounds__(kKdThreads, 1)
         tc_fence_after();
         return true;
       };
-      if (!has_tile) {
-        if (accumulated) {
-          if (!wait_accum()) {
-            give_up();
-            break;
-          }
-          release(0);
-          release(1);
-          ++item_iter;
-        }
-        continue;
+      if (accumulated && !has_tile && !wait_accum()) {
+        give_up();
+        break;
       }
-      prefetch_l1(cosrow);
-      prefetch_l1(sinrow);
-      const int s = tile.seq;
-      const int64_t m_s = p.seq_m[s];
-      float* out_base = p.scores + p.seq_score_off[s];
-      const int kv0 = nblk * kHeads;
-      for (int h = 0; h < 2 && !failed; ++h) {
-        const int hh = h * kHalfHeads + set / kSplit;  // the warp's head within the item
+      if (has_tile) {
+        prefetch_l1(cosrow);
+        prefetch_l1(sinrow);
+        const int s = tile.seq;
+        const int64_t m_s = p.seq_m[s];
+        float* out_base = p.scores + p.seq_score_off[s];
+        const int kv0 = nblk * kHeads;
         for (int qi = 0; qi < p.q_len; ++qi) {
           if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
             give_up();
@@ -350,96 +305,94 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             q_s[i] = half_to_float<F16>(reinterpret_cast<const uint16_t*>(
                 p.query)[((static_cast<int64_t>(s) * p.n_q_heads + hq) * p.q_len + qi) * D + d]);
           }
-          if (h == 0 && qi == 0) {
+          if (qi == 0) {
             const uint16_t* mrow = reinterpret_cast<const uint16_t*>(p.mean) + static_cast<int64_t>(s) * p.mean_seq_stride +
                                    static_cast<int64_t>(p.layer) * p.n_cols + nblk * kKdCols;
             for (int i = et; i < kKdCols; i += kKdEpilogueThreads) mean_s[i] = half_to_float<F16>(mrow[i]);
           }
           if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag) ||
-              (h == 0 && qi == 0 && accumulated && !wait_accum())) {
+              (qi == 0 && accumulated && !wait_accum())) {
             give_up();
             failed = true;
             break;
           }
-          float acc[G];
+          float acc[kSetHeads][G];
 #pragma unroll
-          for (int j = 0; j < G; ++j) acc[j] = 0.f;
+          for (int e = 0; e < kSetHeads; ++e)
+#pragma unroll
+            for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
 #pragma unroll 1
-          for (int c = part * kChunks; c < (part + 1) * kChunks; c += 16) {
-            // The token's cos / sin for these 16 pair dims.
+          for (int c = 0; c < D / 2; c += 16) {
+            // The token's cos / sin for these 16 dims, shared by the warp's heads.
             const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
             const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
             const uint4 cv[2] = {__ldg(cp), __ldg(cp + 1)};
             const uint4 sv[2] = {__ldg(sp), __ldg(sp + 1)};
             const uint32_t* cbv = reinterpret_cast<const uint32_t*>(cv);  // 8 pairs of 16-bit values
             const uint32_t* sbv = reinterpret_cast<const uint32_t*>(sv);
-            uint32_t x1[16], x2[16];
-            if (accumulated) {
-              tmem_ld16(tmem + lane_base + hh * D + c, x1);
-              tmem_ld16(tmem + lane_base + hh * D + D / 2 + c, x2);
-              tmem_ld_wait();
-            } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) x1[i] = x2[i] = 0u;
-            }
-            const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
-            const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
+            for (int e = 0; e < kSetHeads; ++e) {
+              const int hh = h0 + e;
+              uint32_t x1[16], x2[16];
+              if (accumulated) {
+                tmem_ld16(tmem + lane_base + hh * D + c, x1);
+                tmem_ld16(tmem + lane_base + hh * D + D / 2 + c, x2);
+                tmem_ld_wait();
+              } else {
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              const float2 cf = half2_to_float2<F16>(cbv[i / 2]);
-              const float2 sf = half2_to_float2<F16>(sbv[i / 2]);
-              const float4 ma = m1[i / 4], mb = m2[i / 4];
-              const float k1a = __uint_as_float(x1[i]) + ((i & 2) ? ma.z : ma.x);
-              const float k1b = __uint_as_float(x1[i + 1]) + ((i & 2) ? ma.w : ma.y);
-              const float k2a = __uint_as_float(x2[i]) + ((i & 2) ? mb.z : mb.x);
-              const float k2b = __uint_as_float(x2[i + 1]) + ((i & 2) ? mb.w : mb.y);
-              x1[i] = __float_as_uint(k1a * cf.x - k2a * sf.x);
-              x1[i + 1] = __float_as_uint(k1b * cf.y - k2b * sf.y);
-              x2[i] = __float_as_uint(k2a * cf.x + k1a * sf.x);
-              x2[i + 1] = __float_as_uint(k2b * cf.y + k1b * sf.y);
-            }
-#pragma unroll
-            for (int j = 0; j < G; ++j) {
-              const float4* q1 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + c);
-              const float4* q2 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + D / 2 + c);
-              float a = 0.f;
-#pragma unroll
-              for (int i = 0; i < 16; i += 4) {
-                const float4 qa = q1[i / 4], qb = q2[i / 4];
-                a += qa.x * __uint_as_float(x1[i]) + qa.y * __uint_as_float(x1[i + 1]) +
-                     qa.z * __uint_as_float(x1[i + 2]) + qa.w * __uint_as_float(x1[i + 3]);
-                a += qb.x * __uint_as_float(x2[i]) + qb.y * __uint_as_float(x2[i + 1]) +
-                     qb.z * __uint_as_float(x2[i + 2]) + qb.w * __uint_as_float(x2[i + 3]);
+                for (int i = 0; i < 16; ++i) x1[i] = x2[i] = 0u;
               }
-              acc[j] += a;
+              const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
+              const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
+#pragma unroll
+              for (int i = 0; i < 16; i += 2) {
+                const float2 cf = half2_to_float2<F16>(cbv[i / 2]);
+                const float2 sf = half2_to_float2<F16>(sbv[i / 2]);
+                const float4 ma = m1[i / 4], mb = m2[i / 4];
+                const float k1a = __uint_as_float(x1[i]) + ((i & 2) ? ma.z : ma.x);
+                const float k1b = __uint_as_float(x1[i + 1]) + ((i & 2) ? ma.w : ma.y);
+                const float k2a = __uint_as_float(x2[i]) + ((i & 2) ? mb.z : mb.x);
+                const float k2b = __uint_as_float(x2[i + 1]) + ((i & 2) ? mb.w : mb.y);
+                x1[i] = __float_as_uint(k1a * cf.x - k2a * sf.x);
+                x1[i + 1] = __float_as_uint(k1b * cf.y - k2b * sf.y);
+                x2[i] = __float_as_uint(k2a * cf.x + k1a * sf.x);
+                x2[i + 1] = __float_as_uint(k2b * cf.y + k1b * sf.y);
+              }
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+                const float4* q1 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + c);
+                const float4* q2 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + D / 2 + c);
+                float a = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                  const float4 qa = q1[i / 4], qb = q2[i / 4];
+                  a += qa.x * __uint_as_float(x1[i]) + qa.y * __uint_as_float(x1[i + 1]) +
+                       qa.z * __uint_as_float(x1[i + 2]) + qa.w * __uint_as_float(x1[i + 3]);
+                  a += qb.x * __uint_as_float(x2[i]) + qb.y * __uint_as_float(x2[i + 1]) +
+                       qb.z * __uint_as_float(x2[i + 2]) + qb.w * __uint_as_float(x2[i + 3]);
+                }
+                acc[e][j] += a;
+              }
             }
           }
-          float* red = red_s + ((hh - h * kHalfHeads) * G) * 128 + r;
-          if (kSplit == 2) {
-            // The second part's partial products go through shared memory to the first part's warp.
-            if (part == 1) {
+          if (valid) {
 #pragma unroll
-              for (int j = 0; j < G; ++j) red[j * 128] = acc[j];
-            }
-            if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
-              give_up();
-              failed = true;
-              break;
-            }
-          }
-          if (valid && part == 0) {
+            for (int e = 0; e < kSetHeads; ++e)
 #pragma unroll
-            for (int j = 0; j < G; ++j) {
-              const float v = kSplit == 2 ? acc[j] + red[j * 128] : acc[j];
-              const int hq = (kv0 + hh) * G + j;
-              out_base[(static_cast<int64_t>(hq) * p.q_len + qi) * m_s + tile.score_base + r] =
-                  hidden ? -INFINITY : v * p.scaling;
-            }
+              for (int j = 0; j < G; ++j) {
+                const int hq = (kv0 + h0 + e) * G + j;
+                out_base[(static_cast<int64_t>(hq) * p.q_len + qi) * m_s + tile.score_base + r] =
+                    hidden ? -INFINITY : acc[e][j] * p.scaling;
+              }
           }
         }
-        if (accumulated && !failed) release(h);
       }
-      if (accumulated) ++item_iter;
+      if (accumulated) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(accum_empty_lead);
+        ++item_iter;
+      }
     }
   }
   tc_fence_before();
@@ -452,9 +405,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
 template <int D, int G, bool F16>
 static int launch_dense(const CUtensorMap& bmap, const CUtensorMap& amap, const KeyScoreParams& p, int grid,
                         cudaStream_t stream) {
-  constexpr int kHeads = kKdCols / D;
-  const int smem = 1024 + kKdStages * kKdStage + kHeads * G * D * 4 + kKdCols * 4 + (kHeads / 2) * G * 128 * 4 +
-                   32 * 8 + 32;
+  const int smem = 1024 + kKdStages * kKdStage + (kKdCols / D) * G * D * 4 + kKdCols * 4 + 32 * 8 + 32;
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_dense_kernel<D, G, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
