@@ -30,9 +30,15 @@ namespace dkv {
 
 namespace {
 
-constexpr int kKdThreads = 640;
-constexpr int kKdEpilogueWarps = 16;
+// Epilogue warps: 16 (one KV head of the item each, 96 registers per thread) or 8 (two heads each, 168
+// registers, both heads' TMEM columns loaded before one wait).
+#ifndef DKV_KD_EPI_WARPS
+#define DKV_KD_EPI_WARPS 16
+#endif
+constexpr int kKdEpilogueWarps = DKV_KD_EPI_WARPS;
 constexpr int kKdEpilogueThreads = kKdEpilogueWarps * 32;
+constexpr int kKdThreads = 128 + kKdEpilogueThreads;
+static_assert(kKdEpilogueWarps == 8 || kKdEpilogueWarps == 16, "epilogue warps");
 constexpr int kKdCols = 512;                 // key columns per item (one 512-column TMEM accumulator)
 constexpr int kKdMmaN = 256;                 // N of one pair MMA (two per K step)
 constexpr int kKdHalfCols = 128;             // basis rows of one pair MMA loaded by each CTA
@@ -48,7 +54,9 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     key_scores_dense_kernel(const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap amap,
                             const KeyScoreParams p) {
   constexpr int kHeads = kKdCols / D;        // KV heads per item
-  constexpr int kSetHeads = kHeads / 4;      // heads per epilogue warp
+  constexpr int kSetHeads = kHeads / (kKdEpilogueWarps / 4);  // heads per epilogue warp
+  // Heads whose columns one TMEM wait covers (two only with the 8-warp epilogue's larger register budget).
+  constexpr int kLoadHeads = (kKdEpilogueWarps == 8 && kSetHeads >= 2) ? 2 : 1;
   constexpr uint32_t kIdesc = idesc_f16(256, kKdMmaN, /*is_bf16=*/!F16, false, false);
 
   extern __shared__ uint8_t smem_raw[];
@@ -254,7 +262,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warps
     // Warp w reads TMEM lane quarter w % 4 (the tile rows 32 (w % 4) ..); warps 4..7, 8..11, 12..15 and
-    // 16..19 each cover the four quarters for their own kSetHeads of the item's KV heads.
+    // 16..19 (or 4..7 and 8..11 with 8 epilogue warps) each cover the four quarters for their own kSetHeads
+    // of the item's KV heads.
     const int r = (warp & 3) * 32 + lane;  // TMEM lane == tile token row
     const int et = tid - 128;              // 0..511 within the epilogue group
     const int h0 = ((warp - 4) >> 2) * kSetHeads;
@@ -331,17 +340,26 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             const uint32_t* cbv = reinterpret_cast<const uint32_t*>(cv);  // 8 pairs of 16-bit values
             const uint32_t* sbv = reinterpret_cast<const uint32_t*>(sv);
 #pragma unroll
-            for (int e = 0; e < kSetHeads; ++e) {
-              const int hh = h0 + e;
-              uint32_t x1[16], x2[16];
+            for (int hp = 0; hp < kSetHeads; hp += kLoadHeads) {
+              uint32_t xs1[kLoadHeads][16], xs2[kLoadHeads][16];
               if (accumulated) {
-                tmem_ld16(tmem + lane_base + hh * D + c, x1);
-                tmem_ld16(tmem + lane_base + hh * D + D / 2 + c, x2);
+#pragma unroll
+                for (int e = 0; e < kLoadHeads; ++e) {
+                  tmem_ld16(tmem + lane_base + (h0 + hp + e) * D + c, xs1[e]);
+                  tmem_ld16(tmem + lane_base + (h0 + hp + e) * D + D / 2 + c, xs2[e]);
+                }
                 tmem_ld_wait();
               } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) x1[i] = x2[i] = 0u;
+                for (int e = 0; e < kLoadHeads; ++e)
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) xs1[e][i] = xs2[e][i] = 0u;
               }
+#pragma unroll
+            for (int e = hp; e < hp + kLoadHeads; ++e) {
+              const int hh = h0 + e;
+              uint32_t* x1 = xs1[e - hp];
+              uint32_t* x2 = xs2[e - hp];
               const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
               const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
 #pragma unroll
@@ -373,6 +391,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
                 }
                 acc[e][j] += a;
               }
+            }
             }
           }
           if (valid) {
