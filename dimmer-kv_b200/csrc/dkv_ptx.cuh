@@ -197,6 +197,35 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// ---------------------------------------------------------------- packed fp32 pairs (sm_100)
+// Two fp32 values in one 64-bit register, low word first; each lane of add / mul / fma.rn.f32x2 rounds like
+// the scalar fp32 instruction.
+__device__ __forceinline__ uint64_t f32x2_pack(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+__device__ __forceinline__ float f32x2_sum(uint64_t v) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  return __uint_as_float(lo) + __uint_as_float(hi);
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // Bring the line holding addr into L1 (no data returned, nothing to wait for).
 __device__ __forceinline__ void prefetch_l1(const void* addr) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(addr)));

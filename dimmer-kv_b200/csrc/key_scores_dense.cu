@@ -30,10 +30,10 @@ namespace dkv {
 
 namespace {
 
-// Epilogue warps: 16 (one KV head of the item each, 96 registers per thread) or 8 (two heads each, 168
-// registers, both heads' TMEM columns loaded before one wait).
+// Epilogue warps: 8 (two KV heads of the item each, 168 registers per thread, both heads' TMEM columns
+// loaded before one wait) or 16 (one head each, 96 registers).
 #ifndef DKV_KD_EPI_WARPS
-#define DKV_KD_EPI_WARPS 16
+#define DKV_KD_EPI_WARPS 8
 #endif
 constexpr int kKdEpilogueWarps = DKV_KD_EPI_WARPS;
 constexpr int kKdEpilogueThreads = kKdEpilogueWarps * 32;
@@ -360,35 +360,41 @@ __global__ void __launch_bounds__(kKdThreads, 1)
               const int hh = h0 + e;
               uint32_t* x1 = xs1[e - hp];
               uint32_t* x2 = xs2[e - hp];
-              const float4* m1 = reinterpret_cast<const float4*>(mean_s + hh * D + c);
-              const float4* m2 = reinterpret_cast<const float4*>(mean_s + hh * D + D / 2 + c);
+              // Pairs of dims (c + 2k, c + 2k + 1) in packed fp32x2 arithmetic: + mean, RoPE, q.k.
+              const ulonglong2* m1 = reinterpret_cast<const ulonglong2*>(mean_s + hh * D + c);
+              const ulonglong2* m2 = reinterpret_cast<const ulonglong2*>(mean_s + hh * D + D / 2 + c);
+              uint64_t r1[8], r2[8];
 #pragma unroll
-              for (int i = 0; i < 16; i += 2) {
-                const float2 cf = half2_to_float2<F16>(cbv[i / 2]);
-                const float2 sf = half2_to_float2<F16>(sbv[i / 2]);
-                const float4 ma = m1[i / 4], mb = m2[i / 4];
-                const float k1a = __uint_as_float(x1[i]) + ((i & 2) ? ma.z : ma.x);
-                const float k1b = __uint_as_float(x1[i + 1]) + ((i & 2) ? ma.w : ma.y);
-                const float k2a = __uint_as_float(x2[i]) + ((i & 2) ? mb.z : mb.x);
-                const float k2b = __uint_as_float(x2[i + 1]) + ((i & 2) ? mb.w : mb.y);
-                x1[i] = __float_as_uint(k1a * cf.x - k2a * sf.x);
-                x1[i + 1] = __float_as_uint(k1b * cf.y - k2b * sf.y);
-                x2[i] = __float_as_uint(k2a * cf.x + k1a * sf.x);
-                x2[i + 1] = __float_as_uint(k2b * cf.y + k1b * sf.y);
+              for (int k2 = 0; k2 < 8; k2 += 2) {
+                const ulonglong2 ma = m1[k2 / 2], mb = m2[k2 / 2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int k = k2 + u;
+                  const float2 cf = half2_to_float2<F16>(cbv[k]);
+                  const float2 sf = half2_to_float2<F16>(sbv[k]);
+                  const uint64_t cc = f32x2_pack(__float_as_uint(cf.x), __float_as_uint(cf.y));
+                  const uint64_t ss = f32x2_pack(__float_as_uint(sf.x), __float_as_uint(sf.y));
+                  const uint64_t ns = ss ^ 0x8000000080000000ull;  // -sin, both lanes
+                  const uint64_t k1 = add_f32x2(f32x2_pack(x1[2 * k], x1[2 * k + 1]), u ? ma.y : ma.x);
+                  const uint64_t kb = add_f32x2(f32x2_pack(x2[2 * k], x2[2 * k + 1]), u ? mb.y : mb.x);
+                  r1[k] = fma_f32x2(k1, cc, mul_f32x2(kb, ns));  // k1 cos - k2 sin
+                  r2[k] = fma_f32x2(kb, cc, mul_f32x2(k1, ss));  // k2 cos + k1 sin
+                }
               }
 #pragma unroll
               for (int j = 0; j < G; ++j) {
-                const float4* q1 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + c);
-                const float4* q2 = reinterpret_cast<const float4*>(q_s + (hh * G + j) * D + D / 2 + c);
-                float a = 0.f;
+                const ulonglong2* q1 = reinterpret_cast<const ulonglong2*>(q_s + (hh * G + j) * D + c);
+                const ulonglong2* q2 = reinterpret_cast<const ulonglong2*>(q_s + (hh * G + j) * D + D / 2 + c);
+                uint64_t a2 = 0ull;  // (+0.0, +0.0)
 #pragma unroll
-                for (int i = 0; i < 16; i += 4) {
-                  const float4 qa = q1[i / 4], qb = q2[i / 4];
-                  a += qa.x * __uint_as_float(x1[i]) + qa.y * __uint_as_float(x1[i + 1]) +
-                       qa.z * __uint_as_float(x1[i + 2]) + qa.w * __uint_as_float(x1[i + 3]);
-                  a += qb.x * __uint_as_float(x2[i]) + qb.y * __uint_as_float(x2[i + 1]) +
-                       qb.z * __uint_as_float(x2[i + 2]) + qb.w * __uint_as_float(x2[i + 3]);
+                for (int k2 = 0; k2 < 8; k2 += 2) {
+                  const ulonglong2 qa = q1[k2 / 2], qb = q2[k2 / 2];
+                  a2 = fma_f32x2(qa.x, r1[k2], a2);
+                  a2 = fma_f32x2(qa.y, r1[k2 + 1], a2);
+                  a2 = fma_f32x2(qb.x, r2[k2], a2);
+                  a2 = fma_f32x2(qb.y, r2[k2 + 1], a2);
                 }
+                const float a = f32x2_sum(a2);
                 acc[e][j] += a;
               }
             }
