@@ -290,6 +290,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_ld_wait: ties the registers a tcgen05.ld wrote to the wait, so that no use of them can be
+// scheduled before it (the load writes them asynchronously).
+__device__ __forceinline__ void tmem_reg_fence(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 "version 1" layout).
 //   K-major operand:  SBO = byte stride between 8-row groups (1024 for dense rows of 128 B), LBO unused (16).
 //   MN-major operand: LBO = byte stride between 64-element MN atoms, SBO = byte stride between 8-row K groups.

@@ -39,6 +39,10 @@ constexpr int kKdEpilogueWarps = DKV_KD_EPI_WARPS;
 constexpr int kKdEpilogueThreads = kKdEpilogueWarps * 32;
 constexpr int kKdThreads = 128 + kKdEpilogueThreads;
 static_assert(kKdEpilogueWarps == 8 || kKdEpilogueWarps == 16, "epilogue warps");
+#ifndef DKV_KD_CHUNK_UNROLL
+#define DKV_KD_CHUNK_UNROLL 1
+#endif
+constexpr int kKdChunkUnroll = DKV_KD_CHUNK_UNROLL;  // epilogue RoPE chunks unrolled (1: none)
 constexpr int kKdCols = 512;                 // key columns per item (one 512-column TMEM accumulator)
 constexpr int kKdMmaN = 256;                 // N of one pair MMA (two per K step)
 constexpr int kKdHalfCols = 128;             // basis rows of one pair MMA loaded by each CTA
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
           for (int e = 0; e < kSetHeads; ++e)
 #pragma unroll
             for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
-#pragma unroll 1
+#pragma unroll kKdChunkUnroll
           for (int c = 0; c < D / 2; c += 16) {
             // The token's cos / sin for these 16 dims, shared by the warp's heads.
             const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
@@ -349,6 +353,11 @@ __global__ void __launch_bounds__(kKdThreads, 1)
                   tmem_ld16(tmem + lane_base + (h0 + hp + e) * D + D / 2 + c, xs2[e]);
                 }
                 tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < kLoadHeads; ++e) {
+                  tmem_reg_fence(xs1[e]);
+                  tmem_reg_fence(xs2[e]);
+                }
               } else {
 #pragma unroll
                 for (int e = 0; e < kLoadHeads; ++e)
