@@ -173,6 +173,10 @@ def pair_work_lists(present: torch.Tensor, group_base: torch.Tensor, ranges: lis
 class CompressedBatch:
     """Compressed middle tokens of a batch of conversations (one row of the HF batch each)."""
 
+    # Value work items per CTA the value stage's schedule aims at: more items balance the persistent CTAs
+    # better, fewer write fewer per-item partial sums for the value basis to reduce.
+    value_items_per_cta = 8
+
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
                  device=None, dtype=torch.bfloat16, tile_chunk: int = 16, union: dict | None = None,
@@ -336,7 +340,7 @@ class CompressedBatch:
         # about an eighth of a CTA's share so that the longest-first deal ends level.
         counts = [(wprefix[:, g1] - wprefix[:, g0]).tolist() for g0, g1 in ranges_g]
         total = sum(sum(c) for c in counts) + 0.5 * present.shape[0] * max(1, len(ranges_g))
-        target = max(4.0, total / (8 * self.sm_count))
+        target = max(4.0, total / (self.value_items_per_cta * self.sm_count))
         rows, ranges, spans, costs = [], [], [], []
         for s, seq_ranges in enumerate(tile_ranges):
             first = len(rows)
