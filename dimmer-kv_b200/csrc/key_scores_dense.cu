@@ -43,6 +43,12 @@ static_assert(kKdEpilogueWarps == 8 || kKdEpilogueWarps == 16, "epilogue warps")
 #define DKV_KD_CHUNK_UNROLL 1
 #endif
 constexpr int kKdChunkUnroll = DKV_KD_CHUNK_UNROLL;  // epilogue RoPE chunks unrolled (1: none)
+// 1: each epilogue thread loads its token's cos / sin rows into registers before it waits for the
+// accumulator (their latency then overlaps the MMAs); 0: from L1, chunk by chunk.
+#ifndef DKV_KD_ROPE_REGS
+#define DKV_KD_ROPE_REGS 0
+#endif
+constexpr bool kKdRopeRegs = DKV_KD_ROPE_REGS != 0;
 constexpr int kKdCols = 512;                 // key columns per item (one 512-column TMEM accumulator)
 constexpr int kKdMmaN = 256;                 // N of one pair MMA (two per K step)
 constexpr int kKdHalfCols = 128;             // basis rows of one pair MMA loaded by each CTA
@@ -60,7 +66,9 @@ __global__ void __launch_bounds__(kKdThreads, 1)
   constexpr int kHeads = kKdCols / D;        // KV heads per item
   constexpr int kSetHeads = kHeads / (kKdEpilogueWarps / 4);  // heads per epilogue warp
   // Heads whose columns one TMEM wait covers (two only with the 8-warp epilogue's larger register budget).
-  constexpr int kLoadHeads = (kKdEpilogueWarps == 8 && kSetHeads >= 2) ? 2 : 1;
+  constexpr int kLoadHeads = (kKdEpilogueWarps == 8 && kSetHeads >= 2 && !kKdRopeRegs) ? 2 : 1;
+  constexpr int kRopeWords = kKdRopeRegs ? D / 4 : 1;  // 32-bit words of a token's cos (or sin) row
+  constexpr int kChunkUnroll = kKdRopeRegs ? (D / 2) / 16 : kKdChunkUnroll;
   constexpr uint32_t kIdesc = idesc_f16(256, kKdMmaN, /*is_bf16=*/!F16, false, false);
 
   extern __shared__ uint8_t smem_raw[];
@@ -299,9 +307,20 @@ __global__ void __launch_bounds__(kKdThreads, 1)
         give_up();
         break;
       }
+      uint32_t cs[kRopeWords], sn[kRopeWords];  // the token's cos / sin row (kKdRopeRegs)
       if (has_tile) {
-        prefetch_l1(cosrow);
-        prefetch_l1(sinrow);
+        if constexpr (kKdRopeRegs) {
+#pragma unroll
+          for (int w = 0; w < kRopeWords; w += 4) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(cosrow) + w / 4);
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(sinrow) + w / 4);
+            cs[w] = a.x, cs[w + 1] = a.y, cs[w + 2] = a.z, cs[w + 3] = a.w;
+            sn[w] = b.x, sn[w + 1] = b.y, sn[w + 2] = b.z, sn[w + 3] = b.w;
+          }
+        } else {
+          prefetch_l1(cosrow);
+          prefetch_l1(sinrow);
+        }
         const int s = tile.seq;
         const int64_t m_s = p.seq_m[s];
         float* out_base = p.scores + p.seq_score_off[s];
@@ -334,15 +353,22 @@ __global__ void __launch_bounds__(kKdThreads, 1)
           for (int e = 0; e < kSetHeads; ++e)
 #pragma unroll
             for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
-#pragma unroll kKdChunkUnroll
+#pragma unroll kChunkUnroll
           for (int c = 0; c < D / 2; c += 16) {
-            // The token's cos / sin for these 16 dims, shared by the warp's heads.
-            const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
-            const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
-            const uint4 cv[2] = {__ldg(cp), __ldg(cp + 1)};
-            const uint4 sv[2] = {__ldg(sp), __ldg(sp + 1)};
-            const uint32_t* cbv = reinterpret_cast<const uint32_t*>(cv);  // 8 pairs of 16-bit values
-            const uint32_t* sbv = reinterpret_cast<const uint32_t*>(sv);
+            // The token's cos / sin for these 16 dims (8 pairs of 16-bit values), shared by the warp's heads.
+            uint32_t cbv[8], sbv[8];
+            if constexpr (kKdRopeRegs) {
+#pragma unroll
+              for (int k = 0; k < 8; ++k) cbv[k] = cs[c / 2 + k], sbv[k] = sn[c / 2 + k];
+            } else {
+              const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
+              const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
+              const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+              cbv[0] = c0.x, cbv[1] = c0.y, cbv[2] = c0.z, cbv[3] = c0.w;
+              cbv[4] = c1.x, cbv[5] = c1.y, cbv[6] = c1.z, cbv[7] = c1.w;
+              sbv[0] = s0.x, sbv[1] = s0.y, sbv[2] = s0.z, sbv[3] = s0.w;
+              sbv[4] = s1.x, sbv[5] = s1.y, sbv[6] = s1.z, sbv[7] = s1.w;
+            }
 #pragma unroll
             for (int hp = 0; hp < kSetHeads; hp += kLoadHeads) {
               uint32_t xs1[kLoadHeads][16], xs2[kLoadHeads][16];

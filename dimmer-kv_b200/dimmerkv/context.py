@@ -175,7 +175,7 @@ class CompressedBatch:
 
     # Value work items per CTA the value stage's schedule aims at: more items balance the persistent CTAs
     # better, fewer write fewer per-item partial sums for the value basis to reduce.
-    value_items_per_cta = 8
+    value_items_per_cta = 4
 
     def __init__(self, conversations: list[ConversationCodes], *, layers: int, kv_heads: int, head_dim: int,
                  q_heads: int, basis: dict, mean: dict, cos: torch.Tensor, sin: torch.Tensor,
