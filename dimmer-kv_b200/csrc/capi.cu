@@ -299,7 +299,7 @@ int dkv_finalize(const dkv_attend_args* a, void* stream) {
 
 int64_t dkv_vpart_floats(int32_t v_width, int32_t n_seq, int32_t rows_pad, int32_t head_dim) {
   if (v_width < 0 || n_seq < 0 || rows_pad < 0 || head_dim < 0) return -1;
-  return static_cast<int64_t>(dkv::finalize_chunks(v_width)) * n_seq * rows_pad * head_dim;
+  return dkv::finalize_vpart_floats(v_width, n_seq, rows_pad, head_dim);
 }
 
 int dkv_attend_tail(const dkv_attend_args* a, void* stream) {

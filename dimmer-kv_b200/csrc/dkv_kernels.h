@@ -131,11 +131,11 @@ struct FinalizeParams {
   int n_seq, n_q_heads, q_per_kv, q_len, head_dim, n_exact, layer, n_cols;
   void* out;                      // [n_seq][q_len][n_q_heads][head_dim]
   int out_f32;                    // fp32 output instead of bf16
-  float* vpart;                   // [finalize_chunks(r_v)][n_seq][n_rows_pad][head_dim]
+  float* vpart;                   // finalize_vpart_floats(r_v, n_seq, n_rows_pad, head_dim) floats of scratch
   int* status;
   int f16;                        // 16-bit operands and output in fp16 (else bf16)
 };
-int finalize_chunks(int r_v);
+int64_t finalize_vpart_floats(int r_v, int n_seq, int rows_pad, int head_dim);
 int run_finalize(const FinalizeParams& p, cudaStream_t stream);
 
 // Encode side of the progressive codec: quantize8 + per-rung errors (encode.cu).

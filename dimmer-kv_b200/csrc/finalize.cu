@@ -3,15 +3,18 @@
 // Replaces the tail of CompressedContext.attend (scripts/compressed_attention.py:130-137):
 //   out_c = sum(p_c) * mean_v + (p_c @ C_v) @ B_v[layer, head]     (values never decoded)
 //   out   = out_c + p_e @ V_exact
-// The probability-weighted coefficients p_c @ C_v arrive as per-item partial sums from
-// value_weights.cu. Two kernels:
-//   vbasis  : one CTA per (chunk of 128 basis components, KV head, block of 8 conversations). The
-//             CTA stages its basis slice [128 components x head_dim] in shared memory, reduces the
-//             items' partial sums of those components for its conversations and multiplies them by
-//             the slice: the layer's value basis is read once per 8 conversations instead of once per
-//             conversation. Output: per-chunk partial outputs [chunks][conversations][rows][head_dim].
-//   combine : sums the chunks in a fixed order (deterministic), adds the mean term and the exact
+// The probability-weighted coefficients p_c @ C_v arrive as per-item partial sums from the value stage
+// (value_dense.cu / value_weights.cu). Three kernels:
+//   wsum    : one CTA per (conversation, 64 components): sums the conversation's items that cover the
+//             components, in item order (deterministic), into W [conversation][row][component] (fp32).
+//   vbasis  : per KV head a fp32 product W[rows of the head, all conversations] x B_v[layer][:, head] on the
+//             CUDA cores (the reference's product is fp32-accurate; tensor-core inputs would round W),
+//             tiled 32 rows x head_dim columns x 32 components through shared memory, the components split
+//             into up to kMaxKSplit slices so that the grid covers the SMs. Output: per-slice partial outputs
+//             [slices][conversations][rows][head_dim].
+//   combine : sums the slices in a fixed order (deterministic), adds the mean term and the exact
 //             tokens, and writes the HF layout [batch, q_len, q_heads, head_dim].
+// Scratch (vpart): W [n_seq][rows_pad][r_v], then the slices' partial outputs.
 #include "dkv_kernels.h"
 #include "dkv_ptx.cuh"
 #include "dkv_format.cuh"
@@ -19,118 +22,125 @@
 namespace dkv {
 
 namespace {
-constexpr int kFinalizeThreads = 256;
+constexpr int kWsumComps = 64;       // components per wsum CTA (one group; item ranges hold whole groups)
+constexpr int kWsumThreads = 256;    // 64 components x 4 row phases
+constexpr int kGemmThreads = 256;
+constexpr int kGemmBM = 32;          // rows per vbasis CTA
+constexpr int kGemmBK = 32;          // components per shared-memory step
+constexpr int kMaxKSplit = 8;        // component slices of vbasis (partial outputs summed by combine)
 constexpr int kCombineThreads = 128;
-constexpr int kCombineRows = 8;  // rows of one KV head per combine CTA (one when a head has many rows)
-constexpr int kRChunk = 128;   // basis components per vbasis CTA
-constexpr int kSeqBlock = 8;   // conversations per vbasis CTA (fewer when many rows share a KV head)
-constexpr int kCoverPerSeq = 512;  // items of one conversation that cover a component chunk
+constexpr int kCombineRows = 8;      // rows of one KV head per combine CTA (one when a head has many rows)
 }  // namespace
 
-__global__ void __launch_bounds__(kFinalizeThreads) vbasis_kernel(const FinalizeParams p, int seq_block,
-                                                                  int row_block, int n_row_blocks) {
+// W[s][lr][c] = sum over the conversation's items covering component c (item order) of
+// partial[item][lr][c - first component of the item]. Rows lr in [0, n_rows).
+__global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams p, float* w) {
   if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
-  extern __shared__ float smem_f[];
-  const int D = p.head_dim;
-  const int D2 = D / 2;
-  const int G = p.q_per_kv;
-  const int chunk = blockIdx.x, kvh = blockIdx.y;
-  const int s0 = (blockIdx.z / n_row_blocks) * seq_block;
-  const int n_s = min(seq_block, p.n_seq - s0);
-  const int r0 = chunk * kRChunk;
-  // Rows of this KV head inside the call, then this CTA's block of them (many query rows per head,
-  // few conversations: the rows are spread over more CTAs).
-  const int head_lo = max(p.row_begin, kvh * G * p.q_len);
-  const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
-  const int rlo = head_lo + static_cast<int>(blockIdx.z % n_row_blocks) * row_block;
-  const int rhi = min(head_hi, rlo + row_block);
-  const int nr = rhi - rlo;
-  if (nr <= 0 || n_s <= 0) return;
-  uint32_t* bs = reinterpret_cast<uint32_t*>(smem_f);  // [kRChunk][D/2] pairs of 16-bit basis values
-  float* ws = smem_f + kRChunk * D2;                                // [n_s][nr][kRChunk]
-  const int tid = threadIdx.x;
+  const int s = blockIdx.x;
+  const int c0 = blockIdx.y * kWsumComps;
+  const int c = c0 + (threadIdx.x % kWsumComps);
+  const int phase = threadIdx.x / kWsumComps;
   const int item_cols = p.item_groups * 64;
-
-  // Basis slice of this KV head: rows r0 .. r0+127 of [layer][r_v][n_cols], columns kvh*D .. +D.
-  const uint32_t* bsrc =
-      reinterpret_cast<const uint32_t*>(p.basis_v + static_cast<int64_t>(p.layer) * p.r_v * p.n_cols) + kvh * D2;
-  for (int i = tid; i < kRChunk * D2; i += kFinalizeThreads) {
-    const int r = i / D2, dp = i % D2;
-    bs[i] = (r0 + r < p.r_v) ? bsrc[static_cast<int64_t>(r0 + r) * (p.n_cols / 2) + dp] : 0u;  // +0.0 in both
-  }
-  // Weighted coefficients of the block's conversations. First the items of each conversation that cover
-  // this chunk (in item order), then every element sums them with independent loads.
-  // One warp per conversation builds its list (at most kCoverPerSeq items).
-  __shared__ int cover[kSeqBlock * kCoverPerSeq];
-  __shared__ int n_cover[kSeqBlock];
-  {
-    const int sl = tid >> 5, ln = tid & 31;
-    if (sl < n_s) {
-      const int it0 = p.seq_items[2 * (s0 + sl)], it1 = p.seq_items[2 * (s0 + sl) + 1];
-      int n = 0;
-      for (int base = it0; base < it1; base += 32) {
-        const int it = base + ln;
-        bool hit = false;
-        if (it < it1) {
-          const int cb = p.items[4 * it + 3] * 64;
-          hit = r0 >= cb && r0 < cb + item_cols;
-        }
-        const unsigned mask = __ballot_sync(0xffffffffu, hit);
-        const int slot = n + __popc(mask & ((1u << ln) - 1u));
-        if (hit) {
-          if (slot < kCoverPerSeq)
-            cover[sl * kCoverPerSeq + slot] = it;
-          else  // more covering items than the list holds: report, never drop silently
-            record_error(p.status, kErrBadDescriptor);
-        }
-        n += __popc(mask);
-      }
-      if (ln == 0) n_cover[sl] = n < kCoverPerSeq ? n : kCoverPerSeq;
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < n_s * nr * kRChunk; i += kFinalizeThreads) {
-    const int sl = i / (nr * kRChunk);
-    const int rr = (i / kRChunk) % nr, c = i % kRChunk;
-    const int64_t col = (rlo - p.row_begin + rr) * static_cast<int64_t>(item_cols) + (r0 % item_cols) + c;
+  const int it0 = __ldg(p.seq_items + 2 * s), it1 = __ldg(p.seq_items + 2 * s + 1);
+  for (int lr = phase; lr < p.n_rows; lr += kWsumThreads / kWsumComps) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int j = sl * kCoverPerSeq;
-    const int j1 = j + n_cover[sl];
-    for (; j + 4 <= j1; j += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        acc[u] += p.partial[static_cast<int64_t>(cover[j + u]) * p.n_rows_pad * item_cols + col];
+    int u = 0;
+    for (int it = it0; it < it1; ++it) {
+      const int cb = __ldg(p.items + 4 * it + 3) * 64;  // first component of the item
+      if (c0 < cb || c0 >= cb + item_cols) continue;   // the item does not cover this block
+      acc[u & 3] += p.partial[(static_cast<int64_t>(it) * p.n_rows_pad + lr) * item_cols + (c - cb)];
+      ++u;
     }
-    float tail = 0.f;
-    for (; j < j1; ++j) tail += p.partial[static_cast<int64_t>(cover[j]) * p.n_rows_pad * item_cols + col];
-    ws[i] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + tail;
+    w[(static_cast<int64_t>(s) * p.n_rows_pad + lr) * p.r_v + c] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
-  __syncthreads();
-  const int dp = tid % D2;
-  const int rg = tid / D2;
-  const int n_rg = kFinalizeThreads / D2;
-  for (int j = rg; j < n_s * nr; j += n_rg) {
-    const float* w = ws + j * kRChunk;
-    float ax = 0.f, ay = 0.f;
-    if (p.f16) {
-#pragma unroll 8
-      for (int c = 0; c < kRChunk; ++c) {
-        const float2 b = half2_to_float2<true>(bs[c * D2 + dp]);
-        ax = fmaf(w[c], b.x, ax);
-        ay = fmaf(w[c], b.y, ay);
+}
+
+// Rows of KV head kvh inside the call: [head_lo, head_hi) (absolute row indices), nrh of them.
+__device__ __forceinline__ void head_rows(const FinalizeParams& p, int kvh, int& head_lo, int& nrh) {
+  const int G = p.q_per_kv;
+  head_lo = max(p.row_begin, kvh * G * p.q_len);
+  const int head_hi = min(p.row_begin + p.n_rows, (kvh + 1) * G * p.q_len);
+  nrh = max(0, head_hi - head_lo);
+}
+
+// vpart[slice][s][lr][d] = sum over components k of the slice of W[s][lr][k] * B_v[layer][k][kvh * D + d], for
+// the rows lr of KV head kvh = blockIdx.y of every conversation (GEMM rows m = s * nrh + row within the head).
+template <int D>
+__global__ void __launch_bounds__(kGemmThreads) vbasis_kernel(const FinalizeParams p, const float* w, float* vpart,
+                                                             int k_slice) {
+  if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
+  constexpr int kTN = 4;                      // columns per thread
+  constexpr int kThreadsN = D / kTN;          // 32 (D = 128) or 16 (D = 64)
+  constexpr int kThreadsM = kGemmThreads / kThreadsN;
+  constexpr int kTM = kGemmBM / kThreadsM;    // rows per thread: 4 or 2
+  __shared__ float as[kGemmBK][kGemmBM + 4];  // W tile, component-major (rows contiguous)
+  __shared__ float bs[kGemmBK][D];            // B_v tile in fp32
+  const int kvh = blockIdx.y;
+  int head_lo, nrh;
+  head_rows(p, kvh, head_lo, nrh);
+  const int M = p.n_seq * nrh;
+  const int m0 = blockIdx.x * kGemmBM;
+  if (nrh == 0 || m0 >= M) return;
+  const int k0 = blockIdx.z * k_slice;
+  const int k1 = min(p.r_v, k0 + k_slice);
+  const int tid = threadIdx.x;
+  const int tn = tid % kThreadsN, tm = tid / kThreadsN;
+  float acc[kTM][kTN];
+#pragma unroll
+  for (int i = 0; i < kTM; ++i)
+#pragma unroll
+    for (int j = 0; j < kTN; ++j) acc[i][j] = 0.f;
+  const uint16_t* bsrc = reinterpret_cast<const uint16_t*>(p.basis_v) + static_cast<int64_t>(p.layer) * p.r_v * p.n_cols +
+                         kvh * D;
+  for (int kb = k0; kb < k1; kb += kGemmBK) {
+    // W tile: kGemmBM rows x kGemmBK components (rows past M or components past the slice read as 0).
+    for (int i = tid; i < kGemmBM * kGemmBK; i += kGemmThreads) {
+      const int mm = i / kGemmBK, kk = i % kGemmBK;
+      const int m = m0 + mm, k = kb + kk;
+      float v = 0.f;
+      if (m < M && k < k1) {
+        const int sq = m / nrh, lr = head_lo - p.row_begin + m % nrh;
+        v = w[(static_cast<int64_t>(sq) * p.n_rows_pad + lr) * p.r_v + k];
       }
-    } else {
+      as[kk][mm] = v;
+    }
+    // B_v tile: kGemmBK components x D columns of this head, 16-bit -> fp32.
+    for (int i = tid; i < kGemmBK * (D / 2); i += kGemmThreads) {
+      const int kk = i / (D / 2), dp = i % (D / 2);
+      const int k = kb + kk;
+      float2 b = make_float2(0.f, 0.f);
+      if (k < k1) {
+        const uint32_t bits = *reinterpret_cast<const uint32_t*>(bsrc + static_cast<int64_t>(k) * p.n_cols + 2 * dp);
+        b = p.f16 ? half2_to_float2<true>(bits) : half2_to_float2<false>(bits);
+      }
+      bs[kk][2 * dp] = b.x;
+      bs[kk][2 * dp + 1] = b.y;
+    }
+    __syncthreads();
 #pragma unroll 8
-      for (int c = 0; c < kRChunk; ++c) {
-        const float2 b = half2_to_float2<false>(bs[c * D2 + dp]);
-        ax = fmaf(w[c], b.x, ax);
-        ay = fmaf(w[c], b.y, ay);
+    for (int kk = 0; kk < kGemmBK; ++kk) {
+      float a[kTM];
+#pragma unroll
+      for (int i = 0; i < kTM; ++i) a[i] = as[kk][tm * kTM + i];
+      const float4 b = *reinterpret_cast<const float4*>(&bs[kk][tn * kTN]);
+#pragma unroll
+      for (int i = 0; i < kTM; ++i) {
+        acc[i][0] = fmaf(a[i], b.x, acc[i][0]);
+        acc[i][1] = fmaf(a[i], b.y, acc[i][1]);
+        acc[i][2] = fmaf(a[i], b.z, acc[i][2]);
+        acc[i][3] = fmaf(a[i], b.w, acc[i][3]);
       }
     }
-    const int s = s0 + j / nr, rr = j % nr;
-    float2* dst = reinterpret_cast<float2*>(
-        p.vpart + ((static_cast<int64_t>(chunk) * p.n_seq + s) * p.n_rows_pad + (rlo - p.row_begin + rr)) * D);
-    dst[dp] = make_float2(ax, ay);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < kTM; ++i) {
+    const int m = m0 + tm * kTM + i;
+    if (m >= M) continue;
+    const int sq = m / nrh, lr = head_lo - p.row_begin + m % nrh;
+    float4* dst = reinterpret_cast<float4*>(
+        vpart + ((static_cast<int64_t>(blockIdx.z) * p.n_seq + sq) * p.n_rows_pad + lr) * D + tn * kTN);
+    *dst = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
 }
 
@@ -199,38 +209,50 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Finalize
   }
 }
 
-int finalize_chunks(int r_v) { return (r_v + kRChunk - 1) / kRChunk; }
+int64_t finalize_vpart_floats(int r_v, int n_seq, int rows_pad, int head_dim) {
+  return static_cast<int64_t>(n_seq) * rows_pad * (static_cast<int64_t>(r_v) + kMaxKSplit * head_dim);
+}
+
+template <int D>
+static int launch_vbasis(const FinalizeParams& p, const float* w, float* vpart, int m_tiles, int n_kv, int splits,
+                         int k_slice, cudaStream_t stream) {
+  vbasis_kernel<D><<<dim3(m_tiles, n_kv, splits), kGemmThreads, 0, stream>>>(p, w, vpart, k_slice);
+  return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
+}
 
 int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
-  if (p.head_dim % 64 != 0 || p.head_dim > 256 || p.q_per_kv < 1 || p.n_q_heads % p.q_per_kv != 0 ||
-      p.vpart == nullptr || p.item_groups % 2 != 0 || p.n_rows > p.n_rows_pad)
+  if ((p.head_dim != 64 && p.head_dim != 128) || p.q_per_kv < 1 || p.n_q_heads % p.q_per_kv != 0 ||
+      p.vpart == nullptr || p.item_groups % 2 != 0 || p.n_rows > p.n_rows_pad || p.r_v % kWsumComps != 0)
     return kDkvErrConfig;
   if (p.n_seq == 0 || p.n_rows == 0) return kDkvOk;
-  // Rows of one KV head inside this call: at most q_per_kv * q_len and at most n_rows.
-  const int nr_max = min(p.n_rows, p.q_per_kv * p.q_len);
-  const int n_chunks = finalize_chunks(p.r_v);
-  const int n_kv = p.n_q_heads / p.q_per_kv;
-  // Many rows per KV head and few conversations (question-length queries): cut each head's rows into
-  // blocks of 16 so that the grid covers the SMs (a call's rows then span one or two KV heads).
-  int row_block = nr_max;
-  if (p.n_seq < kSeqBlock && nr_max > 16) row_block = 16;
-  const int n_row_blocks = (nr_max + row_block - 1) / row_block;
-  const int basis_bytes = kRChunk * p.head_dim / 2 * 4;
-  const int per_seq = row_block * kRChunk * 4;
-  const int seq_block = min(kSeqBlock, (200 * 1024 - basis_bytes) / per_seq);
-  if (seq_block < 1) return kDkvErrConfig;
-  const int smem = basis_bytes + seq_block * per_seq;
-  if (cudaFuncSetAttribute(vbasis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return kDkvErrCuda;
-  const int seq_blocks = (p.n_seq + seq_block - 1) / seq_block;
-  vbasis_kernel<<<dim3(n_chunks, n_kv, seq_blocks * n_row_blocks), kFinalizeThreads, smem, stream>>>(
-      p, seq_block, row_block, n_row_blocks);
+  float* w = p.vpart;                                                              // [n_seq][rows_pad][r_v]
+  float* vpart = p.vpart + static_cast<int64_t>(p.n_seq) * p.n_rows_pad * p.r_v;  // [splits][n_seq][rows_pad][D]
+  wsum_kernel<<<dim3(p.n_seq, p.r_v / kWsumComps), kWsumThreads, 0, stream>>>(p, w);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
+  // GEMM rows per KV head: every conversation's rows of the head inside this call.
+  const int n_kv = p.n_q_heads / p.q_per_kv;
+  int max_rows = 0;
+  for (int kvh = 0; kvh < n_kv; ++kvh) {
+    const int lo = max(p.row_begin, kvh * p.q_per_kv * p.q_len);
+    const int hi = min(p.row_begin + p.n_rows, (kvh + 1) * p.q_per_kv * p.q_len);
+    max_rows = max(max_rows, hi - lo);
+  }
+  const int m_tiles = (p.n_seq * max_rows + kGemmBM - 1) / kGemmBM;
+  // Component slices: enough CTAs for about two per SM, each slice a multiple of kGemmBK components.
+  int splits = (2 * 148 + m_tiles * n_kv - 1) / (m_tiles * n_kv);
+  splits = max(1, min(kMaxKSplit, min(splits, p.r_v / kGemmBK)));
+  const int k_slice = ((p.r_v + splits - 1) / splits + kGemmBK - 1) / kGemmBK * kGemmBK;
+  splits = (p.r_v + k_slice - 1) / k_slice;
+  const int rc = p.head_dim == 128 ? launch_vbasis<128>(p, w, vpart, m_tiles, n_kv, splits, k_slice, stream)
+                                   : launch_vbasis<64>(p, w, vpart, m_tiles, n_kv, splits, k_slice, stream);
+  if (rc != kDkvOk) return rc;
+  FinalizeParams pc = p;
+  pc.vpart = vpart;
   const int rows_per_head = min(p.n_rows, p.q_per_kv * p.q_len);
   // Question-length queries put many rows on a head: one row per CTA then keeps the SMs busy.
   const int rows_per_cta = rows_per_head >= 32 ? 1 : kCombineRows;
   const dim3 cgrid(p.n_seq * n_kv, (rows_per_head + rows_per_cta - 1) / rows_per_cta);
-  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(p, n_chunks, rows_per_cta);
+  combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(pc, splits, rows_per_cta);
   return cudaGetLastError() == cudaSuccess ? kDkvOk : kDkvErrCuda;
 }
 

@@ -93,13 +93,12 @@ extern "C" int dkv_attend_layer_static(const dkv_attend_args* args, int64_t n_sc
                                                                 static_cast<size_t>(args->rows_pad)),
                                                         static_cast<size_t>(args->v_item_groups)),
                                                 64 * sizeof(float)));
-  // dkv_vpart_floats is a product of its arguments: take its per-(conversation, row, component) factor and
-  // multiply the rest here with saturation.
-  const int64_t vpart_chunks = dkv_vpart_floats(args->v_width, 1, 1, 1);
-  if (vpart_chunks < 0 || args->head_dim < 0) return DKV_ERR_ARGS;
-  const size_t vpart_floats = sat_mul(sat_mul(sat_mul(static_cast<size_t>(vpart_chunks), static_cast<size_t>(args->n_seq)),
-                                              static_cast<size_t>(args->rows_pad)),
-                                      static_cast<size_t>(args->head_dim));
+  // dkv_vpart_floats is n_seq * rows_pad * (a per-(conversation, row) factor of v_width and head_dim): take the
+  // factor and multiply the rest here with saturation.
+  const int64_t vpart_row = dkv_vpart_floats(args->v_width, 1, 1, args->head_dim);
+  if (vpart_row < 0) return DKV_ERR_ARGS;
+  const size_t vpart_floats = sat_mul(sat_mul(static_cast<size_t>(vpart_row), static_cast<size_t>(args->n_seq)),
+                                      static_cast<size_t>(args->rows_pad));
   const size_t vpart_bytes = align256(sat_mul(vpart_floats, sizeof(float)));
   const size_t total =
       sat_add(sat_add(sat_add(sat_add(scores_bytes, stats_bytes), exact_bytes), partial_bytes), vpart_bytes);
