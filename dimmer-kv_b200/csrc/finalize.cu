@@ -33,7 +33,9 @@ constexpr int kCombineRows = 8;      // rows of one KV head per combine CTA (one
 }  // namespace
 
 // W[s][lr][c] = sum over the conversation's items covering component c (item order) of
-// partial[item][lr][c - first component of the item]. Rows lr in [0, n_rows).
+// partial[item][lr][c - first component of the item]. Rows lr in [0, n_rows). A conversation's items are
+// ordered by first group (then tile), so the items covering one block are consecutive: found by a binary
+// search, then summed with independent loads.
 __global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams p, float* w) {
   if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   const int s = blockIdx.x;
@@ -41,16 +43,28 @@ __global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams
   const int c = c0 + (threadIdx.x % kWsumComps);
   const int phase = threadIdx.x / kWsumComps;
   const int item_cols = p.item_groups * 64;
+  const int g_first = (c0 / item_cols) * p.item_groups;  // first group of the items covering this block
   const int it0 = __ldg(p.seq_items + 2 * s), it1 = __ldg(p.seq_items + 2 * s + 1);
+  int lo = it0, hi = it1;  // first item whose first group is >= g_first
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(p.items + 4 * mid + 3) < g_first) lo = mid + 1;
+    else hi = mid;
+  }
+  int end = lo;
+  while (end < it1 && __ldg(p.items + 4 * end + 3) == g_first) ++end;
+  const int cb = g_first * 64;
   for (int lr = phase; lr < p.n_rows; lr += kWsumThreads / kWsumComps) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int u = 0;
-    for (int it = it0; it < it1; ++it) {
-      const int cb = __ldg(p.items + 4 * it + 3) * 64;  // first component of the item
-      if (c0 < cb || c0 >= cb + item_cols) continue;   // the item does not cover this block
-      acc[u & 3] += p.partial[(static_cast<int64_t>(it) * p.n_rows_pad + lr) * item_cols + (c - cb)];
-      ++u;
+    int it = lo;
+    for (; it + 4 <= end; it += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        acc[u] += p.partial[(static_cast<int64_t>(it + u) * p.n_rows_pad + lr) * item_cols + (c - cb)];
     }
+#pragma unroll
+    for (int u = 0; u < 3; ++u)
+      if (it + u < end) acc[u] += p.partial[(static_cast<int64_t>(it + u) * p.n_rows_pad + lr) * item_cols + (c - cb)];
     w[(static_cast<int64_t>(s) * p.n_rows_pad + lr) * p.r_v + c] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
 }

@@ -342,10 +342,12 @@ class CompressedBatch:
         total = sum(sum(c) for c in counts) + 0.5 * present.shape[0] * max(1, len(ranges_g))
         target = max(4.0, total / (self.value_items_per_cta * self.sm_count))
         rows, ranges, spans, costs = [], [], [], []
+        # Items of a conversation in group-range order (then tile order): the items that cover one range are
+        # consecutive, which the value basis's reduction of their partial sums relies on.
         for s, seq_ranges in enumerate(tile_ranges):
             first = len(rows)
-            for t0, t1 in seq_ranges:
-                for ri, (g0, g1) in enumerate(ranges_g):
+            for ri, (g0, g1) in enumerate(ranges_g):
+                for t0, t1 in seq_ranges:
                     cnt = counts[ri]
                     c0, acc, used = t0, 0.0, False
                     for t in range(t0, t1):
