@@ -5,7 +5,7 @@
 //   out   = out_c + p_e @ V_exact
 // The probability-weighted coefficients p_c @ C_v arrive as per-item partial sums from the value stage
 // (value_dense.cu / value_weights.cu). Three kernels:
-//   wsum    : one CTA per (conversation, 64 components, 8 rows): sums the conversation's items that cover the
+//   wsum    : one CTA per (conversation, 64 components, block of rows): sums the conversation's items that cover the
 //             components, in item order (deterministic), into W [conversation][row][component] (fp32).
 //   vbasis  : per KV head a fp32 product W[rows of the head, all conversations] x B_v[layer][:, head] on the
 //             CUDA cores (the reference's product is fp32-accurate; tensor-core inputs would round W),
@@ -24,7 +24,7 @@ namespace dkv {
 namespace {
 constexpr int kWsumComps = 64;       // components per wsum CTA (one group; item ranges hold whole groups)
 constexpr int kWsumThreads = 256;    // 64 components x 4 row phases
-constexpr int kWsumRows = 8;         // rows per wsum CTA (two per thread)
+constexpr int kWsumRows = 8;         // rows per wsum CTA when few conversations leave the grid small
 constexpr int kGemmThreads = 256;
 constexpr int kGemmBM = 32;          // rows per vbasis CTA
 constexpr int kGemmBK = 32;          // components per shared-memory step
@@ -37,7 +37,7 @@ constexpr int kCombineRows = 8;      // rows of one KV head per combine CTA (one
 // partial[item][lr][c - first component of the item]. Rows lr in [0, n_rows). A conversation's items are
 // ordered by first group (then tile), so the items covering one block are consecutive: found by a binary
 // search, then summed with independent loads.
-__global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams p, float* w) {
+__global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams p, float* w, int row_block) {
   if (cta_failed_at_entry(p.status)) return;  // an earlier kernel of the call failed
   const int s = blockIdx.x;
   const int c0 = blockIdx.y * kWsumComps;
@@ -55,8 +55,8 @@ __global__ void __launch_bounds__(kWsumThreads) wsum_kernel(const FinalizeParams
   int end = lo;
   while (end < it1 && __ldg(p.items + 4 * end + 3) == g_first) ++end;
   const int cb = g_first * 64;
-  const int lr_end = min(p.n_rows, static_cast<int>(blockIdx.z + 1) * kWsumRows);
-  for (int lr = blockIdx.z * kWsumRows + phase; lr < lr_end; lr += kWsumThreads / kWsumComps) {
+  const int lr_end = min(p.n_rows, static_cast<int>(blockIdx.z + 1) * row_block);
+  for (int lr = blockIdx.z * row_block + phase; lr < lr_end; lr += kWsumThreads / kWsumComps) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int it = lo;
     for (; it + 4 <= end; it += 4) {
@@ -243,8 +243,11 @@ int run_finalize(const FinalizeParams& p, cudaStream_t stream) {
   if (p.n_seq == 0 || p.n_rows == 0) return kDkvOk;
   float* w = p.vpart;                                                              // [n_seq][rows_pad][r_v]
   float* vpart = p.vpart + static_cast<int64_t>(p.n_seq) * p.n_rows_pad * p.r_v;  // [splits][n_seq][rows_pad][D]
-  wsum_kernel<<<dim3(p.n_seq, p.r_v / kWsumComps, (p.n_rows + kWsumRows - 1) / kWsumRows), kWsumThreads, 0, stream>>>(
-      p, w);
+  // Rows per CTA: all of the call's rows when (conversation, component block) CTAs already fill the GPU a few
+  // times over, else blocks of kWsumRows (question-length calls of one conversation).
+  const int row_block = static_cast<int64_t>(p.n_seq) * (p.r_v / kWsumComps) >= 1024 ? p.n_rows : kWsumRows;
+  wsum_kernel<<<dim3(p.n_seq, p.r_v / kWsumComps, (p.n_rows + row_block - 1) / row_block), kWsumThreads, 0, stream>>>(
+      p, w, row_block);
   if (cudaGetLastError() != cudaSuccess) return kDkvErrCuda;
   // GEMM rows per KV head: every conversation's rows of the head inside this call.
   const int n_kv = p.n_q_heads / p.q_per_kv;
