@@ -815,12 +815,14 @@ def run_question(args, cfg, device) -> dict:
         torch.cuda.synchronize(device)
         # The timed path, not the interpreter's collector: collect now, none inside the timed phases.
         gc.collect()
+        side = torch.cuda.Stream(device)  # the cold-tier copies' stream, created outside the timed phases
         gc.disable()
         ev[0].record(stream)
         imp = question_importance_direct(model, batch, cache, tail, [tokens])[0]
         ev[1].record(stream)
+        t_call = time.perf_counter()
         selected = batch.select_top([count])
-        side = torch.cuda.Stream(device)
+        select_call_s = time.perf_counter() - t_call  # includes the wait for the scoring pass to finish
         ev[2].record(stream)
         t_call = time.perf_counter()
         fetched = batch.refine(selected, [cold], side)
@@ -867,6 +869,7 @@ def run_question(args, cfg, device) -> dict:
             "phases_ms": {k: round(v, 3) for k, v in phases.items()}, "fetched_bytes": fetched,
             "refine_host_ms": {k: round(v * 1e3, 3) for k, v in getattr(batch, "last_refine_seconds", {}).items()},
             "refine_call_host_ms": round(refine_call_s * 1e3, 3),
+            "select_call_host_ms": round(select_call_s * 1e3, 3),
             "topk_matches_lowest_index_rule": exact, "importance_roofline": imp_roof,
             "answer_after_refine": {"question_tokens": cfg["question"], "decode_steps": cfg["decode"],
                                     "seconds": round(answer_s, 3), "decode_tok_s": round(cfg["decode"] / answer_s, 2),
