@@ -49,6 +49,14 @@ constexpr int kKdChunkUnroll = DKV_KD_CHUNK_UNROLL;  // epilogue RoPE chunks unr
 #define DKV_KD_ROPE_REGS 0
 #endif
 constexpr bool kKdRopeRegs = DKV_KD_ROPE_REGS != 0;
+// 1 (8 epilogue warps only): the two warps of a TMEM lane quarter split each head's RoPE pairs instead of the
+// heads (each token's cos / sin words are then loaded by one warp, not two) and add their partial products
+// through shared memory; 0: each warp takes whole heads.
+#ifndef DKV_KD_DIM_SPLIT
+#define DKV_KD_DIM_SPLIT 0
+#endif
+constexpr bool kKdDimSplit = DKV_KD_DIM_SPLIT != 0;
+static_assert(!kKdDimSplit || kKdEpilogueWarps == 8, "the dimension split pairs the two warps of a quarter");
 constexpr int kKdCols = 512;                 // key columns per item (one 512-column TMEM accumulator)
 constexpr int kKdMmaN = 256;                 // N of one pair MMA (two per K step)
 constexpr int kKdHalfCols = 128;             // basis rows of one pair MMA loaded by each CTA
@@ -64,7 +72,9 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     key_scores_dense_kernel(const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap amap,
                             const KeyScoreParams p) {
   constexpr int kHeads = kKdCols / D;        // KV heads per item
-  constexpr int kSetHeads = kHeads / (kKdEpilogueWarps / 4);  // heads per epilogue warp
+  constexpr int kSetHeads = kKdDimSplit ? kHeads : kHeads / (kKdEpilogueWarps / 4);  // heads per epilogue warp
+  constexpr int kParts = kKdDimSplit ? 2 : 1;                    // warps sharing a head (split RoPE pairs)
+  constexpr int kPairSpan = (D / 2) / kParts;                    // RoPE pair dims of one warp's part
   // Heads whose columns one TMEM wait covers (two only with the 8-warp epilogue's larger register budget).
   constexpr int kLoadHeads = (kKdEpilogueWarps == 8 && kSetHeads >= 2 && !kKdRopeRegs) ? 2 : 1;
   constexpr int kRopeWords = kKdRopeRegs ? D / 4 : 1;  // 32-bit words of a token's cos (or sin) row
@@ -76,7 +86,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
   uint8_t* stages = smem;                                                // [kKdStages][A | B half 0 | B half 1]
   float* q_s = reinterpret_cast<float*>(smem + kKdStages * kKdStage);   // [kHeads * G][D]
   float* mean_s = q_s + kHeads * G * D;                                  // [kKdCols]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(mean_s + kKdCols);
+  float* red_s = mean_s + kKdCols;                                       // [kHeads][G][128] (dimension split)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red_s + (kKdDimSplit ? kHeads * G * 128 : 0));
   uint64_t* full = bars;                       // [kKdStages] this CTA's A and B boxes (TMA)
   uint64_t* peer_full = full + kKdStages;      // [kKdStages] even CTA: the odd CTA's forward
   uint64_t* empty = peer_full + kKdStages;     // [kKdStages] pair-MMA commit (both CTAs)
@@ -278,7 +289,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     // of the item's KV heads.
     const int r = (warp & 3) * 32 + lane;  // TMEM lane == tile token row
     const int et = tid - 128;              // 0..511 within the epilogue group
-    const int h0 = ((warp - 4) >> 2) * kSetHeads;
+    const int part = kKdDimSplit ? ((warp - 4) >> 2) : 0;
+    const int h0 = kKdDimSplit ? 0 : ((warp - 4) >> 2) * kSetHeads;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t item_iter = 0, n_sync = 0;
     bool failed = false;
@@ -307,7 +319,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
         give_up();
         break;
       }
-      uint32_t cs[kRopeWords], sn[kRopeWords];  // the token's cos / sin row (kKdRopeRegs)
+      [[maybe_unused]] uint32_t cs[kRopeWords], sn[kRopeWords];  // the token's cos / sin row (kKdRopeRegs)
       if (has_tile) {
         if constexpr (kKdRopeRegs) {
 #pragma unroll
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
 #pragma unroll
             for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
 #pragma unroll kChunkUnroll
-          for (int c = 0; c < D / 2; c += 16) {
+          for (int c = part * kPairSpan; c < (part + 1) * kPairSpan; c += 16) {
             // The token's cos / sin for these 16 dims (8 pairs of 16-bit values), shared by the warp's heads.
             uint32_t cbv[8], sbv[8];
             if constexpr (kKdRopeRegs) {
@@ -435,7 +447,27 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             }
             }
           }
-          if (valid) {
+          if constexpr (kKdDimSplit) {
+            // The second part's partial products go through shared memory to the first part's warp.
+            if (part == 1) {
+#pragma unroll
+              for (int e = 0; e < kSetHeads; ++e)
+#pragma unroll
+                for (int j = 0; j < G; ++j) red_s[(e * G + j) * 128 + r] = acc[e][j];
+            }
+            if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
+              give_up();
+              failed = true;
+              break;
+            }
+            if (part == 0) {
+#pragma unroll
+              for (int e = 0; e < kSetHeads; ++e)
+#pragma unroll
+                for (int j = 0; j < G; ++j) acc[e][j] += red_s[(e * G + j) * 128 + r];
+            }
+          }
+          if (valid && part == 0) {
 #pragma unroll
             for (int e = 0; e < kSetHeads; ++e)
 #pragma unroll
@@ -465,7 +497,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
 template <int D, int G, bool F16>
 static int launch_dense(const CUtensorMap& bmap, const CUtensorMap& amap, const KeyScoreParams& p, int grid,
                         cudaStream_t stream) {
-  const int smem = 1024 + kKdStages * kKdStage + (kKdCols / D) * G * D * 4 + kKdCols * 4 + 32 * 8 + 32;
+  const int smem = 1024 + kKdStages * kKdStage + (kKdCols / D) * G * D * 4 + kKdCols * 4 +
+                   (kKdDimSplit ? (kKdCols / D) * G * 128 * 4 : 0) + 32 * 8 + 32;
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_dense_kernel<D, G, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
