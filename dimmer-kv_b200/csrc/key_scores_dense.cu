@@ -53,7 +53,7 @@ constexpr bool kKdRopeRegs = DKV_KD_ROPE_REGS != 0;
 // heads (each token's cos / sin words are then loaded by one warp, not two) and add their partial products
 // through shared memory; 0: each warp takes whole heads.
 #ifndef DKV_KD_DIM_SPLIT
-#define DKV_KD_DIM_SPLIT 0
+#define DKV_KD_DIM_SPLIT 1
 #endif
 constexpr bool kKdDimSplit = DKV_KD_DIM_SPLIT != 0;
 static_assert(!kKdDimSplit || kKdEpilogueWarps == 8, "the dimension split pairs the two warps of a quarter");
