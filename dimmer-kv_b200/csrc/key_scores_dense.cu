@@ -15,11 +15,13 @@
 // two) x 512 key columns, its groups the sorted union of the two tiles' groups. Per merged group each CTA
 // loads one stage: its tile's 128 x 64 coefficient box (A, 16 KB) and 128 of each pair MMA's 256 basis
 // rows (B, 2 x 16 KB). The even CTA issues M = 256 (128 rows of each CTA) x N = 256 pair MMAs, two per
-// K step, into a 512-column fp32 accumulator per CTA. Roles (640 threads, no register reallocation):
+// K step, into a 512-column fp32 accumulator per CTA. Roles (384 threads, 168 registers each, no register
+// reallocation):
 //   warp 0      producer: A and B boxes of every merged group into a ring of stages (TMA, no multicast)
 //   warp 1      even CTA: pair MMA issuer; odd CTA: forwards its stage completions to the even CTA
-//   warps 4-19  epilogue, four warps per TMEM lane quarter (warp % 4), each one KV head of the item (two
-//               for head_dim 64): TMEM -> + mean -> RoPE -> q.k for the head's query group -> fp32 scores
+//   warps 4-11  epilogue, two warps per TMEM lane quarter (warp % 4), each half of every head's RoPE pairs:
+//               TMEM -> + mean -> RoPE -> q.k for each head's query group (packed fp32x2 arithmetic), the
+//               two halves' products added through shared memory -> fp32 scores
 // Every wait is bounded and abort-aware (dkv_ptx.cuh); the abort flag is cluster-wide; the kernel does
 // no work when the call's status word is already set.
 #include "dkv_ptx.cuh"
@@ -30,33 +32,12 @@ namespace dkv {
 
 namespace {
 
-// Epilogue warps: 8 (two KV heads of the item each, 168 registers per thread, both heads' TMEM columns
-// loaded before one wait) or 16 (one head each, 96 registers).
-#ifndef DKV_KD_EPI_WARPS
-#define DKV_KD_EPI_WARPS 8
-#endif
-constexpr int kKdEpilogueWarps = DKV_KD_EPI_WARPS;
+// Epilogue: 8 warps, two per TMEM lane quarter. The two warps of a quarter split every head's RoPE pairs (so
+// each token's cos / sin words are loaded by one warp, not two), take all of the item's heads, load two heads'
+// TMEM columns before one wait, and add their partial q.k products through shared memory.
+constexpr int kKdEpilogueWarps = 8;
 constexpr int kKdEpilogueThreads = kKdEpilogueWarps * 32;
 constexpr int kKdThreads = 128 + kKdEpilogueThreads;
-static_assert(kKdEpilogueWarps == 8 || kKdEpilogueWarps == 16, "epilogue warps");
-#ifndef DKV_KD_CHUNK_UNROLL
-#define DKV_KD_CHUNK_UNROLL 1
-#endif
-constexpr int kKdChunkUnroll = DKV_KD_CHUNK_UNROLL;  // epilogue RoPE chunks unrolled (1: none)
-// 1: each epilogue thread loads its token's cos / sin rows into registers before it waits for the
-// accumulator (their latency then overlaps the MMAs); 0: from L1, chunk by chunk.
-#ifndef DKV_KD_ROPE_REGS
-#define DKV_KD_ROPE_REGS 0
-#endif
-constexpr bool kKdRopeRegs = DKV_KD_ROPE_REGS != 0;
-// 1 (8 epilogue warps only): the two warps of a TMEM lane quarter split each head's RoPE pairs instead of the
-// heads (each token's cos / sin words are then loaded by one warp, not two) and add their partial products
-// through shared memory; 0: each warp takes whole heads.
-#ifndef DKV_KD_DIM_SPLIT
-#define DKV_KD_DIM_SPLIT 1
-#endif
-constexpr bool kKdDimSplit = DKV_KD_DIM_SPLIT != 0;
-static_assert(!kKdDimSplit || kKdEpilogueWarps == 8, "the dimension split pairs the two warps of a quarter");
 constexpr int kKdCols = 512;                 // key columns per item (one 512-column TMEM accumulator)
 constexpr int kKdMmaN = 256;                 // N of one pair MMA (two per K step)
 constexpr int kKdHalfCols = 128;             // basis rows of one pair MMA loaded by each CTA
@@ -72,13 +53,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     key_scores_dense_kernel(const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap amap,
                             const KeyScoreParams p) {
   constexpr int kHeads = kKdCols / D;        // KV heads per item
-  constexpr int kSetHeads = kKdDimSplit ? kHeads : kHeads / (kKdEpilogueWarps / 4);  // heads per epilogue warp
-  constexpr int kParts = kKdDimSplit ? 2 : 1;                    // warps sharing a head (split RoPE pairs)
-  constexpr int kPairSpan = (D / 2) / kParts;                    // RoPE pair dims of one warp's part
-  // Heads whose columns one TMEM wait covers (two only with the 8-warp epilogue's larger register budget).
-  constexpr int kLoadHeads = (kKdEpilogueWarps == 8 && kSetHeads >= 2 && !kKdRopeRegs) ? 2 : 1;
-  constexpr int kRopeWords = kKdRopeRegs ? D / 4 : 1;  // 32-bit words of a token's cos (or sin) row
-  constexpr int kChunkUnroll = kKdRopeRegs ? (D / 2) / 16 : kKdChunkUnroll;
+  constexpr int kPairSpan = D / 4;           // RoPE pair dims of one warp's part: half of each head's D / 2
+  constexpr int kLoadHeads = 2;              // heads whose TMEM columns one wait covers
   constexpr uint32_t kIdesc = idesc_f16(256, kKdMmaN, /*is_bf16=*/!F16, false, false);
 
   extern __shared__ uint8_t smem_raw[];
@@ -86,8 +62,8 @@ __global__ void __launch_bounds__(kKdThreads, 1)
   uint8_t* stages = smem;                                                // [kKdStages][A | B half 0 | B half 1]
   float* q_s = reinterpret_cast<float*>(smem + kKdStages * kKdStage);   // [kHeads * G][D]
   float* mean_s = q_s + kHeads * G * D;                                  // [kKdCols]
-  float* red_s = mean_s + kKdCols;                                       // [kHeads][G][128] (dimension split)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red_s + (kKdDimSplit ? kHeads * G * 128 : 0));
+  float* red_s = mean_s + kKdCols;                                       // [kHeads][G][128] second parts' q.k
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red_s + kHeads * G * 128);
   uint64_t* full = bars;                       // [kKdStages] this CTA's A and B boxes (TMA)
   uint64_t* peer_full = full + kKdStages;      // [kKdStages] even CTA: the odd CTA's forward
   uint64_t* empty = peer_full + kKdStages;     // [kKdStages] pair-MMA commit (both CTAs)
@@ -284,13 +260,11 @@ __global__ void __launch_bounds__(kKdThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warps
-    // Warp w reads TMEM lane quarter w % 4 (the tile rows 32 (w % 4) ..); warps 4..7, 8..11, 12..15 and
-    // 16..19 (or 4..7 and 8..11 with 8 epilogue warps) each cover the four quarters for their own kSetHeads
-    // of the item's KV heads.
+    // Warp w reads TMEM lane quarter w % 4 (the tile rows 32 (w % 4) ..); warps 4..7 take the first half of
+    // every head's RoPE pairs (dims [0, D / 4) and [D / 2, 3 D / 4)), warps 8..11 the second half.
     const int r = (warp & 3) * 32 + lane;  // TMEM lane == tile token row
     const int et = tid - 128;              // 0..511 within the epilogue group
-    const int part = kKdDimSplit ? ((warp - 4) >> 2) : 0;
-    const int h0 = kKdDimSplit ? 0 : ((warp - 4) >> 2) * kSetHeads;
+    const int part = (warp - 4) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t item_iter = 0, n_sync = 0;
     bool failed = false;
@@ -319,20 +293,9 @@ __global__ void __launch_bounds__(kKdThreads, 1)
         give_up();
         break;
       }
-      [[maybe_unused]] uint32_t cs[kRopeWords], sn[kRopeWords];  // the token's cos / sin row (kKdRopeRegs)
       if (has_tile) {
-        if constexpr (kKdRopeRegs) {
-#pragma unroll
-          for (int w = 0; w < kRopeWords; w += 4) {
-            const uint4 a = __ldg(reinterpret_cast<const uint4*>(cosrow) + w / 4);
-            const uint4 b = __ldg(reinterpret_cast<const uint4*>(sinrow) + w / 4);
-            cs[w] = a.x, cs[w + 1] = a.y, cs[w + 2] = a.z, cs[w + 3] = a.w;
-            sn[w] = b.x, sn[w + 1] = b.y, sn[w + 2] = b.z, sn[w + 3] = b.w;
-          }
-        } else {
-          prefetch_l1(cosrow);
-          prefetch_l1(sinrow);
-        }
+        prefetch_l1(cosrow);
+        prefetch_l1(sinrow);
         const int s = tile.seq;
         const int64_t m_s = p.seq_m[s];
         float* out_base = p.scores + p.seq_score_off[s];
@@ -360,35 +323,27 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             failed = true;
             break;
           }
-          float acc[kSetHeads][G];
+          float acc[kHeads][G];
 #pragma unroll
-          for (int e = 0; e < kSetHeads; ++e)
+          for (int e = 0; e < kHeads; ++e)
 #pragma unroll
             for (int j = 0; j < G; ++j) acc[e][j] = 0.f;
-#pragma unroll kChunkUnroll
+#pragma unroll 1
           for (int c = part * kPairSpan; c < (part + 1) * kPairSpan; c += 16) {
             // The token's cos / sin for these 16 dims (8 pairs of 16-bit values), shared by the warp's heads.
-            uint32_t cbv[8], sbv[8];
-            if constexpr (kKdRopeRegs) {
+            const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
+            const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
+            const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+            const uint32_t cbv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const uint32_t sbv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-              for (int k = 0; k < 8; ++k) cbv[k] = cs[c / 2 + k], sbv[k] = sn[c / 2 + k];
-            } else {
-              const uint4* cp = reinterpret_cast<const uint4*>(cosrow + c);
-              const uint4* sp = reinterpret_cast<const uint4*>(sinrow + c);
-              const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-              cbv[0] = c0.x, cbv[1] = c0.y, cbv[2] = c0.z, cbv[3] = c0.w;
-              cbv[4] = c1.x, cbv[5] = c1.y, cbv[6] = c1.z, cbv[7] = c1.w;
-              sbv[0] = s0.x, sbv[1] = s0.y, sbv[2] = s0.z, sbv[3] = s0.w;
-              sbv[4] = s1.x, sbv[5] = s1.y, sbv[6] = s1.z, sbv[7] = s1.w;
-            }
-#pragma unroll
-            for (int hp = 0; hp < kSetHeads; hp += kLoadHeads) {
+            for (int hp = 0; hp < kHeads; hp += kLoadHeads) {
               uint32_t xs1[kLoadHeads][16], xs2[kLoadHeads][16];
               if (accumulated) {
 #pragma unroll
                 for (int e = 0; e < kLoadHeads; ++e) {
-                  tmem_ld16(tmem + lane_base + (h0 + hp + e) * D + c, xs1[e]);
-                  tmem_ld16(tmem + lane_base + (h0 + hp + e) * D + D / 2 + c, xs2[e]);
+                  tmem_ld16(tmem + lane_base + (hp + e) * D + c, xs1[e]);
+                  tmem_ld16(tmem + lane_base + (hp + e) * D + D / 2 + c, xs2[e]);
                 }
                 tmem_ld_wait();
 #pragma unroll
@@ -404,7 +359,7 @@ __global__ void __launch_bounds__(kKdThreads, 1)
               }
 #pragma unroll
             for (int e = hp; e < hp + kLoadHeads; ++e) {
-              const int hh = h0 + e;
+              const int hh = e;
               uint32_t* x1 = xs1[e - hp];
               uint32_t* x2 = xs2[e - hp];
               // Pairs of dims (c + 2k, c + 2k + 1) in packed fp32x2 arithmetic: + mean, RoPE, q.k.
@@ -447,32 +402,30 @@ __global__ void __launch_bounds__(kKdThreads, 1)
             }
             }
           }
-          if constexpr (kKdDimSplit) {
-            // The second part's partial products go through shared memory to the first part's warp.
-            if (part == 1) {
+          // The second part's partial products go through shared memory to the first part's warp.
+          if (part == 1) {
 #pragma unroll
-              for (int e = 0; e < kSetHeads; ++e)
+            for (int e = 0; e < kHeads; ++e)
 #pragma unroll
-                for (int j = 0; j < G; ++j) red_s[(e * G + j) * 128 + r] = acc[e][j];
-            }
-            if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
-              give_up();
-              failed = true;
-              break;
-            }
-            if (part == 0) {
+              for (int j = 0; j < G; ++j) red_s[(e * G + j) * 128 + r] = acc[e][j];
+          }
+          if (!group_sync(ep_sync, n_sync, p.status, kSiteKeyDense + kErrWaitAccum, abort_flag)) {
+            give_up();
+            failed = true;
+            break;
+          }
+          if (part == 0) {
 #pragma unroll
-              for (int e = 0; e < kSetHeads; ++e)
+            for (int e = 0; e < kHeads; ++e)
 #pragma unroll
-                for (int j = 0; j < G; ++j) acc[e][j] += red_s[(e * G + j) * 128 + r];
-            }
+              for (int j = 0; j < G; ++j) acc[e][j] += red_s[(e * G + j) * 128 + r];
           }
           if (valid && part == 0) {
 #pragma unroll
-            for (int e = 0; e < kSetHeads; ++e)
+            for (int e = 0; e < kHeads; ++e)
 #pragma unroll
               for (int j = 0; j < G; ++j) {
-                const int hq = (kv0 + h0 + e) * G + j;
+                const int hq = (kv0 + e) * G + j;
                 out_base[(static_cast<int64_t>(hq) * p.q_len + qi) * m_s + tile.score_base + r] =
                     hidden ? -INFINITY : acc[e][j] * p.scaling;
               }
@@ -498,7 +451,7 @@ template <int D, int G, bool F16>
 static int launch_dense(const CUtensorMap& bmap, const CUtensorMap& amap, const KeyScoreParams& p, int grid,
                         cudaStream_t stream) {
   const int smem = 1024 + kKdStages * kKdStage + (kKdCols / D) * G * D * 4 + kKdCols * 4 +
-                   (kKdDimSplit ? (kKdCols / D) * G * 128 * 4 : 0) + 32 * 8 + 32;
+                   (kKdCols / D) * G * 128 * 4 + 32 * 8 + 32;
   if (smem > 232448) return kDkvErrConfig;
   cudaError_t e =
       cudaFuncSetAttribute(key_scores_dense_kernel<D, G, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
