@@ -102,3 +102,15 @@ def test_synthetic_ladder_feeds_the_drop_in_codec(tmp_path):
     assert out.used_bytes <= int(0.02 * tokens * 2 * codec.exact_bytes)
     assert codec.last_codes is not None and codec.last_codes["key"].kind == 1
     assert int((codec.last_choice["key"] >= 0).sum()) == end - start
+
+    # The bench's algorithmic work for these codes: every middle token costs the groups its rung codes.
+    import types
+
+    batch = types.SimpleNamespace(n_cols=heads * dim, q_heads=c.num_attention_heads, head_dim=dim, v_width=4 * 64)
+    key, code_bytes, step = bench.ladder_work(codec, types.SimpleNamespace(batch=batch), out, tokens)
+    middle = end - start
+    coded = {k: [int((r > 0).sum()) for r in codec.streams[k].rungs] + [4] for k in ("key", "value")}
+    width = {k: 64 * sum(coded[k][int(x)] for x in codec.last_choice[k]) for k in ("key", "value")}
+    assert key == 2 * width["key"] * heads * dim + 2 * middle * c.num_attention_heads * dim
+    assert step == layers * (key + 2 * c.num_attention_heads * width["value"] + 2 * c.num_attention_heads * 256 * dim)
+    assert code_bytes == (out.used_bytes - (tokens - middle) * 2 * codec.exact_bytes) * layers
