@@ -67,3 +67,16 @@ def test_static_scratch_entry_rejects_oversized_requests_on_the_host():
     assert fn(ctypes.byref(big), 0, None) == 5
     assert fn(ctypes.byref(a), -1, None) == 1
     assert lib.dkv_status_string(5) != b""
+
+
+@pytest.mark.skipif(not _lib.LIB_PATH.exists(), reason="library not built (dimmer-kv_b200/build_lib.py)")
+def test_vpart_size_covers_the_weighted_coefficients_and_the_basis_slices():
+    """dkv_vpart_floats: the value basis's scratch holds W [n_seq][rows_pad][v_width] and up to 16 component
+    slices of partial outputs [n_seq][rows_pad][head_dim]; it is n_seq * rows_pad times a per-row factor
+    (dkv_attend_layer_static multiplies that factor out with saturation), and negative sizes are rejected."""
+    lib = _lib.lib()
+    for v_width, n_seq, rows_pad, head_dim in ((4096, 64, 32, 128), (1024, 1, 128, 64), (192, 3, 16, 128)):
+        got = lib.dkv_vpart_floats(v_width, n_seq, rows_pad, head_dim)
+        assert got == n_seq * rows_pad * (v_width + 16 * head_dim)
+        assert got == n_seq * rows_pad * lib.dkv_vpart_floats(v_width, 1, 1, head_dim)
+    assert lib.dkv_vpart_floats(-1, 1, 1, 64) < 0
